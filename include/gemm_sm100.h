@@ -1,0 +1,231 @@
+/*
+ * gemm_sm100.h -- C ABI of libgemm_sm100.so, the B200 (sm_100a) matmul
+ * backend for php-gpu-tensors.
+ *
+ * The first block is a drop-in for the reference's native matmul boundary:
+ * identical types, names, argument meaning and return conventions as
+ *   src/backends/cuda/matmul_kernels.h:8-57   (launchers, precision, tuning)
+ *   src/backends/cuda/backend_info.h:7-16     (cuda_backend_info, cuda_blas_info)
+ * so src/cuda_array/ca_private.c:1127-1137,1195-1200, src/fusion_execute.c:
+ * 159-173 and src/cuda.c:136-290 link against it unchanged.  The second block
+ * is additive (FP64, fused epilogue, diagnostics, multi-GPU).
+ *
+ * Conventions (all entry points):
+ *   - a, b, c, bias are DEVICE pointers owned by the caller; shape/stride
+ *     arrays are HOST memory read during the call only (matmul_kernels.h:46).
+ *   - strides are in ELEMENTS; a view's offset is folded into its pointer.
+ *   - launchers return 1 on success and 0 on failure; on a CUDA failure
+ *     cuda_blas_info().last_blas_status carries the cudaError_t (or a
+ *     GEMM_SM100_STATUS_* code).  Degenerate extents (M or N or a batch extent
+ *     of 0) return 1 without a launch; K == 0 writes zeros.
+ *   - work is enqueued asynchronously on `stream` (NULL = legacy default
+ *     stream); launchers never allocate, synchronise or read device memory,
+ *     so they can be captured into CUDA graphs after the first call on a
+ *     device (which performs one-time per-device set-up).
+ *   - precision mode, counters and tuning plans are per host thread.
+ *
+ * When building inside the php-gpu-tensors extension, include the
+ * extension's data_types.h, backend_info.h and matmul_kernels.h first; the
+ * shared declarations below are then skipped by their include guards.
+ */
+#ifndef PT_GEMM_SM100_H
+#define PT_GEMM_SM100_H
+
+#include <stddef.h>
+#include <cuda_runtime_api.h>
+
+#ifndef DATA_TYPES_H
+/* Same enumerators and values as the reference's dtype_t (src/data_types.h:8-27). */
+typedef enum {
+    DTYPE_FLOAT32,
+    DTYPE_FLOAT64,
+    DTYPE_INT8,
+    DTYPE_INT16,
+    DTYPE_INT32,
+    DTYPE_INT64,
+    DTYPE_UINT8,
+    DTYPE_UINT16,
+    DTYPE_UINT32,
+    DTYPE_UINT64,
+    DTYPE_BOOL,
+    DTYPE_FLOAT16,
+    DTYPE_BFLOAT16,
+    DTYPE_UNKNOWN,
+    DTYPE_COUNT,
+    DTYPE_LIST,
+    DTYPE_VOID
+} dtype_t;
+#endif
+
+#ifndef MAX_DIMS
+#define MAX_DIMS 10 /* src/tensor.h:16 */
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ------------------------------------------------------------------ */
+/* Drop-in block: src/backends/cuda/backend_info.h:7-16               */
+/* ------------------------------------------------------------------ */
+#ifndef CUDA_BACKEND_INFO_H
+#define CUDA_BACKEND_INFO_H
+typedef struct {
+    int cublas, cublas_lt, cudnn;
+    unsigned long long blas_calls, lt_calls, builtin_matmul_calls;
+    unsigned long long cub_calls, axis_calls, generic_reduce_calls;
+    const char *last_matmul;
+    const char *precision;
+    int last_blas_status;
+} cuda_backend_info;
+#endif
+
+/* Replaces backend_info.h:15.  Fills the matmul fields: cublas = cublas_lt =
+ * 0 (this library contains no cuBLAS), builtin_matmul_calls counts launches,
+ * last_matmul is "builtin" (float32), "builtin-low-precision" (float16 /
+ * bfloat16) or "builtin-f64", precision is the thread's mode, last_blas_status
+ * the last error code.  cudnn and the reduction counters are left untouched. */
+void cuda_blas_info(cuda_backend_info *info);
+
+/* ------------------------------------------------------------------ */
+/* Drop-in block: src/backends/cuda/matmul_kernels.h:8-57             */
+/* ------------------------------------------------------------------ */
+#ifndef MATMUL_KERNELS_H
+#define MATMUL_KERNELS_H
+
+enum {
+    CUDA_MATMUL_PRECISION_FP32_STRICT = 0, /* float32 via 3xTF32 tensor-core split */
+    CUDA_MATMUL_PRECISION_TF32 = 1         /* float32 via one TF32 pass */
+};
+
+#define CUDA_MATMUL_TUNING_MAX_CANDIDATES 8
+
+typedef struct {
+    int algorithm_id;
+    size_t workspace_bytes;
+    double median_ms;
+} cuda_matmul_tuning_candidate;
+
+typedef struct {
+    int candidate_count;
+    int selected_candidate;
+    cuda_matmul_tuning_candidate candidates[CUDA_MATMUL_TUNING_MAX_CANDIDATES];
+} cuda_matmul_tuning_result;
+
+#endif /* MATMUL_KERNELS_H */
+
+/* matmul_kernels.h:31.  Clears this thread's counters and tuning plans. */
+void cuda_blas_shutdown(void);
+
+/* matmul_kernels.h:32.  Returns 1 and sets the thread's float32 mode, or 0
+ * for an unknown mode. */
+int cuda_blas_set_precision(int precision);
+
+/* matmul_kernels.h:33.  "fp32-strict" or "tf32". */
+const char *cuda_blas_precision_name(void);
+
+/* matmul_kernels.h:34-38.  Times this library's tile configurations for a
+ * 2-D float32 product (2 warm-ups, median of 5, CUDA events on `stream`),
+ * pins the fastest for this shape/layout/precision, and leaves the product
+ * in c.  Returns 1 on success, 0 when the product is ineligible (null
+ * pointer, a non-positive extent, rows*inner*cols < 1e7, or a layout the
+ * tensor-core path cannot read), -1 on a CUDA error.  Synchronises `stream`;
+ * not for use during graph capture.  algorithm_id values are listed by
+ * gemm_sm100_algorithm_name(). */
+int cuda_blas_tune_matmul(float *a, float *b, float *c,
+                          int rows, int inner, int cols,
+                          size_t a_stride0, size_t a_stride1,
+                          size_t b_stride0, size_t b_stride1,
+                          cudaStream_t stream, cuda_matmul_tuning_result *result);
+
+/* matmul_kernels.h:40-44.  2-D float32 C = A.B.  NOTE the reference's
+ * argument naming: m = rows of C, n = INNER extent, k = cols of C. */
+int cuda_matmul_launcher(float *a, float *b, float *c,
+                         int m, int n, int k,
+                         size_t a_stride0, size_t a_stride1,
+                         size_t b_stride0, size_t b_stride1,
+                         size_t c_stride0, size_t c_stride1, cudaStream_t stream);
+
+/* matmul_kernels.h:46-51.  Batched float32 C[...,M,N] = A[...,M,K] . B[...,K,N]
+ * with NumPy batch broadcasting (right-aligned batch axes; an operand axis of
+ * extent 1 or a missing axis is broadcast).  Shape and stride pointers refer
+ * to host metadata. */
+int cuda_batched_matmul_nd_launcher(
+    float *a, float *b, float *c,
+    int *shape_a, size_t *stride_a, int nd_a,
+    int *shape_b, size_t *stride_b, int nd_b,
+    int *shape_c, size_t *stride_c, int nd_c, cudaStream_t stream);
+
+/* matmul_kernels.h:53-57.  As above for DTYPE_FLOAT16 / DTYPE_BFLOAT16
+ * operands and result, FP32 accumulation, round-to-nearest-even output. */
+int cuda_low_precision_matmul_nd_launcher(
+    void *a, void *b, void *c, dtype_t dtype,
+    int *shape_a, size_t *stride_a, int nd_a,
+    int *shape_b, size_t *stride_b, int nd_b,
+    int *shape_c, size_t *stride_c, int nd_c, cudaStream_t stream);
+
+/* ------------------------------------------------------------------ */
+/* Additive block (no counterpart in the reference's ABI)             */
+/* ------------------------------------------------------------------ */
+
+/* Error codes reported in last_blas_status besides cudaError_t values. */
+#define GEMM_SM100_STATUS_TENSOR_MAP 9001  /* cuTensorMapEncodeTiled rejected a layout */
+#define GEMM_SM100_STATUS_NO_DRIVER 9002   /* driver entry point unavailable */
+#define GEMM_SM100_STATUS_NO_DEVICE 9003   /* no current CUDA device / not sm_100 */
+#define GEMM_SM100_STATUS_NCCL 9004        /* NCCL failure (multi-GPU entry points) */
+
+/* FP64 C = A.B with the batched launcher's shape/broadcast rules.  New scope:
+ * the reference rejects float64 matmul (src/cuda_array/ca_private.c:1099-1106). */
+int cuda_f64_matmul_nd_launcher(
+    double *a, double *b, double *c,
+    int *shape_a, size_t *stride_a, int nd_a,
+    int *shape_b, size_t *stride_b, int nd_b,
+    int *shape_c, size_t *stride_c, int nd_c, cudaStream_t stream);
+
+/* Activations a fused epilogue can apply (the Fusion plan unary ops). */
+enum {
+    CUDA_MATMUL_EPILOGUE_NONE = 0,
+    CUDA_MATMUL_EPILOGUE_TANH = 1,
+    CUDA_MATMUL_EPILOGUE_RELU = 2,
+    CUDA_MATMUL_EPILOGUE_SIGMOID = 3
+};
+
+/* Fused native-matmul step: c = act(round(A.B) + bias[N]), the values the
+ * unfused Fusion plan (matmul step, then the +bias / unary elementwise
+ * kernel) produces: the product is rounded to the result dtype, the bias add
+ * and activation run in float (double for float64) and round once.  dtype is
+ * FLOAT32, FLOAT64, FLOAT16 or BFLOAT16; bias is a contiguous [N] vector of
+ * that dtype or NULL; activation is a CUDA_MATMUL_EPILOGUE_* value. */
+int cuda_matmul_epilogue_nd_launcher(
+    void *a, void *b, void *c, dtype_t dtype,
+    int *shape_a, size_t *stride_a, int nd_a,
+    int *shape_b, size_t *stride_b, int nd_b,
+    int *shape_c, size_t *stride_c, int nd_c,
+    const void *bias, int activation, cudaStream_t stream);
+
+/* Name of the kernel the last successful launch on this thread used, e.g.
+ * "tc-bf16-128x256", "tc-3xtf32-128x128", "simt-f32"; "none" before any. */
+const char *gemm_sm100_last_kernel(void);
+
+/* Selects the kernel family for this thread's later launches and returns the
+ * previous setting: 0 = automatic, 1 = tensor-core kernel whenever the layout
+ * allows it (ignoring the size heuristic), 2 = CUDA-core kernel only. */
+int gemm_sm100_set_path(int path);
+
+/* Reads (and with clear != 0 resets) the device status word of `device`:
+ * 0 = no kernel has reported a problem; 1..4 = a tensor-core kernel gave up a
+ * bounded wait (producer, MMA, epilogue, split stage) and returned early.
+ * Synchronises the device.  Returns -1 if the device cannot be queried. */
+int gemm_sm100_device_status(int device, int clear);
+
+/* Human-readable name of a tuning algorithm_id. */
+const char *gemm_sm100_algorithm_name(int algorithm_id);
+
+/* Library version, major * 10000 + minor * 100 + patch. */
+int gemm_sm100_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* PT_GEMM_SM100_H */

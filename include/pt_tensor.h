@@ -1,0 +1,90 @@
+/*
+ * pt_tensor.h -- tensor-level matmul entry points of libgemm_sm100.so.
+ *
+ * The host layer above the launcher ABI (gemm_sm100.h), written in C++ in
+ * place of the PHP extension's C dispatch, with the same argument meaning
+ * and error behaviour as
+ *   cuda_tensor_matmul / cuda_tensor_matmul_nd
+ *       src/cuda_array/ca_private.c:1097-1213
+ *   ZEND_METHOD(CudaArray, matmul)   src/cuda_array/cuda_array_ce.c:1568-1607
+ *   fusion_native_submit (matmul)    src/fusion_execute.c:157-182
+ *   AUTOGRAD_MATMUL backward GEMMs   src/autograd.c:1539-1585
+ * A pt_tensor is the matmul-relevant part of the reference's tensor_t
+ * (src/tensor.h:49-79): device data pointer with the view offset folded in,
+ * dtype, rank, shape and ELEMENT strides.
+ */
+#ifndef PT_TENSOR_H
+#define PT_TENSOR_H
+
+#include "gemm_sm100.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct {
+    void *data;
+    dtype_t dtype;
+    int ndims;
+    int shape[MAX_DIMS];
+    size_t strides[MAX_DIMS];
+} pt_tensor;
+
+/* Status codes: PT_OK, or the PHP exception class the reference throws. */
+enum {
+    PT_OK = 0,
+    PT_INVALID_ARGUMENT = 1, /* PhpTensors\InvalidArgumentException */
+    PT_RUNTIME = 2           /* PhpTensors\RuntimeException */
+};
+
+/* Flags for pt_tensor_matmul_into. */
+enum {
+    PT_MATMUL_ALLOW_FLOAT64 = 1 /* accept float64 operands (the reference rejects them) */
+};
+
+/* Message of the last non-OK status on this thread (the reference's
+ * exception text), "" when none. */
+const char *pt_last_error(void);
+
+/* Result shape of a matmul (src/operations.c:32-35 -> src/tensor_shape.h:46-59):
+ * returns PT_OK, or PT_INVALID_ARGUMENT with "Matrix multiplication failed -
+ * incompatible dimensions". */
+int pt_matmul_result_shape(const pt_tensor *a, const pt_tensor *b, int *shape, int *ndims);
+
+/* C = A . B into a preallocated, contiguous row-major result of the shape
+ * pt_matmul_result_shape reports (the Fusion plan contract).  Checks, in the
+ * reference's order: matching float32/float16/bfloat16 dtypes ("matmul
+ * requires matching float32, float16 or bfloat16 operands"), the shape rule,
+ * then dispatches -- 2-D float32 to cuda_matmul_launcher, other float32 to
+ * cuda_batched_matmul_nd_launcher, float16/bfloat16 to
+ * cuda_low_precision_matmul_nd_launcher, float64 (with
+ * PT_MATMUL_ALLOW_FLOAT64) to cuda_f64_matmul_nd_launcher -- and reports a
+ * launcher failure as PT_RUNTIME "Matmul backend submission failed (cuBLAS
+ * status %d)".  Asynchronous on `stream`. */
+int pt_tensor_matmul_into(const pt_tensor *a, const pt_tensor *b, const pt_tensor *result,
+                          int flags, cudaStream_t stream);
+
+/* As pt_tensor_matmul_into, but allocates the contiguous result with
+ * cudaMallocAsync on `stream` (the eager CudaArray::matmul path).  Release
+ * it with pt_tensor_release. */
+int pt_tensor_matmul(const pt_tensor *a, const pt_tensor *b, pt_tensor *result, int flags,
+                     cudaStream_t stream);
+
+/* Frees a tensor allocated by pt_tensor_matmul (cudaFreeAsync on stream). */
+void pt_tensor_release(pt_tensor *t, cudaStream_t stream);
+
+/* The two GEMMs of the matmul backward node (src/autograd.c:1552-1577) for
+ * float32 operands: grad_a = grad_c . B^T and grad_b = A^T . grad_c, with B^T
+ * and A^T taken as zero-copy transposed views (last two axes swapped), into
+ * preallocated contiguous results of the shapes those products have (the
+ * batch-broadcast shape; the un-broadcast reduction is the caller's, as in
+ * src/autograd.c:714-760).  Either result may be NULL to skip that GEMM. */
+int pt_tensor_matmul_backward(const pt_tensor *a, const pt_tensor *b, const pt_tensor *grad_c,
+                              const pt_tensor *grad_a, const pt_tensor *grad_b,
+                              cudaStream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* PT_TENSOR_H */

@@ -1,0 +1,897 @@
+// libgemm_sm100.so: the C ABI of include/gemm_sm100.h.
+//
+// Host-side dispatch that replaces src/backends/cuda/matmul_kernels.cu of
+// lcmialichi/php-gpu-tensors.  For every call it
+//   1. validates shapes and strides exactly as the reference launchers do
+//      (matmul_kernels.cu:680-710, 856-875, 912-914), with NumPy batch
+//      broadcasting (right-aligned axes, as src/tensor_shape.h:46-59 and the
+//      host loop src/contiguous_array_ce.c:1280-1293 define it);
+//   2. drops extent-1 batch axes and merges adjacent batch axes whose strides
+//      compose, for all three operands at once;
+//   3. when the layout can be described with TMA (unit stride in one of each
+//      operand's matrix axes, 16-byte aligned pointer and strides, <= 3
+//      merged batch axes, N-contiguous result) launches the persistent tcgen05
+//      kernel (gemm_tc.cuh), otherwise the CUDA-core kernel (gemm_simt.cuh).
+// Launches are asynchronous on the caller's stream and allocate nothing.
+#include "gemm_sm100.h"
+
+#include "gemm_simt.cuh"
+#include "gemm_tc.cuh"
+
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdint>
+#include <cstring>
+#include <mutex>
+#include <vector>
+
+#define PT_API extern "C" __attribute__((visibility("default")))
+
+using namespace ptg;
+
+namespace {
+
+// Device status word (one copy per device): first timeout code reported by a
+// tensor-core kernel, 0 otherwise.
+__device__ int g_device_status;
+
+enum DType : int { DT_F32 = 0, DT_F16 = 1, DT_BF16 = 2, DT_F64 = 3 };
+
+constexpr int kMaxBatchDims = kSimtMaxBatchDims;
+constexpr double kTcMinWork = 4194304.0;   // M*N*K*batches below this: CUDA-core kernel
+constexpr double kTuneMinWork = 10000000.0; // matmul_kernels.cu:24 (MATMUL_LT_MIN_WORK)
+
+struct Problem {
+    int dt;
+    const void *a, *b;
+    void *c;
+    int M, N, K;
+    long long batches;
+    int nbd;                       // C batch axes with extent > 1
+    int bshape[kMaxBatchDims];
+    long long a_bs[kMaxBatchDims]; // element strides, 0 = broadcast
+    long long b_bs[kMaxBatchDims];
+    long long c_bs[kMaxBatchDims];
+    long long a_sm, a_sk, b_sk, b_sn, c_sm, c_sn;
+    const void *bias;
+    int act;
+    int forced_bn;                 // 0 = heuristic / tuned plan
+};
+
+// ------------------------------------------------------------ thread state
+thread_local cuda_backend_info t_info = {};
+thread_local int t_precision = CUDA_MATMUL_PRECISION_FP32_STRICT;
+thread_local int t_path = 0;
+thread_local const char *t_last_kernel = "none";
+
+struct TunedPlan {
+    int rows, inner, cols;
+    size_t a_s0, a_s1, b_s0, b_s1;
+    int precision;
+    int algorithm;
+};
+constexpr size_t kMaxTunedPlans = 64;   // matmul_kernels.cu plan cache bound
+thread_local std::vector<TunedPlan> t_plans;
+
+// ------------------------------------------------------------ device state
+constexpr int kMaxDevices = 64;
+struct DeviceState {
+    bool ready;
+    int sms;
+    int cc_major, cc_minor;
+    int *status;                   // this device's copy of g_device_status
+    unsigned long long attr_mask;  // kernels whose shared-memory limit has been raised
+};
+std::mutex g_mutex;
+DeviceState g_devices[kMaxDevices];
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+bool g_encode_looked_up = false;
+
+void set_status(int code) { t_info.last_blas_status = code; }
+
+DeviceState *device_state()
+{
+    int dev = -1;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices)
+        return nullptr;
+    std::lock_guard<std::mutex> lock(g_mutex);
+    DeviceState &d = g_devices[dev];
+    if (!d.ready) {
+        if (cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
+            cudaDeviceGetAttribute(&d.cc_major, cudaDevAttrComputeCapabilityMajor, dev) !=
+                cudaSuccess ||
+            cudaDeviceGetAttribute(&d.cc_minor, cudaDevAttrComputeCapabilityMinor, dev) !=
+                cudaSuccess)
+            return nullptr;
+        void *status = nullptr;
+        if (cudaGetSymbolAddress(&status, g_device_status) != cudaSuccess)
+            return nullptr;
+        d.status = static_cast<int *>(status);
+        d.attr_mask = 0;
+        d.ready = true;
+    }
+    if (!g_encode_looked_up) {
+        g_encode_looked_up = true;
+        void *fn = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) ==
+                cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+    }
+    return &d;
+}
+
+// Raises the dynamic shared-memory limit of a kernel once per device.
+template <typename K>
+bool ensure_smem_attr(DeviceState *ds, int kernel_id, K kernel, int bytes)
+{
+    std::lock_guard<std::mutex> lock(g_mutex);
+    if (ds->attr_mask & (1ull << kernel_id))
+        return true;
+    if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) !=
+        cudaSuccess)
+        return false;
+    ds->attr_mask |= 1ull << kernel_id;
+    return true;
+}
+
+// ------------------------------------------------------------ validation
+// Returns 1 when there is work to launch, 2 when the call is a successful
+// no-op (an M, N or batch extent of 0), 0 when the arguments are invalid.
+int build_problem(int dt, const void *a, const void *b, void *c, const int *sa, const size_t *ta,
+                  int na, const int *sb, const size_t *tb, int nb, const int *sc,
+                  const size_t *tc, int nc, Problem *P)
+{
+    if (na < 2 || nb < 2 || nc < 2 || na > MAX_DIMS || nb > MAX_DIMS || nc > MAX_DIMS)
+        return 0;
+    if (!sa || !sb || !sc || !ta || !tb || !tc)
+        return 0;
+    const int rows = sa[na - 2], inner = sa[na - 1], cols = sb[nb - 1];
+    if (inner != sb[nb - 2] || rows < 0 || inner < 0 || cols < 0 || sc[nc - 2] != rows ||
+        sc[nc - 1] != cols)
+        return 0;
+    const int nbc = nc - 2, nba = na - 2, nbb = nb - 2;
+    if (nba > nbc || nbb > nbc)
+        return 0;
+    std::memset(P, 0, sizeof(*P));
+    P->dt = dt;
+    P->a = a;
+    P->b = b;
+    P->c = c;
+    P->M = rows;
+    P->N = cols;
+    P->K = inner;
+    bool empty = rows == 0 || cols == 0;
+    long long batches = 1;
+    for (int d = 0; d < nbc; d++) {
+        const int ext = sc[d];
+        if (ext < 0)
+            return 0;
+        const int ia = d - (nbc - nba), ib = d - (nbc - nbb);
+        const int ea = ia >= 0 ? sa[ia] : 1, eb = ib >= 0 ? sb[ib] : 1;
+        if ((ea != 1 && ea != ext) || (eb != 1 && eb != ext) || ea < 0 || eb < 0)
+            return 0;
+        if (ext == 0) {
+            empty = true;
+            continue;
+        }
+        if (ext == 1)
+            continue;
+        if (batches > (1ll << 40) / ext)
+            return 0;
+        batches *= ext;
+        const int k = P->nbd++;
+        P->bshape[k] = ext;
+        P->a_bs[k] = ea != 1 ? static_cast<long long>(ta[ia]) : 0;
+        P->b_bs[k] = eb != 1 ? static_cast<long long>(tb[ib]) : 0;
+        P->c_bs[k] = static_cast<long long>(tc[d]);
+    }
+    P->batches = batches;
+    P->a_sm = static_cast<long long>(ta[na - 2]);
+    P->a_sk = static_cast<long long>(ta[na - 1]);
+    P->b_sk = static_cast<long long>(tb[nb - 2]);
+    P->b_sn = static_cast<long long>(tb[nb - 1]);
+    P->c_sm = static_cast<long long>(tc[nc - 2]);
+    P->c_sn = static_cast<long long>(tc[nc - 1]);
+    if (empty)
+        return 2;
+    if (!c || (inner > 0 && (!a || !b)))
+        return 0;
+    return 1;
+}
+
+// ------------------------------------------------------------ tensor maps
+int element_bytes(int dt) { return dt == DT_F64 ? 8 : (dt == DT_F32 ? 4 : 2); }
+
+CUtensorMapDataType tma_type(int dt)
+{
+    switch (dt) {
+    case DT_F16: return CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+    case DT_BF16: return CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+    default: return CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+    }
+}
+
+struct MapDims {
+    int rank = 0;            // used dims
+    uint64_t ext[5];
+    long long stride[5];     // element strides; stride[0] must be 1
+};
+
+// Encodes a rank-5, 128-byte-swizzled tiled tensor map.  Dims beyond `rank`
+// and dims of extent 1 get a harmless 16-byte-multiple stride.  Returns false
+// when TMA cannot describe the view.
+bool encode_map(CUtensorMap *map, int dt, const void *base, const MapDims &m,
+                const uint32_t (&box)[5])
+{
+    if (!g_encode)
+        return false;
+    const int es = element_bytes(dt);
+    if (reinterpret_cast<uintptr_t>(base) % 16 != 0)
+        return false;
+    cuuint64_t dims[5];
+    cuuint64_t strides[4];
+    cuuint32_t boxd[5], estr[5] = {1, 1, 1, 1, 1};
+    const uint64_t filler = ((m.ext[0] * es + 15) / 16) * 16;
+    for (int i = 0; i < 5; i++) {
+        dims[i] = i < m.rank ? m.ext[i] : 1;
+        boxd[i] = box[i];
+        if (dims[i] == 0 || dims[i] > (1ull << 32))
+            return false;
+    }
+    for (int i = 1; i < 5; i++) {
+        uint64_t s = filler;
+        if (i < m.rank && dims[i] > 1) {
+            if (m.stride[i] <= 0)
+                return false;
+            s = static_cast<uint64_t>(m.stride[i]) * es;
+            if (s % 16 != 0 || s >= (1ull << 40))
+                return false;
+        }
+        strides[i - 1] = s;
+    }
+    const CUresult r = g_encode(map, tma_type(dt), 5, const_cast<void *>(base), dims, strides, boxd,
+                                estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
+}
+
+// Merged batch axes of a tensor-core launch.
+struct TcBatch {
+    int nbd;
+    int bshape[3];
+    long long a[3], b[3], c[3];
+};
+
+bool merge_batches(const Problem &P, TcBatch *out)
+{
+    int n = P.nbd;
+    long long ext[kMaxBatchDims], sa[kMaxBatchDims], sb[kMaxBatchDims], sc[kMaxBatchDims];
+    for (int d = 0; d < n; d++) {
+        ext[d] = P.bshape[d];
+        sa[d] = P.a_bs[d];
+        sb[d] = P.b_bs[d];
+        sc[d] = P.c_bs[d];
+        if (sc[d] == 0)
+            return false;   // distinct batches must not alias in the result
+    }
+    auto composable = [](long long outer, long long inner, long long inner_ext) {
+        return (outer == 0 && inner == 0) || (outer != 0 && inner != 0 && outer == inner * inner_ext);
+    };
+    for (int d = n - 1; d > 0; d--) {
+        if (composable(sa[d - 1], sa[d], ext[d]) && composable(sb[d - 1], sb[d], ext[d]) &&
+            composable(sc[d - 1], sc[d], ext[d]) && ext[d - 1] * ext[d] < (1ll << 31)) {
+            ext[d - 1] *= ext[d];
+            sa[d - 1] = sa[d];
+            sb[d - 1] = sb[d];
+            sc[d - 1] = sc[d];
+            for (int e = d; e < n - 1; e++) {
+                ext[e] = ext[e + 1];
+                sa[e] = sa[e + 1];
+                sb[e] = sb[e + 1];
+                sc[e] = sc[e + 1];
+            }
+            n--;
+        }
+    }
+    if (n > 3)
+        return false;
+    out->nbd = n;
+    for (int d = 0; d < 3; d++) {
+        out->bshape[d] = d < n ? static_cast<int>(ext[d]) : 1;
+        out->a[d] = d < n ? sa[d] : 0;
+        out->b[d] = d < n ? sb[d] : 0;
+        out->c[d] = d < n ? sc[d] : 0;
+    }
+    return true;
+}
+
+// Appends an operand's present batch axes to its map and records their slots.
+void add_batch_dims(MapDims &m, const TcBatch &tb, const long long (&bs)[3], int (&slot)[3])
+{
+    for (int d = 0; d < 3; d++) {
+        slot[d] = -1;
+        if (d < tb.nbd && bs[d] != 0) {
+            slot[d] = m.rank;
+            m.ext[m.rank] = static_cast<uint64_t>(tb.bshape[d]);
+            m.stride[m.rank] = bs[d];
+            m.rank++;
+        }
+    }
+}
+
+uint32_t make_idesc(int fmt, int a_mn, int b_mn, int bn)
+{
+    return (1u << 4)                                       // D: f32
+           | (static_cast<uint32_t>(fmt) << 7)             // A format
+           | (static_cast<uint32_t>(fmt) << 10)            // B format
+           | (static_cast<uint32_t>(a_mn) << 15)           // A MN-major
+           | (static_cast<uint32_t>(b_mn) << 16)           // B MN-major
+           | (static_cast<uint32_t>(bn >> 3) << 17)        // N / 8
+           | (static_cast<uint32_t>(128 >> 4) << 24);      // M / 16
+}
+
+enum KernelId : int {
+    KID_BF16_128 = 0,
+    KID_BF16_256,
+    KID_F16_128,
+    KID_F16_256,
+    KID_TF32_128,
+    KID_TF32_256,
+    KID_F32X3_128,
+};
+
+const char *kernel_name(int kid)
+{
+    switch (kid) {
+    case KID_BF16_128: return "tc-bf16-128x128";
+    case KID_BF16_256: return "tc-bf16-128x256";
+    case KID_F16_128: return "tc-f16-128x128";
+    case KID_F16_256: return "tc-f16-128x256";
+    case KID_TF32_128: return "tc-tf32-128x128";
+    case KID_TF32_256: return "tc-tf32-128x256";
+    case KID_F32X3_128: return "tc-3xtf32-128x128";
+    default: return "tc-unknown";
+    }
+}
+
+// Tuning algorithm ids (cuda_blas_tune_matmul) -> kernel ids.
+int algorithm_kernel(int algo)
+{
+    switch (algo) {
+    case 1: return KID_F32X3_128;
+    case 2: return KID_TF32_128;
+    case 3: return KID_TF32_256;
+    default: return -1;
+    }
+}
+
+template <int IN, int BN, int OUT>
+cudaError_t launch_tc_kernel(DeviceState *ds, int kid, const CUtensorMap &ma,
+                             const CUtensorMap &mb, const CUtensorMap &mc, TcParams &p,
+                             cudaStream_t stream)
+{
+    using Cfg = TcConfig<IN, BN, OUT>;
+    auto kernel = tc_gemm_kernel<IN, BN, OUT>;
+    if (!ensure_smem_attr(ds, kid, kernel, Cfg::kSmemBytes))
+        return cudaErrorInvalidConfiguration;
+    p.status = ds->status;
+    const long long grid = std::min<long long>(p.tiles, ds->sms);
+    kernel<<<static_cast<unsigned>(grid), Cfg::kThreads, Cfg::kSmemBytes, stream>>>(ma, mb, mc, p);
+    return cudaGetLastError();
+}
+
+const TunedPlan *find_plan(const Problem &P)
+{
+    if (P.nbd != 0 || P.dt != DT_F32)
+        return nullptr;
+    for (const TunedPlan &t : t_plans)
+        if (t.rows == P.M && t.inner == P.K && t.cols == P.N &&
+            t.a_s0 == static_cast<size_t>(P.a_sm) && t.a_s1 == static_cast<size_t>(P.a_sk) &&
+            t.b_s0 == static_cast<size_t>(P.b_sk) && t.b_s1 == static_cast<size_t>(P.b_sn) &&
+            t.precision == t_precision)
+            return &t;
+    return nullptr;
+}
+
+// Tries the tensor-core kernel.  Returns 1 launched, 0 ineligible, -1 error.
+int try_tc(const Problem &P, DeviceState *ds, cudaStream_t stream, int *kid_out)
+{
+    if (P.dt == DT_F64 || ds->cc_major != 10 || !g_encode)
+        return 0;
+    const int es = element_bytes(P.dt);
+    TcBatch tb;
+    if (!merge_batches(P, &tb))
+        return 0;
+
+    // A: K-major when K is contiguous, M-major for a transposed view.
+    int a_mn;
+    if (P.a_sk == 1 || P.K == 1)
+        a_mn = 0;
+    else if (P.a_sm == 1 || P.M == 1)
+        a_mn = 1;
+    else
+        return 0;
+    // B: N-major for a row-major B, K-major for a transposed view.
+    int b_mn;
+    if (P.b_sn == 1 || P.N == 1)
+        b_mn = 1;
+    else if (P.b_sk == 1 || P.K == 1)
+        b_mn = 0;
+    else
+        return 0;
+    if (!(P.c_sn == 1 || P.N == 1))
+        return 0;
+
+    // kernel selection
+    int kid;
+    const bool fp32 = P.dt == DT_F32;
+    const long long m_blocks = (P.M + 127) / 128;
+    int bn = P.forced_bn;
+    if (fp32 && t_precision == CUDA_MATMUL_PRECISION_FP32_STRICT) {
+        bn = 128;
+    } else if (bn == 0) {
+        const TunedPlan *plan = fp32 ? find_plan(P) : nullptr;
+        if (plan) {
+            bn = plan->algorithm == 3 ? 256 : 128;
+        } else {
+            const long long tiles256 = P.batches * m_blocks * ((P.N + 255) / 256);
+            bn = (P.N <= 128 || tiles256 < ds->sms / 2) ? 128 : 256;
+        }
+    }
+    if (fp32)
+        kid = t_precision == CUDA_MATMUL_PRECISION_FP32_STRICT ? KID_F32X3_128
+                                                                : (bn == 256 ? KID_TF32_256 : KID_TF32_128);
+    else if (P.dt == DT_BF16)
+        kid = bn == 256 ? KID_BF16_256 : KID_BF16_128;
+    else
+        kid = bn == 256 ? KID_F16_256 : KID_F16_128;
+
+    const int bk = 128 / es;            // K elements per stage
+    const int chunk = 128 / es;         // MN elements per 128-byte row
+    const int out_es = fp32 ? 4 : 2;
+    const int epi_cols = 128 / out_es;
+
+    TcParams p;
+    std::memset(&p, 0, sizeof(p));
+    MapDims ma, mb, mc;
+    uint32_t box_a[5] = {1, 1, 1, 1, 1}, box_b[5] = {1, 1, 1, 1, 1}, box_c[5] = {1, 1, 1, 1, 1};
+    if (!a_mn) {
+        ma.ext[0] = P.K; ma.stride[0] = 1;
+        ma.ext[1] = P.M; ma.stride[1] = P.a_sm;
+        box_a[0] = bk; box_a[1] = 128;
+    } else {
+        ma.ext[0] = P.M; ma.stride[0] = 1;
+        ma.ext[1] = P.K; ma.stride[1] = P.a_sk;
+        box_a[0] = chunk; box_a[1] = bk;
+    }
+    ma.rank = 2;
+    if (b_mn) {
+        mb.ext[0] = P.N; mb.stride[0] = 1;
+        mb.ext[1] = P.K; mb.stride[1] = P.b_sk;
+        box_b[0] = chunk; box_b[1] = bk;
+    } else {
+        mb.ext[0] = P.K; mb.stride[0] = 1;
+        mb.ext[1] = P.N; mb.stride[1] = P.b_sn;
+        box_b[0] = bk; box_b[1] = bn;
+    }
+    mb.rank = 2;
+    mc.ext[0] = P.N; mc.stride[0] = 1;
+    mc.ext[1] = P.M; mc.stride[1] = P.c_sm;
+    mc.rank = 2;
+    box_c[0] = epi_cols; box_c[1] = 32;
+    int c_slot[3];
+    add_batch_dims(ma, tb, tb.a, p.a_slot);
+    add_batch_dims(mb, tb, tb.b, p.b_slot);
+    add_batch_dims(mc, tb, tb.c, c_slot);
+
+    CUtensorMap tma_a, tma_b, tma_c;
+    if (!encode_map(&tma_a, P.dt, P.a, ma, box_a) || !encode_map(&tma_b, P.dt, P.b, mb, box_b) ||
+        !encode_map(&tma_c, P.dt, P.c, mc, box_c))
+        return 0;
+
+    p.M = P.M;
+    p.N = P.N;
+    p.K = P.K;
+    p.m_blocks = static_cast<int>(m_blocks);
+    p.n_blocks = (P.N + bn - 1) / bn;
+    p.k_blocks = (P.K + bk - 1) / bk;
+    p.tiles = P.batches * p.m_blocks * p.n_blocks;
+    p.nbd = tb.nbd;
+    for (int d = 0; d < 3; d++)
+        p.bshape[d] = tb.bshape[d];
+    p.a_mn_major = a_mn;
+    p.b_mn_major = b_mn;
+    const int fmt = fp32 ? 2 : (P.dt == DT_BF16 ? 1 : 0);
+    p.idesc = make_idesc(fmt, a_mn, b_mn, bn);
+    p.bias = P.bias;
+    p.act = P.act;
+
+    cudaError_t err;
+    switch (kid) {
+    case KID_BF16_128: err = launch_tc_kernel<IN_BF16, 128, OUT_BF16>(ds, kid, tma_a, tma_b, tma_c, p, stream); break;
+    case KID_BF16_256: err = launch_tc_kernel<IN_BF16, 256, OUT_BF16>(ds, kid, tma_a, tma_b, tma_c, p, stream); break;
+    case KID_F16_128: err = launch_tc_kernel<IN_F16, 128, OUT_F16>(ds, kid, tma_a, tma_b, tma_c, p, stream); break;
+    case KID_F16_256: err = launch_tc_kernel<IN_F16, 256, OUT_F16>(ds, kid, tma_a, tma_b, tma_c, p, stream); break;
+    case KID_TF32_128: err = launch_tc_kernel<IN_TF32, 128, OUT_F32>(ds, kid, tma_a, tma_b, tma_c, p, stream); break;
+    case KID_TF32_256: err = launch_tc_kernel<IN_TF32, 256, OUT_F32>(ds, kid, tma_a, tma_b, tma_c, p, stream); break;
+    default: err = launch_tc_kernel<IN_F32X3, 128, OUT_F32>(ds, kid, tma_a, tma_b, tma_c, p, stream); break;
+    }
+    if (err != cudaSuccess) {
+        set_status(static_cast<int>(err));
+        return -1;
+    }
+    *kid_out = kid;
+    return 1;
+}
+
+template <typename T>
+cudaError_t launch_simt(const Problem &P, cudaStream_t stream)
+{
+    SimtParams s;
+    std::memset(&s, 0, sizeof(s));
+    s.a = P.a;
+    s.b = P.b;
+    s.c = P.c;
+    s.M = P.M;
+    s.N = P.N;
+    s.K = P.K;
+    s.batches = P.batches;
+    s.nbd = P.nbd;
+    for (int d = 0; d < P.nbd; d++) {
+        s.bshape[d] = P.bshape[d];
+        s.a_bs[d] = P.a_bs[d];
+        s.b_bs[d] = P.b_bs[d];
+        s.c_bs[d] = P.c_bs[d];
+    }
+    s.a_sm = P.a_sm;
+    s.a_sk = P.a_sk;
+    s.b_sk = P.b_sk;
+    s.b_sn = P.b_sn;
+    s.c_sm = P.c_sm;
+    s.c_sn = P.c_sn;
+    s.bias = P.bias;
+    s.act = P.act;
+    const long long mb = (P.M + kSimtTile - 1) / kSimtTile;
+    const long long nb = (P.N + kSimtTile - 1) / kSimtTile;
+    dim3 grid(static_cast<unsigned>(std::min<long long>(nb, 2147483647ll)),
+              static_cast<unsigned>(std::min<long long>(mb, 65535)),
+              static_cast<unsigned>(std::min<long long>(P.batches, 65535)));
+    simt_gemm_kernel<T><<<grid, 256, 0, stream>>>(s);
+    return cudaGetLastError();
+}
+
+const char *family_name(int dt)
+{
+    switch (dt) {
+    case DT_F32: return "builtin";
+    case DT_F64: return "builtin-f64";
+    default: return "builtin-low-precision";
+    }
+}
+
+const char *simt_name(int dt)
+{
+    switch (dt) {
+    case DT_F32: return "simt-f32";
+    case DT_F64: return "simt-f64";
+    case DT_F16: return "simt-f16";
+    default: return "simt-bf16";
+    }
+}
+
+int run(Problem &P, cudaStream_t stream)
+{
+    DeviceState *ds = device_state();
+    if (!ds) {
+        set_status(GEMM_SM100_STATUS_NO_DEVICE);
+        return 0;
+    }
+    if (P.nbd > kMaxBatchDims) {
+        return 0;
+    }
+    const double work = static_cast<double>(P.M) * P.N * P.K * static_cast<double>(P.batches);
+    const bool want_tc = P.K > 0 && t_path != 2 && (t_path == 1 || work >= kTcMinWork);
+    if (want_tc) {
+        int kid = -1;
+        const int r = try_tc(P, ds, stream, &kid);
+        if (r < 0)
+            return 0;
+        if (r == 1) {
+            t_info.builtin_matmul_calls++;
+            t_info.last_matmul = family_name(P.dt);
+            t_info.last_blas_status = 0;
+            t_last_kernel = kernel_name(kid);
+            return 1;
+        }
+    }
+    cudaError_t err;
+    switch (P.dt) {
+    case DT_F32: err = launch_simt<float>(P, stream); break;
+    case DT_F64: err = launch_simt<double>(P, stream); break;
+    case DT_F16: err = launch_simt<__half>(P, stream); break;
+    default: err = launch_simt<__nv_bfloat16>(P, stream); break;
+    }
+    if (err != cudaSuccess) {
+        set_status(static_cast<int>(err));
+        return 0;
+    }
+    t_info.builtin_matmul_calls++;
+    t_info.last_matmul = family_name(P.dt);
+    t_info.last_blas_status = 0;
+    t_last_kernel = simt_name(P.dt);
+    return 1;
+}
+
+int dtype_code(dtype_t dtype)
+{
+    switch (dtype) {
+    case DTYPE_FLOAT32: return DT_F32;
+    case DTYPE_FLOAT64: return DT_F64;
+    case DTYPE_FLOAT16: return DT_F16;
+    case DTYPE_BFLOAT16: return DT_BF16;
+    default: return -1;
+    }
+}
+
+int nd_entry(int dt, const void *a, const void *b, void *c, int *shape_a, size_t *stride_a,
+             int nd_a, int *shape_b, size_t *stride_b, int nd_b, int *shape_c, size_t *stride_c,
+             int nd_c, const void *bias, int act, cudaStream_t stream)
+{
+    Problem P;
+    const int v = build_problem(dt, a, b, c, shape_a, stride_a, nd_a, shape_b, stride_b, nd_b,
+                                shape_c, stride_c, nd_c, &P);
+    if (v == 0)
+        return 0;
+    if (v == 2)
+        return 1;
+    P.bias = bias;
+    P.act = act;
+    return run(P, stream);
+}
+
+} // namespace
+
+// ============================================================ C ABI
+
+PT_API void cuda_blas_shutdown(void)
+{
+    t_info = {};
+    t_plans.clear();
+    t_last_kernel = "none";
+}
+
+PT_API int cuda_blas_set_precision(int precision)
+{
+    if (precision != CUDA_MATMUL_PRECISION_FP32_STRICT && precision != CUDA_MATMUL_PRECISION_TF32)
+        return 0;
+    t_precision = precision;
+    return 1;
+}
+
+PT_API const char *cuda_blas_precision_name(void)
+{
+    return t_precision == CUDA_MATMUL_PRECISION_TF32 ? "tf32" : "fp32-strict";
+}
+
+PT_API void cuda_blas_info(cuda_backend_info *info)
+{
+    if (!info)
+        return;
+    info->cublas = 0;
+    info->cublas_lt = 0;
+    info->blas_calls = t_info.blas_calls;
+    info->lt_calls = t_info.lt_calls;
+    info->builtin_matmul_calls = t_info.builtin_matmul_calls;
+    info->last_matmul = t_info.last_matmul ? t_info.last_matmul : "none";
+    info->last_blas_status = t_info.last_blas_status;
+    info->precision = cuda_blas_precision_name();
+}
+
+PT_API int cuda_matmul_launcher(float *a, float *b, float *c, int m, int n, int k,
+                                size_t a_stride0, size_t a_stride1, size_t b_stride0,
+                                size_t b_stride1, size_t c_stride0, size_t c_stride1,
+                                cudaStream_t stream)
+{
+    // reference argument naming: m = rows, n = inner, k = cols
+    if (m < 0 || n < 0 || k < 0)
+        return 0;
+    if (!m || !k)
+        return 1;
+    int shape_a[2] = {m, n}, shape_b[2] = {n, k}, shape_c[2] = {m, k};
+    size_t stride_a[2] = {a_stride0, a_stride1}, stride_b[2] = {b_stride0, b_stride1};
+    size_t stride_c[2] = {c_stride0, c_stride1};
+    return nd_entry(DT_F32, a, b, c, shape_a, stride_a, 2, shape_b, stride_b, 2, shape_c, stride_c,
+                    2, nullptr, ACT_NONE, stream);
+}
+
+PT_API int cuda_batched_matmul_nd_launcher(float *a, float *b, float *c, int *shape_a,
+                                           size_t *stride_a, int nd_a, int *shape_b,
+                                           size_t *stride_b, int nd_b, int *shape_c,
+                                           size_t *stride_c, int nd_c, cudaStream_t stream)
+{
+    return nd_entry(DT_F32, a, b, c, shape_a, stride_a, nd_a, shape_b, stride_b, nd_b, shape_c,
+                    stride_c, nd_c, nullptr, ACT_NONE, stream);
+}
+
+PT_API int cuda_low_precision_matmul_nd_launcher(void *a, void *b, void *c, dtype_t dtype,
+                                                 int *shape_a, size_t *stride_a, int nd_a,
+                                                 int *shape_b, size_t *stride_b, int nd_b,
+                                                 int *shape_c, size_t *stride_c, int nd_c,
+                                                 cudaStream_t stream)
+{
+    if (dtype != DTYPE_FLOAT16 && dtype != DTYPE_BFLOAT16)
+        return 0;
+    return nd_entry(dtype_code(dtype), a, b, c, shape_a, stride_a, nd_a, shape_b, stride_b, nd_b,
+                    shape_c, stride_c, nd_c, nullptr, ACT_NONE, stream);
+}
+
+PT_API int cuda_f64_matmul_nd_launcher(double *a, double *b, double *c, int *shape_a,
+                                       size_t *stride_a, int nd_a, int *shape_b, size_t *stride_b,
+                                       int nd_b, int *shape_c, size_t *stride_c, int nd_c,
+                                       cudaStream_t stream)
+{
+    return nd_entry(DT_F64, a, b, c, shape_a, stride_a, nd_a, shape_b, stride_b, nd_b, shape_c,
+                    stride_c, nd_c, nullptr, ACT_NONE, stream);
+}
+
+PT_API int cuda_matmul_epilogue_nd_launcher(void *a, void *b, void *c, dtype_t dtype,
+                                            int *shape_a, size_t *stride_a, int nd_a,
+                                            int *shape_b, size_t *stride_b, int nd_b,
+                                            int *shape_c, size_t *stride_c, int nd_c,
+                                            const void *bias, int activation, cudaStream_t stream)
+{
+    const int dt = dtype_code(dtype);
+    if (dt < 0 || activation < CUDA_MATMUL_EPILOGUE_NONE ||
+        activation > CUDA_MATMUL_EPILOGUE_SIGMOID)
+        return 0;
+    return nd_entry(dt, a, b, c, shape_a, stride_a, nd_a, shape_b, stride_b, nd_b, shape_c,
+                    stride_c, nd_c, bias, activation, stream);
+}
+
+PT_API int cuda_blas_tune_matmul(float *a, float *b, float *c, int rows, int inner, int cols,
+                                 size_t a_stride0, size_t a_stride1, size_t b_stride0,
+                                 size_t b_stride1, cudaStream_t stream,
+                                 cuda_matmul_tuning_result *result)
+{
+    if (!a || !b || !c || !result || rows <= 0 || inner <= 0 || cols <= 0 ||
+        static_cast<double>(rows) * inner * cols < kTuneMinWork)
+        return 0;
+    int shape_a[2] = {rows, inner}, shape_b[2] = {inner, cols}, shape_c[2] = {rows, cols};
+    size_t stride_a[2] = {a_stride0, a_stride1}, stride_b[2] = {b_stride0, b_stride1};
+    size_t stride_c[2] = {static_cast<size_t>(cols), 1};
+    Problem P;
+    if (build_problem(DT_F32, a, b, c, shape_a, stride_a, 2, shape_b, stride_b, 2, shape_c,
+                      stride_c, 2, &P) != 1)
+        return 0;
+    DeviceState *ds = device_state();
+    if (!ds)
+        return -1;
+
+    const int strict_algos[] = {1};
+    const int tf32_algos[] = {2, 3};
+    const int *algos = t_precision == CUDA_MATMUL_PRECISION_TF32 ? tf32_algos : strict_algos;
+    const int n_algos = t_precision == CUDA_MATMUL_PRECISION_TF32 ? 2 : 1;
+
+    cudaEvent_t start = nullptr, stop = nullptr;
+    if (cudaEventCreate(&start) != cudaSuccess || cudaEventCreate(&stop) != cudaSuccess) {
+        if (start) cudaEventDestroy(start);
+        return -1;
+    }
+    cuda_matmul_tuning_result measured = {};
+    measured.selected_candidate = -1;
+    int best_algo = -1;
+    double best_ms = 0.0;
+    int rc = 1;
+    for (int i = 0; i < n_algos && rc == 1; i++) {
+        const int algo = algos[i];
+        const int kid = algorithm_kernel(algo);
+        P.forced_bn = (kid == KID_TF32_256) ? 256 : 128;
+        constexpr int kWarmups = 2, kSamples = 5;   // matmul_kernels.cu:373-374
+        float times[kSamples];
+        bool eligible = true;
+        for (int s = -kWarmups; s < kSamples; s++) {
+            if (s >= 0 && cudaEventRecord(start, stream) != cudaSuccess) { rc = -1; break; }
+            int launched = -1;
+            const int r = try_tc(P, ds, stream, &launched);
+            if (r < 0) { rc = -1; break; }
+            if (r == 0) { eligible = false; break; }
+            if (s >= 0) {
+                if (cudaEventRecord(stop, stream) != cudaSuccess ||
+                    cudaEventSynchronize(stop) != cudaSuccess ||
+                    cudaEventElapsedTime(&times[s], start, stop) != cudaSuccess) {
+                    rc = -1;
+                    break;
+                }
+            }
+        }
+        if (rc != 1 || !eligible)
+            break;
+        std::sort(times, times + kSamples);
+        const double median = times[kSamples / 2];
+        const int idx = measured.candidate_count++;
+        measured.candidates[idx].algorithm_id = algo;
+        measured.candidates[idx].workspace_bytes = 0;
+        measured.candidates[idx].median_ms = median;
+        if (best_algo < 0 || median < best_ms) {
+            best_ms = median;
+            best_algo = algo;
+            measured.selected_candidate = idx;
+        }
+    }
+    cudaEventDestroy(start);
+    cudaEventDestroy(stop);
+    if (rc < 0) {
+        set_status(static_cast<int>(cudaGetLastError()));
+        return -1;
+    }
+    if (best_algo < 0)
+        return 0;
+
+    // pin the winner, replacing an existing plan for the same key
+    TunedPlan plan = {rows, inner, cols, a_stride0, a_stride1, b_stride0, b_stride1,
+                      t_precision, best_algo};
+    for (size_t i = 0; i < t_plans.size(); i++) {
+        const TunedPlan &t = t_plans[i];
+        if (t.rows == rows && t.inner == inner && t.cols == cols && t.a_s0 == a_stride0 &&
+            t.a_s1 == a_stride1 && t.b_s0 == b_stride0 && t.b_s1 == b_stride1 &&
+            t.precision == t_precision) {
+            t_plans.erase(t_plans.begin() + static_cast<long>(i));
+            break;
+        }
+    }
+    if (t_plans.size() >= kMaxTunedPlans)
+        t_plans.erase(t_plans.begin());
+    t_plans.push_back(plan);
+    // leave the product of the selected configuration in c
+    P.forced_bn = best_algo == 3 ? 256 : 128;
+    int kid = -1;
+    if (try_tc(P, ds, stream, &kid) != 1)
+        return -1;
+    t_info.builtin_matmul_calls++;
+    t_info.last_matmul = "builtin";
+    t_last_kernel = kernel_name(kid);
+    *result = measured;
+    return 1;
+}
+
+PT_API const char *gemm_sm100_last_kernel(void) { return t_last_kernel; }
+
+PT_API int gemm_sm100_set_path(int path)
+{
+    const int prev = t_path;
+    if (path >= 0 && path <= 2)
+        t_path = path;
+    return prev;
+}
+
+PT_API int gemm_sm100_device_status(int device, int clear)
+{
+    int prev = -1;
+    if (cudaGetDevice(&prev) != cudaSuccess)
+        return -1;
+    if (device != prev && cudaSetDevice(device) != cudaSuccess)
+        return -1;
+    int value = -1;
+    if (cudaDeviceSynchronize() == cudaSuccess &&
+        cudaMemcpyFromSymbol(&value, g_device_status, sizeof(int)) == cudaSuccess && clear) {
+        const int zero = 0;
+        if (cudaMemcpyToSymbol(g_device_status, &zero, sizeof(int)) != cudaSuccess)
+            value = -1;
+    }
+    if (device != prev)
+        cudaSetDevice(prev);
+    return value;
+}
+
+PT_API const char *gemm_sm100_algorithm_name(int algorithm_id)
+{
+    const int kid = algorithm_kernel(algorithm_id);
+    return kid < 0 ? "unknown" : kernel_name(kid);
+}
+
+PT_API int gemm_sm100_version(void) { return 100; }

@@ -1,0 +1,505 @@
+// Persistent, warp-specialised tcgen05 GEMM for sm_100a.
+//
+//   C[b] = epilogue(A[b] . B[b])      A: [M,K], B: [K,N], C: [M,N] per batch b
+//
+// Replaces the built-in tiled kernels and the cuBLAS calls of the reference
+// (src/backends/cuda/matmul_kernels.cu:458-588, 612-672, 738-848).  Roles:
+//   warp 0       TMA producer: fills a STAGES-deep shared-memory ring with
+//                128-byte-swizzled A and B tiles (K-major or MN-major).
+//   warp 1       allocates TMEM; one thread issues tcgen05.mma into one of two
+//                TMEM accumulators (128 lanes x BN fp32 columns each).
+//   warps 2..5   epilogue: tcgen05.ld the accumulator, optional bias +
+//                activation, convert, stage 32x(128 B) boxes in swizzled shared
+//                memory and write them with TMA stores.  Double-buffered TMEM
+//                lets the epilogue of tile i overlap the mainloop of tile i+1.
+//   warps 6..9   (SPLIT3 only) split each FP32 tile into TF32 hi/lo parts so
+//                the MMA warp can issue hi*hi + hi*lo + lo*hi (3xTF32).
+// Tiles (batch, m-block, n-block) are distributed round-robin over a grid of
+// at most one CTA per SM.  Batch is folded into the tile index and into rank-5
+// tensor maps, so rows past M or columns past N of one batch are clipped by
+// TMA and never touch a neighbouring batch.  Every wait is bounded; a timeout
+// sets the CTA's abort flag and a device status word and the kernel drains
+// its own copies and MMAs, frees TMEM and returns.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include "ptx_sm100.cuh"
+
+namespace ptg {
+
+enum InKind : int { IN_F16 = 0, IN_BF16 = 1, IN_TF32 = 2, IN_F32X3 = 3 };
+enum OutKind : int { OUT_F32 = 0, OUT_F16 = 1, OUT_BF16 = 2 };
+enum Activation : int { ACT_NONE = 0, ACT_TANH = 1, ACT_RELU = 2, ACT_SIGMOID = 3 };
+
+// Status codes written to the device status word (first error wins).
+enum DeviceStatus : int {
+    DEV_OK = 0,
+    DEV_TIMEOUT_PRODUCER = 1,
+    DEV_TIMEOUT_MMA = 2,
+    DEV_TIMEOUT_EPILOGUE = 3,
+    DEV_TIMEOUT_SPLIT = 4,
+};
+
+struct TcParams {
+    int M, N, K;
+    int m_blocks, n_blocks, k_blocks;
+    long long tiles;
+    int nbd;          // merged batch dims (0..3)
+    int bshape[3];    // their extents, outermost first
+    int a_slot[3];    // tensor-map coordinate slot (2..4) of merged dim d in A, -1 = broadcast
+    int b_slot[3];
+    int a_mn_major;   // 1: A tile is M-contiguous (transposed view)
+    int b_mn_major;   // 1: B tile is N-contiguous (row-major B)
+    uint32_t idesc;   // tcgen05 instruction descriptor
+    const void *bias; // [N] in the output dtype, or null
+    int act;
+    int *status;      // device status word
+};
+
+__device__ __forceinline__ float apply_activation(float v, int act)
+{
+    switch (act) {
+    case ACT_TANH: return tanhf(v);
+    case ACT_RELU: return v > 0.0f ? v : 0.0f;
+    case ACT_SIGMOID: return 1.0f / (1.0f + expf(-v));
+    default: return v;
+    }
+}
+
+template <int OUT>
+struct OutTraits;
+template <>
+struct OutTraits<OUT_F32> {
+    static constexpr int kBytes = 4;
+    __device__ static float round_trip(float v) { return v; }
+    __device__ static float load(const void *p, int i) { return static_cast<const float *>(p)[i]; }
+};
+template <>
+struct OutTraits<OUT_F16> {
+    static constexpr int kBytes = 2;
+    __device__ static float round_trip(float v) { return __half2float(__float2half_rn(v)); }
+    __device__ static float load(const void *p, int i)
+    {
+        return __half2float(static_cast<const __half *>(p)[i]);
+    }
+};
+template <>
+struct OutTraits<OUT_BF16> {
+    static constexpr int kBytes = 2;
+    __device__ static float round_trip(float v)
+    {
+        return __bfloat162float(__float2bfloat16_rn(v));
+    }
+    __device__ static float load(const void *p, int i)
+    {
+        return __bfloat162float(static_cast<const __nv_bfloat16 *>(p)[i]);
+    }
+};
+
+__device__ __forceinline__ uint32_t pack2(float lo, float hi, int out)
+{
+    if (out == OUT_F16) {
+        __half2 h = __floats2half2_rn(lo, hi);
+        return *reinterpret_cast<uint32_t *>(&h);
+    }
+    __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<uint32_t *>(&h);
+}
+
+// FP32 -> TF32 with round-to-nearest (ties away), low 13 bits cleared.
+__device__ __forceinline__ float round_tf32(float x)
+{
+    uint32_t r;
+    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+    return __uint_as_float(r);
+}
+
+template <int IN_KIND, int BN_, int OUT>
+struct TcConfig {
+    static constexpr int BM = 128;
+    static constexpr int BN = BN_;
+    static constexpr bool kSplit3 = IN_KIND == IN_F32X3;
+    static constexpr bool kTf32 = IN_KIND == IN_TF32 || IN_KIND == IN_F32X3;
+    static constexpr int kInBytes = kTf32 ? 4 : 2;
+    static constexpr int BK = 128 / kInBytes;            // one 128-byte swizzle row of K
+    static constexpr int kMmaK = kTf32 ? 8 : 16;          // 32 bytes of K per instruction
+    static constexpr int kKSteps = BK / kMmaK;            // 4
+    static constexpr int kChunk = 128 / kInBytes;         // MN elements per 128-byte row
+    static constexpr int kChunkBytes = 128 * BK;          // one MN-major box (chunk x BK)
+    static constexpr int kATile = BM * BK * kInBytes;     // 16 KB
+    static constexpr int kBTile = BN * BK * kInBytes;     // 16 or 32 KB
+    static constexpr int kLoadBytes = kATile + kBTile;    // bytes TMA lands per stage
+    static constexpr int kStageBytes = kLoadBytes * (kSplit3 ? 2 : 1);
+    static constexpr int kStages = (196608 / kStageBytes) > 8 ? 8 : (196608 / kStageBytes);
+    static constexpr int kOutBytes = OutTraits<OUT>::kBytes;
+    static constexpr int kEpiCols = 128 / kOutBytes;      // columns per staged box
+    static constexpr int kEpiChunks = BN / kEpiCols;
+    static constexpr int kEpiBufBytes = 32 * 128;         // 32 rows x 128 B
+    static constexpr int kEpiWarps = 4;
+    static constexpr int kSplitWarps = kSplit3 ? 4 : 0;
+    static constexpr int kThreads = 32 * (2 + kEpiWarps + kSplitWarps);
+    static constexpr int kTmemCols = 2 * BN;              // two accumulators
+    static constexpr int kRingBytes = kStages * kStageBytes;
+    static constexpr int kEpiOffset = kRingBytes;
+    static constexpr int kBarOffset = kEpiOffset + kEpiWarps * 2 * kEpiBufBytes;
+    // full, empty, ready per stage; tmem full/empty x2; drain
+    static constexpr int kNumBars = 3 * kStages + 4 + 1;
+    static constexpr int kSmemBytes = kBarOffset + kNumBars * 8 + 16 + 1024;
+    static_assert(kStages >= 2, "pipeline needs at least two stages");
+    static_assert(BN % kEpiCols == 0, "epilogue box must divide BN");
+    static_assert(kSmemBytes <= 232448, "shared memory budget exceeded");
+};
+
+__device__ __forceinline__ void decode_batch(long long b, const TcParams &p, int (&c)[3])
+{
+    c[0] = c[1] = c[2] = 0;
+    for (int d = p.nbd - 1; d >= 0; d--) {
+        c[d] = static_cast<int>(b % p.bshape[d]);
+        b /= p.bshape[d];
+    }
+}
+
+__device__ __forceinline__ void operand_coords(const int (&c)[3], const int (&slot)[3], int nbd,
+                                               int (&o)[3])
+{
+    o[0] = o[1] = o[2] = 0;
+    for (int d = 0; d < nbd; d++)
+        if (slot[d] >= 2)
+            o[slot[d] - 2] = c[d];
+}
+
+__device__ __forceinline__ void record_failure(volatile int *abort, int *status, int code)
+{
+    *abort = 1;
+    atomicCAS(status, 0, code);
+}
+
+template <int IN_KIND, int BN, int OUT>
+__global__ void __launch_bounds__(TcConfig<IN_KIND, BN, OUT>::kThreads, 1)
+    tc_gemm_kernel(const __grid_constant__ CUtensorMap tma_a,
+                   const __grid_constant__ CUtensorMap tma_b,
+                   const __grid_constant__ CUtensorMap tma_c, const TcParams p)
+{
+    using Cfg = TcConfig<IN_KIND, BN, OUT>;
+    constexpr int S = Cfg::kStages;
+
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + Cfg::kBarOffset);
+    uint64_t *full = bars;
+    uint64_t *empty = bars + S;
+    uint64_t *ready = bars + 2 * S;
+    uint64_t *tfull = bars + 3 * S;
+    uint64_t *tempty = bars + 3 * S + 2;
+    uint64_t *drain = bars + 3 * S + 4;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + Cfg::kNumBars);
+    volatile int *abort = reinterpret_cast<volatile int *>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+
+    if (warp == 0 && lane == 0) {
+        prefetch_tensor_map(&tma_a);
+        prefetch_tensor_map(&tma_b);
+        prefetch_tensor_map(&tma_c);
+        for (int s = 0; s < S; s++) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+            mbar_init(&ready[s], Cfg::kSplit3 ? Cfg::kSplitWarps * 32 : 1);
+        }
+        for (int i = 0; i < 2; i++) {
+            mbar_init(&tfull[i], 1);
+            mbar_init(&tempty[i], Cfg::kEpiWarps);
+        }
+        mbar_init(drain, 1);
+        *abort = 0;
+        fence_barrier_init();
+    }
+    if (warp == 1) {
+        tmem_alloc(tmem_slot, Cfg::kTmemCols);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    if (warp == 0) {
+        // ------------------------------------------------------------ producer
+        if (lane == 0) {
+            int stage = 0;
+            uint32_t phase = 0;
+            uint32_t issued_mask = 0, parity_mask = 0;
+            bool ok = true;
+            for (long long t = blockIdx.x; ok && t < p.tiles; t += gridDim.x) {
+                const int nb = static_cast<int>(t % p.n_blocks);
+                const long long r = t / p.n_blocks;
+                const int mb = static_cast<int>(r % p.m_blocks);
+                const long long batch = r / p.m_blocks;
+                int c[3], ca[3], cb[3];
+                decode_batch(batch, p, c);
+                operand_coords(c, p.a_slot, p.nbd, ca);
+                operand_coords(c, p.b_slot, p.nbd, cb);
+                const int m0 = mb * Cfg::BM, n0 = nb * BN;
+                for (int kb = 0; kb < p.k_blocks; kb++) {
+                    if (!mbar_wait(&empty[stage], phase ^ 1, abort)) {
+                        record_failure(abort, p.status, DEV_TIMEOUT_PRODUCER);
+                        ok = false;
+                        break;
+                    }
+                    uint8_t *sa = smem + stage * Cfg::kStageBytes;
+                    uint8_t *sb = sa + Cfg::kATile;
+                    mbar_arrive_expect_tx(&full[stage], Cfg::kLoadBytes);
+                    const int k0 = kb * Cfg::BK;
+                    if (!p.a_mn_major) {
+                        tma_load_5d(sa, &tma_a, &full[stage], k0, m0, ca[0], ca[1], ca[2]);
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < Cfg::BM / Cfg::kChunk; j++)
+                            tma_load_5d(sa + j * Cfg::kChunkBytes, &tma_a, &full[stage],
+                                        m0 + j * Cfg::kChunk, k0, ca[0], ca[1], ca[2]);
+                    }
+                    if (!p.b_mn_major) {
+                        tma_load_5d(sb, &tma_b, &full[stage], k0, n0, cb[0], cb[1], cb[2]);
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < BN / Cfg::kChunk; j++)
+                            tma_load_5d(sb + j * Cfg::kChunkBytes, &tma_b, &full[stage],
+                                        n0 + j * Cfg::kChunk, k0, cb[0], cb[1], cb[2]);
+                    }
+                    issued_mask |= 1u << stage;
+                    parity_mask = (parity_mask & ~(1u << stage)) | (phase << stage);
+                    if (++stage == S) {
+                        stage = 0;
+                        phase ^= 1;
+                    }
+                }
+            }
+            // Let every copy this thread started land before shared memory
+            // can be released (bounded, ignores the abort flag).
+            for (int s = 0; s < S; s++) {
+                if (issued_mask & (1u << s)) {
+                    int no_abort = 0;
+                    mbar_wait(&full[s], (parity_mask >> s) & 1u, &no_abort);
+                }
+            }
+        }
+    } else if (warp == 1) {
+        // ------------------------------------------------------------ MMA issuer
+        if (lane == 0) {
+            int stage = 0;
+            uint32_t phase = 0;
+            long long iter = 0;
+            bool ok = true;
+            const uint32_t smem_base = smem_addr(smem);
+            for (long long t = blockIdx.x; ok && t < p.tiles; t += gridDim.x, iter++) {
+                const int acc = static_cast<int>(iter & 1);
+                const uint32_t acc_phase = static_cast<uint32_t>((iter >> 1) & 1);
+                if (!mbar_wait(&tempty[acc], acc_phase ^ 1, abort)) {
+                    record_failure(abort, p.status, DEV_TIMEOUT_MMA);
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
+                for (int kb = 0; kb < p.k_blocks; kb++) {
+                    uint64_t *gate = Cfg::kSplit3 ? &ready[stage] : &full[stage];
+                    if (!mbar_wait(gate, phase, abort)) {
+                        record_failure(abort, p.status, DEV_TIMEOUT_MMA);
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t sa = smem_base + stage * Cfg::kStageBytes;
+                    const uint32_t sb = sa + Cfg::kATile;
+#pragma unroll
+                    for (int k = 0; k < Cfg::kKSteps; k++) {
+                        const uint32_t a_off = p.a_mn_major ? k * (Cfg::kMmaK / 8) * 1024 : k * 32;
+                        const uint32_t b_off = p.b_mn_major ? k * (Cfg::kMmaK / 8) * 1024 : k * 32;
+                        const uint32_t a_lbo = p.a_mn_major ? Cfg::kChunkBytes : 16;
+                        const uint32_t b_lbo = p.b_mn_major ? Cfg::kChunkBytes : 16;
+                        const uint64_t ad = smem_desc_sw128(sa + a_off, a_lbo, 1024);
+                        const uint64_t bd = smem_desc_sw128(sb + b_off, b_lbo, 1024);
+                        const uint32_t accumulate = (kb | k) != 0;
+                        if constexpr (Cfg::kTf32) {
+                            umma_tf32(d_tmem, ad, bd, p.idesc, accumulate);
+                            if constexpr (Cfg::kSplit3) {
+                                const uint64_t ad_lo =
+                                    smem_desc_sw128(sa + Cfg::kLoadBytes + a_off, a_lbo, 1024);
+                                const uint64_t bd_lo =
+                                    smem_desc_sw128(sb + Cfg::kLoadBytes + b_off, b_lbo, 1024);
+                                umma_tf32(d_tmem, ad, bd_lo, p.idesc, 1);
+                                umma_tf32(d_tmem, ad_lo, bd, p.idesc, 1);
+                            }
+                        } else {
+                            umma_f16(d_tmem, ad, bd, p.idesc, accumulate);
+                        }
+                    }
+                    umma_commit(&empty[stage]);
+                    if (++stage == S) {
+                        stage = 0;
+                        phase ^= 1;
+                    }
+                }
+                if (!ok)
+                    break;
+                umma_commit(&tfull[acc]);
+            }
+            // Wait until every MMA this thread issued has completed, so TMEM
+            // and the shared-memory ring can be released safely.
+            umma_commit(drain);
+            int no_abort = 0;
+            mbar_wait(drain, 0, &no_abort);
+        }
+    } else if (warp < 2 + Cfg::kEpiWarps) {
+        // ------------------------------------------------------------ epilogue
+        const int ew = warp - 2;                 // 0..3
+        const int quad = warp & 3;               // TMEM lane quadrant this warp may access
+        uint8_t *stage_buf = smem + Cfg::kEpiOffset + ew * 2 * Cfg::kEpiBufBytes;
+        int buf = 0;
+        long long iter = 0;
+        for (long long t = blockIdx.x; t < p.tiles; t += gridDim.x, iter++) {
+            const int acc = static_cast<int>(iter & 1);
+            const uint32_t acc_phase = static_cast<uint32_t>((iter >> 1) & 1);
+            // the whole warp must agree before the .sync.aligned TMEM loads
+            const bool got = __all_sync(0xffffffffu, mbar_wait(&tfull[acc], acc_phase, abort));
+            if (!got) {
+                if (lane == 0)
+                    record_failure(abort, p.status, DEV_TIMEOUT_EPILOGUE);
+                break;
+            }
+            tc_fence_after();
+            const int nb = static_cast<int>(t % p.n_blocks);
+            const long long r = t / p.n_blocks;
+            const int mb = static_cast<int>(r % p.m_blocks);
+            const long long batch = r / p.m_blocks;
+            int c[3];
+            decode_batch(batch, p, c);
+            const int m0 = mb * Cfg::BM, n0 = nb * BN;
+            const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) +
+                                   static_cast<uint32_t>(acc * BN);
+#pragma unroll 1
+            for (int ch = 0; ch < Cfg::kEpiChunks; ch++) {
+                float v[Cfg::kEpiCols];
+                {
+                    uint32_t r32[32];
+#pragma unroll
+                    for (int h = 0; h < Cfg::kEpiCols / 32; h++) {
+                        tmem_ld_32x32b_x32(t_row + ch * Cfg::kEpiCols + h * 32, r32);
+                        tmem_ld_wait();
+#pragma unroll
+                        for (int i = 0; i < 32; i++)
+                            v[h * 32 + i] = __uint_as_float(r32[i]);
+                    }
+                }
+                if (ch == Cfg::kEpiChunks - 1) {
+                    // accumulator fully read: hand it back to the MMA warp
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0)
+                        mbar_arrive(&tempty[acc]);
+                }
+                const int col0 = n0 + ch * Cfg::kEpiCols;
+                if (p.bias != nullptr || p.act != ACT_NONE) {
+                    // Same arithmetic as the unfused plan: the matmul result is
+                    // rounded to the output dtype, then bias add and activation
+                    // run in float and round once.
+#pragma unroll
+                    for (int i = 0; i < Cfg::kEpiCols; i++) {
+                        float x = OutTraits<OUT>::round_trip(v[i]);
+                        const int col = col0 + i;
+                        if (p.bias != nullptr && col < p.N)
+                            x += OutTraits<OUT>::load(p.bias, col);
+                        v[i] = apply_activation(x, p.act);
+                    }
+                }
+                uint8_t *sbuf = stage_buf + buf * Cfg::kEpiBufBytes;
+                if (lane == 0)
+                    bulk_wait_group_read<1>();   // the store that last used sbuf has read it
+                __syncwarp();
+                uint8_t *row = sbuf + lane * 128;
+#pragma unroll
+                for (int j = 0; j < 8; j++) {
+                    uint4 q;
+                    if constexpr (OUT == OUT_F32) {
+                        q.x = __float_as_uint(v[4 * j + 0]);
+                        q.y = __float_as_uint(v[4 * j + 1]);
+                        q.z = __float_as_uint(v[4 * j + 2]);
+                        q.w = __float_as_uint(v[4 * j + 3]);
+                    } else {
+                        q.x = pack2(v[8 * j + 0], v[8 * j + 1], OUT);
+                        q.y = pack2(v[8 * j + 2], v[8 * j + 3], OUT);
+                        q.z = pack2(v[8 * j + 4], v[8 * j + 5], OUT);
+                        q.w = pack2(v[8 * j + 6], v[8 * j + 7], OUT);
+                    }
+                    // 128-byte swizzle: 16-byte chunk j of row r lives at j ^ (r % 8)
+                    *reinterpret_cast<uint4 *>(row + ((j ^ (lane & 7)) << 4)) = q;
+                }
+                fence_proxy_async_smem();
+                __syncwarp();
+                // boxes entirely past N or M hold nothing to write
+                if (lane == 0 && col0 < p.N && m0 + quad * 32 < p.M) {
+                    tma_store_5d(&tma_c, sbuf, col0, m0 + quad * 32, c[0], c[1], c[2]);
+                    bulk_commit_group();
+                }
+                buf ^= 1;
+            }
+        }
+        if (lane == 0)
+            bulk_wait_group<0>();
+        __syncwarp();
+    } else {
+        // ------------------------------------------------------------ 3xTF32 split
+        if constexpr (Cfg::kSplit3) {
+            const int st = threadIdx.x - 32 * (2 + Cfg::kEpiWarps);   // 0..127
+            int stage = 0;
+            uint32_t phase = 0;
+            bool ok = true;
+            for (long long t = blockIdx.x; ok && t < p.tiles; t += gridDim.x) {
+                for (int kb = 0; kb < p.k_blocks; kb++) {
+                    if (!mbar_wait(&full[stage], phase, abort)) {
+                        record_failure(abort, p.status, DEV_TIMEOUT_SPLIT);
+                        ok = false;
+                        break;
+                    }
+                    float4 *raw = reinterpret_cast<float4 *>(smem + stage * Cfg::kStageBytes);
+                    float4 *lo = reinterpret_cast<float4 *>(smem + stage * Cfg::kStageBytes +
+                                                            Cfg::kLoadBytes);
+                    constexpr int kVecs = Cfg::kLoadBytes / 16;
+#pragma unroll 4
+                    for (int i = st; i < kVecs; i += Cfg::kSplitWarps * 32) {
+                        float4 x = raw[i], h, l;
+                        h.x = round_tf32(x.x);
+                        h.y = round_tf32(x.y);
+                        h.z = round_tf32(x.z);
+                        h.w = round_tf32(x.w);
+                        l.x = isfinite(h.x) ? round_tf32(x.x - h.x) : 0.0f;
+                        l.y = isfinite(h.y) ? round_tf32(x.y - h.y) : 0.0f;
+                        l.z = isfinite(h.z) ? round_tf32(x.z - h.z) : 0.0f;
+                        l.w = isfinite(h.w) ? round_tf32(x.w - h.w) : 0.0f;
+                        raw[i] = h;
+                        lo[i] = l;
+                    }
+                    fence_proxy_async_smem();
+                    mbar_arrive(&ready[stage]);
+                    if (++stage == S) {
+                        stage = 0;
+                        phase ^= 1;
+                    }
+                }
+            }
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 1) {
+        __syncwarp();
+        tmem_dealloc(tmem_base, Cfg::kTmemCols);
+    }
+}
+
+} // namespace ptg

@@ -1,0 +1,236 @@
+// Tensor-level matmul dispatch (include/pt_tensor.h): the C++ host layer that
+// sits where the PHP extension's C dispatch sits in the reference
+// (src/cuda_array/ca_private.c:1097-1213, src/fusion_execute.c:157-182,
+// src/autograd.c:1539-1585) and calls the launcher ABI of gemm_sm100.h.
+#include "pt_tensor.h"
+
+#include <cstdio>
+#include <cstring>
+
+#define PT_API extern "C" __attribute__((visibility("default")))
+
+namespace {
+
+thread_local char t_error[256] = "";
+
+int fail(int code, const char *fmt, int value = 0)
+{
+    std::snprintf(t_error, sizeof(t_error), fmt, value);
+    return code;
+}
+
+int ok()
+{
+    t_error[0] = '\0';
+    return PT_OK;
+}
+
+// src/tensor_shape.h:7-22
+bool broadcast_shape(const int *a, int na, const int *b, int nb, int *out, int *nout)
+{
+    const int n = na > nb ? na : nb;
+    for (int axis = 0; axis < n; axis++) {
+        const int ia = axis - (n - na), ib = axis - (n - nb);
+        const int ea = ia < 0 ? 1 : a[ia];
+        const int eb = ib < 0 ? 1 : b[ib];
+        if (ea != eb && ea != 1 && eb != 1)
+            return false;
+        out[axis] = ea == 1 ? eb : ea;
+    }
+    *nout = n;
+    return true;
+}
+
+// src/tensor_shape.h:46-59
+bool matmul_shape(const pt_tensor *a, const pt_tensor *b, int *shape, int *ndims)
+{
+    if (a->ndims < 2 || a->ndims > MAX_DIMS || b->ndims < 2 || b->ndims > MAX_DIMS ||
+        a->shape[a->ndims - 1] != b->shape[b->ndims - 2])
+        return false;
+    int nb = 0;
+    if (!broadcast_shape(a->shape, a->ndims - 2, b->shape, b->ndims - 2, shape, &nb))
+        return false;
+    shape[nb] = a->shape[a->ndims - 2];
+    shape[nb + 1] = b->shape[b->ndims - 1];
+    *ndims = nb + 2;
+    return true;
+}
+
+size_t element_size(dtype_t dt)
+{
+    switch (dt) {
+    case DTYPE_FLOAT64: return 8;
+    case DTYPE_FLOAT32: return 4;
+    case DTYPE_FLOAT16:
+    case DTYPE_BFLOAT16: return 2;
+    default: return 0;
+    }
+}
+
+bool supported_dtype(dtype_t dt, int flags)
+{
+    return dt == DTYPE_FLOAT32 || dt == DTYPE_FLOAT16 || dt == DTYPE_BFLOAT16 ||
+           (dt == DTYPE_FLOAT64 && (flags & PT_MATMUL_ALLOW_FLOAT64));
+}
+
+int submission_failed()
+{
+    cuda_backend_info info;
+    std::memset(&info, 0, sizeof(info));
+    cuda_blas_info(&info);
+    return fail(PT_RUNTIME, "Matmul backend submission failed (cuBLAS status %d)",
+                info.last_blas_status);
+}
+
+// Launcher choice of ca_private.c:1127-1137,1168-1200 and fusion_execute.c:159-173.
+int dispatch(const pt_tensor *a, const pt_tensor *b, const pt_tensor *r, cudaStream_t stream)
+{
+    pt_tensor ca = *a, cb = *b, cr = *r;   // the launchers take non-const metadata
+    int status;
+    if (a->dtype == DTYPE_FLOAT32 && a->ndims == 2 && b->ndims == 2)
+        status = cuda_matmul_launcher(static_cast<float *>(a->data), static_cast<float *>(b->data),
+                                      static_cast<float *>(r->data), a->shape[0], a->shape[1],
+                                      b->shape[1], a->strides[0], a->strides[1], b->strides[0],
+                                      b->strides[1], r->strides[0], r->strides[1], stream);
+    else if (a->dtype == DTYPE_FLOAT32)
+        status = cuda_batched_matmul_nd_launcher(
+            static_cast<float *>(a->data), static_cast<float *>(b->data),
+            static_cast<float *>(r->data), ca.shape, ca.strides, a->ndims, cb.shape, cb.strides,
+            b->ndims, cr.shape, cr.strides, r->ndims, stream);
+    else if (a->dtype == DTYPE_FLOAT64)
+        status = cuda_f64_matmul_nd_launcher(
+            static_cast<double *>(a->data), static_cast<double *>(b->data),
+            static_cast<double *>(r->data), ca.shape, ca.strides, a->ndims, cb.shape, cb.strides,
+            b->ndims, cr.shape, cr.strides, r->ndims, stream);
+    else
+        status = cuda_low_precision_matmul_nd_launcher(
+            a->data, b->data, r->data, a->dtype, ca.shape, ca.strides, a->ndims, cb.shape,
+            cb.strides, b->ndims, cr.shape, cr.strides, r->ndims, stream);
+    return status ? ok() : submission_failed();
+}
+
+int check_operands(const pt_tensor *a, const pt_tensor *b, int flags, int *shape, int *ndims)
+{
+    if (!a || !b || a->dtype != b->dtype || !supported_dtype(a->dtype, flags))
+        return fail(PT_INVALID_ARGUMENT,
+                    "matmul requires matching float32, float16 or bfloat16 operands");
+    if (!matmul_shape(a, b, shape, ndims))
+        return fail(PT_INVALID_ARGUMENT, "Matrix multiplication failed - incompatible dimensions");
+    return PT_OK;
+}
+
+void contiguous_strides(const int *shape, int ndims, size_t *strides)
+{
+    size_t s = 1;
+    for (int d = ndims - 1; d >= 0; d--) {
+        strides[d] = s;
+        s *= static_cast<size_t>(shape[d]);
+    }
+}
+
+pt_tensor transposed_view(const pt_tensor *t)
+{
+    pt_tensor v = *t;
+    const int n = t->ndims;
+    v.shape[n - 2] = t->shape[n - 1];
+    v.shape[n - 1] = t->shape[n - 2];
+    v.strides[n - 2] = t->strides[n - 1];
+    v.strides[n - 1] = t->strides[n - 2];
+    return v;
+}
+
+} // namespace
+
+PT_API const char *pt_last_error(void) { return t_error; }
+
+PT_API int pt_matmul_result_shape(const pt_tensor *a, const pt_tensor *b, int *shape, int *ndims)
+{
+    if (!a || !b || !shape || !ndims)
+        return fail(PT_INVALID_ARGUMENT, "Both operands must be valid tensor objects.");
+    if (!matmul_shape(a, b, shape, ndims))
+        return fail(PT_INVALID_ARGUMENT, "Matrix multiplication failed - incompatible dimensions");
+    return ok();
+}
+
+PT_API int pt_tensor_matmul_into(const pt_tensor *a, const pt_tensor *b, const pt_tensor *result,
+                                 int flags, cudaStream_t stream)
+{
+    int shape[MAX_DIMS], ndims = 0;
+    const int v = check_operands(a, b, flags, shape, &ndims);
+    if (v != PT_OK)
+        return v;
+    if (!result || result->dtype != a->dtype || result->ndims != ndims)
+        return fail(PT_INVALID_ARGUMENT, "Matrix multiplication failed - incompatible dimensions");
+    for (int d = 0; d < ndims; d++)
+        if (result->shape[d] != shape[d])
+            return fail(PT_INVALID_ARGUMENT,
+                        "Matrix multiplication failed - incompatible dimensions");
+    return dispatch(a, b, result, stream);
+}
+
+PT_API int pt_tensor_matmul(const pt_tensor *a, const pt_tensor *b, pt_tensor *result, int flags,
+                            cudaStream_t stream)
+{
+    if (!result)
+        return fail(PT_INVALID_ARGUMENT, "Both operands must be valid tensor objects.");
+    int shape[MAX_DIMS], ndims = 0;
+    const int v = check_operands(a, b, flags, shape, &ndims);
+    if (v != PT_OK)
+        return v;
+    pt_tensor r;
+    std::memset(&r, 0, sizeof(r));
+    r.dtype = a->dtype;
+    r.ndims = ndims;
+    std::memcpy(r.shape, shape, sizeof(int) * static_cast<size_t>(ndims));
+    contiguous_strides(shape, ndims, r.strides);
+    size_t total = 1;
+    for (int d = 0; d < ndims; d++)
+        total *= static_cast<size_t>(shape[d]);
+    const size_t bytes = total * element_size(a->dtype);
+    if (bytes) {
+        const cudaError_t err = cudaMallocAsync(&r.data, bytes, stream);
+        if (err != cudaSuccess)
+            return fail(PT_RUNTIME, "Failed to allocate the matmul result (CUDA error %d)",
+                        static_cast<int>(err));
+    }
+    const int s = dispatch(a, b, &r, stream);
+    if (s != PT_OK) {
+        if (r.data)
+            cudaFreeAsync(r.data, stream);
+        return s;
+    }
+    *result = r;
+    return PT_OK;
+}
+
+PT_API void pt_tensor_release(pt_tensor *t, cudaStream_t stream)
+{
+    if (t && t->data) {
+        cudaFreeAsync(t->data, stream);
+        t->data = nullptr;
+    }
+}
+
+PT_API int pt_tensor_matmul_backward(const pt_tensor *a, const pt_tensor *b,
+                                     const pt_tensor *grad_c, const pt_tensor *grad_a,
+                                     const pt_tensor *grad_b, cudaStream_t stream)
+{
+    if (!a || !b || !grad_c || a->dtype != DTYPE_FLOAT32 || b->dtype != DTYPE_FLOAT32 ||
+        grad_c->dtype != DTYPE_FLOAT32)
+        return fail(PT_INVALID_ARGUMENT, "matmul backward requires float32 tensors");
+    if (a->ndims < 2 || b->ndims < 2)
+        return fail(PT_INVALID_ARGUMENT, "Matrix multiplication failed - incompatible dimensions");
+    if (grad_a) {
+        const pt_tensor bt = transposed_view(b);
+        const int s = pt_tensor_matmul_into(grad_c, &bt, grad_a, 0, stream);
+        if (s != PT_OK)
+            return s;
+    }
+    if (grad_b) {
+        const pt_tensor at = transposed_view(a);
+        const int s = pt_tensor_matmul_into(&at, grad_c, grad_b, 0, stream);
+        if (s != PT_OK)
+            return s;
+    }
+    return ok();
+}

@@ -1,0 +1,371 @@
+"""GPU parity of libgemm_sm100.so against the CPU oracle (marked gpu).
+
+Every product goes through the C ABI (phptensors.CudaArray.matmul ->
+pt_tensor_matmul_into -> cuda_*_launcher).  Checks:
+  * golden vectors of the reference's matmul tests, on the automatic kernel
+    choice, with the tensor-core kernel forced, and with the CUDA-core kernel
+    forced -- exact wherever the reference asserts exact values;
+  * seeded random parity with the oracle at sizes it finishes in seconds:
+    odd M/N/K, padded (TMA-aligned) and unaligned views, transposed operands,
+    broadcast and rank-4 batches, for float16/bfloat16 (tolerance of the
+    reference harness, tests/host_array_core_cuda.phpt:33, and normwise 1e-2),
+    float32 (normwise 1e-5) and float64 (bit-exact: same fma order);
+  * BASELINE config sizes through size-independent properties: integer-valued
+    inputs make every summation order exact, so the full-size products must
+    match bit for bit; random inputs are compared with the oracle on sampled
+    output rows.
+"""
+import numpy as np
+import pytest
+
+import oracle_lib as O
+import phptensors as P
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+TOL_ELEM = {"float64": 2e-12, "float16": 5e-3, "bfloat16": 3e-2, "float32": 3e-5}
+TOL_NORM = {"float64": 1e-12, "float16": 1e-2, "bfloat16": 1e-2, "float32": 1e-5}
+TORCH_DT = {"float32": torch.float32, "float64": torch.float64, "float16": torch.float16,
+            "bfloat16": torch.bfloat16}
+
+
+@pytest.fixture(autouse=True)
+def _reset_path():
+    prev = P.set_kernel_path("auto")
+    P.cuda_set_matmul_precision("fp32-strict")
+    yield
+    P.library().gemm_sm100_set_path(prev)
+    P.cuda_set_matmul_precision("fp32-strict")
+
+
+def to_device(op, dtype):
+    storage, shape, strides, offset = op
+    s = np.ascontiguousarray(storage)
+    if dtype in ("float16", "bfloat16"):
+        t = torch.from_numpy(s.view(np.int16).copy()).view(TORCH_DT[dtype])
+    else:
+        t = torch.from_numpy(s.copy())
+    return P.CudaArray(t.cuda(), shape, strides, offset, dtype)
+
+
+def as_f64(storage, dtype):
+    return O.to_float32(storage, dtype).astype(np.float64) if dtype != "float64" else storage
+
+
+def check_close(gpu, ref, dtype, what):
+    g = as_f64(gpu.reshape(-1), dtype)
+    r = as_f64(ref.reshape(-1), dtype)
+    assert g.shape == r.shape, what
+    if g.size == 0:
+        return
+    assert np.all(np.abs(g - r) <= TOL_ELEM[dtype] * np.maximum(1.0, np.abs(r))), what
+    norm = np.max(np.abs(g - r)) / max(1.0, np.max(np.abs(r)))
+    assert norm <= TOL_NORM[dtype], (what, norm)
+
+
+# ------------------------------------------------------------------ golden
+@pytest.mark.parametrize("path", ["auto", "tensor-core", "simt"])
+def test_golden_vectors(golden, path):
+    P.set_kernel_path(path)
+    for case in golden["cases"]:
+        for dt in case["dtypes"]:
+            a = to_device(O.golden_operand(case["a"], dt), dt)
+            b = to_device(O.golden_operand(case["b"], dt), dt)
+            c = a.matmul(b)
+            assert c.getShape() == case["expect_shape"], case["name"]
+            got = as_f64(c.to_numpy().reshape(-1), dt)
+            exp = O.golden_expected(case)
+            if case["tol"] is None:
+                assert np.array_equal(got, exp), (case["name"], dt, path)
+            else:
+                assert np.max(np.abs(got - exp)) < case["tol"], (case["name"], dt, path)
+            info = P.cuda_get_backend_info()
+            if got.size:
+                family = "builtin" if dt == "float32" else "builtin-low-precision"
+                assert info["lastMatmul"] == family
+                if path == "simt":
+                    assert info["kernel"].startswith("simt-")
+    assert P.device_status() == 0
+
+
+def test_golden_tensor_core_kernel_is_used(golden):
+    """Cases whose layouts TMA can describe really run on tcgen05."""
+    P.set_kernel_path("tensor-core")
+    names = {"accel_batched": "float32", "accel_broadcast": "float32", "accel_rank4": "float32",
+             "accel_transposed_view": "float32", "lowp_identity": "bfloat16",
+             "fusion_workspace_parallel_x2": "float32"}
+    for case in golden["cases"]:
+        if case["name"] in names:
+            dt = names[case["name"]]
+            a = to_device(O.golden_operand(case["a"], dt), dt)
+            b = to_device(O.golden_operand(case["b"], dt), dt)
+            got = as_f64(a.matmul(b).to_numpy().reshape(-1), dt)
+            assert np.array_equal(got, O.golden_expected(case)), case["name"]
+            assert P.cuda_get_backend_info()["kernel"].startswith("tc-"), case["name"]
+
+
+def test_reference_rejections(golden):
+    for r in golden["rejects"]:
+        dt = r["dtype"]
+        a = P.CudaArray.ones(r["a_shape"], dt)
+        b = P.CudaArray.ones(r["b_shape"], dt)
+        with pytest.raises(P.InvalidArgumentException) as e:
+            a.matmul(b)
+        assert "matmul" in str(e.value) or "Matrix multiplication" in str(e.value)
+
+
+# ------------------------------------------------------------------ seeded parity
+def padded(values, shape, row_pad, dtype, transpose=False):
+    """A [.., R, C] operand stored with a padded row stride (TMA-aligned), or
+    its transposed view when transpose=True (storage is [.., C, R])."""
+    *batch, R, C = shape
+    if transpose:
+        R, C = C, R
+    ld = C + row_pad
+    nb = int(np.prod(batch)) if batch else 1
+    buf = np.zeros((nb, R, ld), dtype=np.float32)
+    buf[:, :, :C] = values.reshape(nb, R, C)
+    storage = O.to_storage(buf.reshape(-1), dtype)
+    strides = []
+    s = R * ld
+    for d in reversed(batch):
+        strides.insert(0, s)
+        s *= d
+    if transpose:
+        return (storage, list(batch) + [C, R], strides + [1, ld], 0)
+    return (storage, list(batch) + [R, C], strides + [ld, 1], 0)
+
+
+CASES = [
+    # (name, a_shape, b_shape, a_transposed, b_transposed, row padding)
+    ("square", [256, 256], [256, 256], False, False, 0),
+    ("odd_mnk", [131, 77], [77, 263], False, False, 0),
+    ("odd_padded", [131, 77], [77, 263], False, False, 11),
+    ("tiny", [1, 7], [7, 1], False, False, 0),
+    ("skinny_k", [300, 8], [8, 520], False, False, 0),
+    ("a_transposed", [200, 136], [136, 312], True, False, 0),
+    ("b_transposed", [129, 264], [264, 257], False, True, 0),
+    ("both_transposed", [96, 200], [200, 136], True, True, 0),
+    ("batched", [5, 130, 72], [5, 72, 96], False, False, 0),
+    ("broadcast_a", [1, 64, 136], [6, 136, 64], False, False, 0),
+    ("broadcast_b", [3, 2, 136, 40], [2, 40, 264], False, False, 0),
+    ("rank4_transposed", [2, 3, 72, 64], [2, 3, 64, 80], True, True, 0),
+    ("long_k", [64, 4104], [4104, 48], False, False, 0),
+]
+
+
+@pytest.mark.parametrize("dtype", ["bfloat16", "float16", "float32"])
+@pytest.mark.parametrize("path", ["auto", "tensor-core"])
+@pytest.mark.parametrize("case", CASES, ids=[c[0] for c in CASES])
+def test_seeded_parity(case, path, dtype):
+    name, ashape, bshape, at, bt, pad = case
+    P.set_kernel_path(path)
+    seed = sum(map(ord, name))
+    av = O.seeded(ashape, seed, "normal")
+    bv = O.seeded(bshape, seed + 1, "normal")
+    a = padded(av, ashape, pad, dtype, at)
+    b = padded(bv, bshape, pad, dtype, bt)
+    ref = O.host_matmul(a, b, dtype, threads=O.oracle().orc_host_threads())
+    c = to_device(a, dtype).matmul(to_device(b, dtype))
+    check_close(c.to_numpy(), ref, dtype, (name, path, P.cuda_get_backend_info()["kernel"]))
+
+
+@pytest.mark.parametrize("case", CASES, ids=[c[0] for c in CASES])
+def test_float64_bit_exact(case):
+    name, ashape, bshape, at, bt, pad = case
+    av = O.seeded(ashape, 5, "uniform")
+    bv = O.seeded(bshape, 6, "uniform")
+    a = padded(av, ashape, pad, "float64", at)
+    b = padded(bv, bshape, pad, "float64", bt)
+    ref = O.host_matmul_f64(a, b, "float64", threads=O.oracle().orc_host_threads())
+    c = to_device(a, "float64").matmul(to_device(b, "float64"), allow_float64=True)
+    assert np.array_equal(c.to_numpy().reshape(-1), ref.reshape(-1)), name
+    assert P.cuda_get_backend_info()["lastMatmul"] == "builtin-f64"
+
+
+def test_fp32_strict_against_fp64_config1():
+    """BASELINE config 1 on the GPU path: compared to the FP64 twin."""
+    a = O.dense(O.seeded([512, 1024], 0), [512, 1024])
+    b = O.dense(O.seeded([1024, 768], 1), [1024, 768])
+    c64 = O.host_matmul_f64(a, b, "float32", threads=O.oracle().orc_host_threads())
+    c32 = O.host_matmul(a, b, "float32", threads=O.oracle().orc_host_threads())
+    g = to_device(a, "float32").matmul(to_device(b, "float32")).to_numpy().astype(np.float64)
+    assert P.cuda_get_backend_info()["kernel"] == "tc-3xtf32-128x128"
+    assert np.max(np.abs(g - c64)) / max(1.0, np.max(np.abs(c64))) <= 1e-5
+    check_close(g.astype(np.float32), c32, "float32", "config1")
+
+
+def test_tf32_mode_differs_but_stays_close():
+    """tests/matmul_precision.phpt:26-53: TF32 != strict, within 2% of the
+    max magnitude, and strict is bit-identical after switching back."""
+    i = np.arange(65536, dtype=np.float64)
+    left = (np.sin(i * 0.013) + 0.000123).astype(np.float32)
+    right = (np.cos(i * 0.017) - 0.000321).astype(np.float32)
+    a = P.CudaArray.fromFlatArray(left, [256, 256])
+    b = P.CudaArray.fromFlatArray(right, [256, 256])
+    P.set_kernel_path("tensor-core")
+    strict = a.matmul(b).toBuffer()
+    P.cuda_set_matmul_precision("tf32")
+    assert P.cuda_get_backend_info()["precision"] == "tf32"
+    fast = a.matmul(b).toBuffer()
+    assert P.cuda_get_backend_info()["kernel"].startswith("tc-tf32")
+    s = np.frombuffer(strict, np.float32).astype(np.float64)
+    f = np.frombuffer(fast, np.float32).astype(np.float64)
+    diff = np.max(np.abs(s - f))
+    assert diff > 0.0 and diff <= 0.02 * max(1.0, np.max(np.abs(s)))
+    P.cuda_set_matmul_precision("fp32-strict")
+    assert a.matmul(b).toBuffer() == strict
+
+
+def test_autotuning_schema():
+    """tests/matmul_tuning.phpt:18-49 on this library's own configurations."""
+    left, right = P.CudaArray.ones([256, 256]), P.CudaArray.ones([256, 256])
+    t = P.cuda_tune_matmul(left, right)
+    assert t["backend"] == "builtin" and t["precision"] == "fp32-strict"
+    assert t["candidateCount"] > 0 and 0 <= t["selectedCandidate"] < t["candidateCount"]
+    assert sum(c["selected"] for c in t["candidates"]) == 1
+    for c in t["candidates"]:
+        assert c["workspaceBytes"] == 0 and np.isfinite(c["medianMs"]) and c["medianMs"] > 0
+    vals = np.frombuffer(t["product"].toBuffer(), np.float32)
+    assert vals[0] == 256.0 and vals[-1] == 256.0
+    prod = np.frombuffer(left.matmul(right).toBuffer(), np.float32)
+    assert prod[0] == 256.0 and prod[-1] == 256.0
+    assert P.cuda_get_backend_info()["lastMatmul"] == "builtin"
+    with pytest.raises(P.InvalidArgumentException):
+        P.cuda_tune_matmul(P.CudaArray.ones([32, 32]), P.CudaArray.ones([32, 32]))
+    P.cuda_set_matmul_precision("tf32")
+    t = P.cuda_tune_matmul(left, right)
+    assert t["precision"] == "tf32" and t["candidateCount"] == 2
+
+
+# ------------------------------------------------------------------ epilogue
+@pytest.mark.parametrize("dtype", ["float16", "bfloat16", "float32"])
+@pytest.mark.parametrize("act", ["tanh", "relu", "sigmoid", "none"])
+def test_fused_epilogue_matches_unfused_plan(dtype, act):
+    """act(round(A.B) + bias) equals the unfused matmul step followed by the
+    elementwise step computed in float (src/fusion_codegen.c:3-27)."""
+    M, K, N = 300, 264, 328
+    av = O.seeded([M, K], 21, "uniform", -0.5, 0.5)
+    xv = O.seeded([N, K], 22, "uniform", -0.5, 0.5)
+    bias = O.seeded([N], 23, "normal", std=0.1)
+    a = to_device(O.dense(O.to_storage(av, dtype), [M, K]), dtype)
+    x = to_device(O.dense(O.to_storage(xv, dtype), [N, K]), dtype)
+    bdev = to_device(O.dense(O.to_storage(bias, dtype), [N]), dtype)
+    for path in ("tensor-core", "simt"):
+        P.set_kernel_path(path)
+        fused = a.matmul_epilogue(x.transpose(), bdev, act).to_torch().float()
+        plain = a.matmul(x.transpose()).to_torch().float()
+        t = plain + bdev.to_torch().float()
+        t = {"tanh": torch.tanh, "relu": torch.relu, "sigmoid": torch.sigmoid,
+             "none": lambda v: v}[act](t)
+        unfused = t.to(TORCH_DT[dtype]).float()
+        ulp = {"float16": 2.0 ** -10, "bfloat16": 2.0 ** -7, "float32": 2.0 ** -22}[dtype]
+        assert torch.all((fused - unfused).abs() <= ulp * unfused.abs().clamp(min=1.0)), path
+
+
+# ------------------------------------------------------------------ configs
+def test_config2_full_size_integer_exact():
+    """bf16 [64,1024,1024] x [64,1024,1024]: with small-integer inputs every
+    partial sum is exact in float32, so the product must be bit-identical to
+    the exact product rounded once to bfloat16 (what the oracle computes)."""
+    g = torch.Generator().manual_seed(2)
+    a = torch.randint(-3, 4, (64, 1024, 1024), generator=g).to(torch.bfloat16)
+    b = torch.randint(-3, 4, (64, 1024, 1024), generator=g).to(torch.bfloat16)
+    c = P.CudaArray.from_torch(a.cuda()).matmul(P.CudaArray.from_torch(b.cuda()))
+    assert P.cuda_get_backend_info()["kernel"].startswith("tc-bf16")
+    exact = torch.bmm(a.double().cuda(), b.double().cuda()).float().to(torch.bfloat16)
+    assert torch.equal(c.to_torch().view(torch.int16), exact.view(torch.int16))
+    assert P.device_status() == 0
+
+
+def test_config2_random_sampled_rows():
+    """bf16 N(0,1) [64,1024,1024]^2 against the oracle on sampled rows."""
+    M = N = K = 1024
+    batches = 64
+    av = O.seeded([batches, M, K], 0, "normal")
+    bv = O.seeded([batches, K, N], 1, "normal")
+    a = O.dense(O.to_storage(av, "bfloat16"), [batches, M, K])
+    b = O.dense(O.to_storage(bv, "bfloat16"), [batches, K, N])
+    c = to_device(a, "bfloat16").matmul(to_device(b, "bfloat16")).to_numpy().reshape(-1)
+    threads = O.oracle().orc_host_threads()
+    for batch in (0, 17, 63):
+        for row in (0, 511, 1023):
+            first = (batch * M + row) * N
+            ref = O.host_matmul_range(a, b, "bfloat16", first, N, threads)
+            check_close(c[first:first + N], ref, "bfloat16", (batch, row))
+
+
+def test_config3_fp16_transposed_bias_tanh():
+    """fp16 A[8192,4096] . X^T (X [4096,4096] row-major) + bias[4096], tanh:
+    fused epilogue vs the unfused plan over the whole output, and the product
+    vs the oracle on sampled rows."""
+    M, K, N = 8192, 4096, 4096
+    av = O.seeded([M, K], 30, "uniform", -0.5, 0.5)
+    xv = O.seeded([N, K], 31, "uniform", -0.5, 0.5)
+    bias = O.seeded([N], 32, "normal", std=0.1)
+    a_op = O.dense(O.to_storage(av, "float16"), [M, K])
+    x_op = O.dense(O.to_storage(xv, "float16"), [N, K])
+    a, x = to_device(a_op, "float16"), to_device(x_op, "float16")
+    bdev = to_device(O.dense(O.to_storage(bias, "float16"), [N]), "float16")
+    fused = a.matmul_epilogue(x.transpose(), bdev, "tanh")
+    assert P.cuda_get_backend_info()["kernel"].startswith("tc-f16")
+    plain = a.matmul(x.transpose())
+    unfused = torch.tanh(plain.to_torch().float() + bdev.to_torch().float()).half().float()
+    assert torch.all((fused.to_torch().float() - unfused).abs() <= 2.0 ** -10)
+    c = plain.to_numpy().reshape(-1)
+    xt = (x_op[0], [K, N], [1, K], 0)
+    threads = O.oracle().orc_host_threads()
+    for row in (0, 4095, 8191):
+        ref = O.host_matmul_range(a_op, xt, "float16", row * N, N, threads)
+        check_close(c[row * N:(row + 1) * N], ref, "float16", row)
+
+
+def test_config4_mlp_forward_backward_fp32():
+    """float32 MLP 784->1024->1024->10, batch 4096: forward GEMMs and the
+    backward pair dA = dC.B^T, dB = A^T.dC of every layer (transposed views),
+    each against the oracle (sampled rows for the large ones)."""
+    batch, dims = 4096, [784, 1024, 1024, 10]
+    rng_seed = 40
+    x = O.seeded([batch, dims[0]], rng_seed, "uniform", 0.0, 1.0)
+    h = O.dense(x, [batch, dims[0]])
+    threads = O.oracle().orc_host_threads()
+    lib = P.library()
+    for layer in range(3):
+        fan_in, fan_out = dims[layer], dims[layer + 1]
+        w = O.dense(O.seeded([fan_in, fan_out], rng_seed + 1 + layer, "normal",
+                             std=1.0 / np.sqrt(fan_in)), [fan_in, fan_out])
+        dc = O.dense(O.seeded([batch, fan_out], rng_seed + 10 + layer, "normal"),
+                     [batch, fan_out])
+        hd, wd, dcd = to_device(h, "float32"), to_device(w, "float32"), to_device(dc, "float32")
+        out = hd.matmul(wd).to_numpy().reshape(batch, fan_out)
+        for row in (0, batch - 1):
+            ref = O.host_matmul_range(h, w, "float32", row * fan_out, fan_out, threads)
+            check_close(out[row], ref, "float32", ("fwd", layer))
+        ga = P.CudaArray.zeros([batch, fan_in])
+        gb = P.CudaArray.zeros([fan_in, fan_out])
+        import ctypes
+        rc = lib.pt_tensor_matmul_backward(ctypes.byref(hd._pt()), ctypes.byref(wd._pt()),
+                                           ctypes.byref(dcd._pt()), ctypes.byref(ga._pt()),
+                                           ctypes.byref(gb._pt()), P.current_stream())
+        assert rc == P.PT_OK
+        wt = (w[0], [fan_out, fan_in], [1, fan_out], 0)
+        ht = (h[0], [fan_in, batch], [1, fan_in], 0)
+        ga_h = ga.to_numpy().reshape(batch, fan_in)
+        for row in (0, batch - 1):
+            ref = O.host_matmul_range(dc, wt, "float32", row * fan_in, fan_in, threads)
+            check_close(ga_h[row], ref, "float32", ("dA", layer))
+        gb_h = gb.to_numpy().reshape(fan_in, fan_out)
+        for row in (0, fan_in - 1):
+            ref = O.host_matmul_range(ht, dc, "float32", row * fan_out, fan_out, threads)
+            check_close(gb_h[row], ref, "float32", ("dB", layer))
+        h = O.dense(out.reshape(-1).copy(), [batch, fan_out])
+    assert P.device_status() == 0
+
+
+def test_k_zero_and_empty_batch_on_device():
+    a = P.CudaArray.zeros([2, 0])
+    b = P.CudaArray.zeros([0, 3])
+    assert a.matmul(b).toArray() == [[0.0, 0.0, 0.0], [0.0, 0.0, 0.0]]
+    e = P.CudaArray.zeros([0, 2, 3]).matmul(P.CudaArray.ones([3, 2]))
+    assert e.getShape() == [0, 2, 2]
