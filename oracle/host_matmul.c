@@ -365,6 +365,22 @@ int orc_host_matmul_f64(const orc_tensor *a, const orc_tensor *b, double *out,
     return 1;
 }
 
+int orc_host_matmul_f64_range(const orc_tensor *a, const orc_tensor *b, double *out,
+                              size_t first, size_t count, int threads)
+{
+    plan_t p;
+    if (a->dtype != b->dtype ||
+        (a->dtype != ORC_FLOAT64 && !dtype_ok_f32_path(a->dtype)))
+        return 0;
+    if (!make_plan(a, b, &p))
+        return 0;
+    const size_t total = shape_total(p.shape, p.ndims);
+    if (first > total || count > total - first)
+        return 0;
+    run_range(a, b, &p, out, first, first, count, threads, 1);
+    return 1;
+}
+
 int orc_host_threads(void)
 {
     long n = sysconf(_SC_NPROCESSORS_ONLN);

@@ -88,6 +88,10 @@ int orc_host_matmul_f64(const orc_tensor *a, const orc_tensor *b, double *out,
 int orc_host_matmul_range(const orc_tensor *a, const orc_tensor *b, void *out,
                           size_t first, size_t count, int threads);
 
+/* Same sample of the double twin (double output). */
+int orc_host_matmul_f64_range(const orc_tensor *a, const orc_tensor *b, double *out,
+                              size_t first, size_t count, int threads);
+
 /* Online host cores (capped at 256): the thread count the CPU baseline uses. */
 int orc_host_threads(void);
 

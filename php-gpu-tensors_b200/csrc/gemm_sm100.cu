@@ -225,7 +225,7 @@ struct MapDims {
 // and dims of extent 1 get a harmless 16-byte-multiple stride.  Returns false
 // when TMA cannot describe the view.
 bool encode_map(CUtensorMap *map, int dt, const void *base, const MapDims &m,
-                const uint32_t (&box)[5])
+                const uint32_t (&box)[5], CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B)
 {
     if (!g_encode)
         return false;
@@ -254,7 +254,7 @@ bool encode_map(CUtensorMap *map, int dt, const void *base, const MapDims &m,
         strides[i - 1] = s;
     }
     const CUresult r = g_encode(map, tma_type(dt), 5, const_cast<void *>(base), dims, strides, boxd,
-                                estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
                                 CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                                 CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return r == CUDA_SUCCESS;
@@ -489,8 +489,14 @@ int try_tc(const Problem &P, DeviceState *ds, cudaStream_t stream, int *kid_out)
     add_batch_dims(mb, tb, tb.b, p.b_slot);
     add_batch_dims(mc, tb, tb.c, c_slot);
 
+    // TF32 operands stored MN-major need the 32-byte-atom 128-byte swizzle
+    const CUtensorMapSwizzle sw_a = (fp32 && a_mn) ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B
+                                                   : CU_TENSOR_MAP_SWIZZLE_128B;
+    const CUtensorMapSwizzle sw_b = (fp32 && b_mn) ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B
+                                                   : CU_TENSOR_MAP_SWIZZLE_128B;
     CUtensorMap tma_a, tma_b, tma_c;
-    if (!encode_map(&tma_a, P.dt, P.a, ma, box_a) || !encode_map(&tma_b, P.dt, P.b, mb, box_b) ||
+    if (!encode_map(&tma_a, P.dt, P.a, ma, box_a, sw_a) ||
+        !encode_map(&tma_b, P.dt, P.b, mb, box_b, sw_b) ||
         !encode_map(&tma_c, P.dt, P.c, mc, box_c))
         return 0;
 

@@ -128,6 +128,11 @@ struct TcConfig {
     static constexpr int kKSteps = BK / kMmaK;            // 4
     static constexpr int kChunk = 128 / kInBytes;         // MN elements per 128-byte row
     static constexpr int kChunkBytes = 128 * BK;          // one MN-major box (chunk x BK)
+    // MN-major tiles: 16-bit types use 8-row (1024 B) swizzle atoms; TF32 must
+    // use the 32-byte-atom variant whose K groups are 4 rows (512 B).  The TMA
+    // map of such a tile uses the matching CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B.
+    static constexpr uint32_t kMnLayout = kTf32 ? kLayoutSw128Base32B : kLayoutSw128;
+    static constexpr uint32_t kMnSbo = kTf32 ? 512 : 1024;
     static constexpr int kATile = BM * BK * kInBytes;     // 16 KB
     static constexpr int kBTile = BN * BK * kInBytes;     // 16 or 32 KB
     static constexpr int kLoadBytes = kATile + kBTile;    // bytes TMA lands per stage
@@ -140,7 +145,16 @@ struct TcConfig {
     static constexpr int kEpiWarps = 4;
     static constexpr int kSplitWarps = kSplit3 ? 4 : 0;
     static constexpr int kThreads = 32 * (2 + kEpiWarps + kSplitWarps);
-    static constexpr int kTmemCols = 2 * BN;              // two accumulators
+    // Accumulator columns per tile: 3xTF32 keeps the small cross terms
+    // (hi*lo + lo*hi) in a second accumulator so that the FP32 accumulator of
+    // the dominant hi*hi term sees a third of the per-instruction roundings.
+    static constexpr int kAccCols = (kSplit3 ? 2 : 1) * BN;
+    // 3xTF32: k-blocks accumulated in TMEM before the epilogue drains the
+    // slot into float registers (bounds the accumulator's per-instruction
+    // rounding to 3 * kChunkKB * kKSteps steps per chunk).  Other kinds keep
+    // one slot for the whole tile.
+    static constexpr int kChunkKB = kSplit3 ? 4 : (1 << 30);
+    static constexpr int kTmemCols = 2 * kAccCols;        // double-buffered
     static constexpr int kRingBytes = kStages * kStageBytes;
     static constexpr int kEpiOffset = kRingBytes;
     static constexpr int kBarOffset = kEpiOffset + kEpiWarps * 2 * kEpiBufBytes;
@@ -150,6 +164,7 @@ struct TcConfig {
     static_assert(kStages >= 2, "pipeline needs at least two stages");
     static_assert(BN % kEpiCols == 0, "epilogue box must divide BN");
     static_assert(kSmemBytes <= 232448, "shared memory budget exceeded");
+    static_assert(kTmemCols <= 512, "TMEM holds 512 columns");
 };
 
 __device__ __forceinline__ void decode_batch(long long b, const TcParams &p, int (&c)[3])
@@ -289,22 +304,31 @@ __global__ void __launch_bounds__(TcConfig<IN_KIND, BN, OUT>::kThreads, 1)
         }
     } else if (warp == 1) {
         // ------------------------------------------------------------ MMA issuer
+        // An accumulator slot covers a whole tile, except for 3xTF32 where it
+        // covers kChunkKB k-blocks and the epilogue drains it into registers.
         if (lane == 0) {
             int stage = 0;
             uint32_t phase = 0;
-            long long iter = 0;
+            long long iter = 0;   // accumulator slot uses
+            int acc = 0;
+            uint32_t d_tmem = 0, d_small = 0;
             bool ok = true;
             const uint32_t smem_base = smem_addr(smem);
-            for (long long t = blockIdx.x; ok && t < p.tiles; t += gridDim.x, iter++) {
-                const int acc = static_cast<int>(iter & 1);
-                const uint32_t acc_phase = static_cast<uint32_t>((iter >> 1) & 1);
-                if (!mbar_wait(&tempty[acc], acc_phase ^ 1, abort)) {
-                    record_failure(abort, p.status, DEV_TIMEOUT_MMA);
-                    break;
-                }
-                tc_fence_after();
-                const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
+            for (long long t = blockIdx.x; ok && t < p.tiles; t += gridDim.x) {
                 for (int kb = 0; kb < p.k_blocks; kb++) {
+                    const int kc = kb % Cfg::kChunkKB;
+                    if (kc == 0) {
+                        acc = static_cast<int>(iter & 1);
+                        const uint32_t acc_phase = static_cast<uint32_t>((iter >> 1) & 1);
+                        if (!mbar_wait(&tempty[acc], acc_phase ^ 1, abort)) {
+                            record_failure(abort, p.status, DEV_TIMEOUT_MMA);
+                            ok = false;
+                            break;
+                        }
+                        tc_fence_after();
+                        d_tmem = tmem_base + static_cast<uint32_t>(acc * Cfg::kAccCols);
+                        d_small = d_tmem + BN;   // 3xTF32 cross terms
+                    }
                     uint64_t *gate = Cfg::kSplit3 ? &ready[stage] : &full[stage];
                     if (!mbar_wait(gate, phase, abort)) {
                         record_failure(abort, p.status, DEV_TIMEOUT_MMA);
@@ -316,22 +340,28 @@ __global__ void __launch_bounds__(TcConfig<IN_KIND, BN, OUT>::kThreads, 1)
                     const uint32_t sb = sa + Cfg::kATile;
 #pragma unroll
                     for (int k = 0; k < Cfg::kKSteps; k++) {
-                        const uint32_t a_off = p.a_mn_major ? k * (Cfg::kMmaK / 8) * 1024 : k * 32;
-                        const uint32_t b_off = p.b_mn_major ? k * (Cfg::kMmaK / 8) * 1024 : k * 32;
+                        // one MMA consumes 32 bytes of K: a 32-byte column step
+                        // in a K-major tile, kMmaK 128-byte rows in an MN-major one
+                        const uint32_t a_off = p.a_mn_major ? k * Cfg::kMmaK * 128 : k * 32;
+                        const uint32_t b_off = p.b_mn_major ? k * Cfg::kMmaK * 128 : k * 32;
                         const uint32_t a_lbo = p.a_mn_major ? Cfg::kChunkBytes : 16;
                         const uint32_t b_lbo = p.b_mn_major ? Cfg::kChunkBytes : 16;
-                        const uint64_t ad = smem_desc_sw128(sa + a_off, a_lbo, 1024);
-                        const uint64_t bd = smem_desc_sw128(sb + b_off, b_lbo, 1024);
-                        const uint32_t accumulate = (kb | k) != 0;
+                        const uint32_t a_sbo = p.a_mn_major ? Cfg::kMnSbo : 1024;
+                        const uint32_t b_sbo = p.b_mn_major ? Cfg::kMnSbo : 1024;
+                        const uint32_t a_lay = p.a_mn_major ? Cfg::kMnLayout : kLayoutSw128;
+                        const uint32_t b_lay = p.b_mn_major ? Cfg::kMnLayout : kLayoutSw128;
+                        const uint64_t ad = smem_desc(sa + a_off, a_lbo, a_sbo, a_lay);
+                        const uint64_t bd = smem_desc(sb + b_off, b_lbo, b_sbo, b_lay);
+                        const uint32_t accumulate = (kc | k) != 0;
                         if constexpr (Cfg::kTf32) {
                             umma_tf32(d_tmem, ad, bd, p.idesc, accumulate);
                             if constexpr (Cfg::kSplit3) {
                                 const uint64_t ad_lo =
-                                    smem_desc_sw128(sa + Cfg::kLoadBytes + a_off, a_lbo, 1024);
+                                    smem_desc(sa + Cfg::kLoadBytes + a_off, a_lbo, a_sbo, a_lay);
                                 const uint64_t bd_lo =
-                                    smem_desc_sw128(sb + Cfg::kLoadBytes + b_off, b_lbo, 1024);
-                                umma_tf32(d_tmem, ad, bd_lo, p.idesc, 1);
-                                umma_tf32(d_tmem, ad_lo, bd, p.idesc, 1);
+                                    smem_desc(sb + Cfg::kLoadBytes + b_off, b_lbo, b_sbo, b_lay);
+                                umma_tf32(d_small, ad, bd_lo, p.idesc, accumulate);
+                                umma_tf32(d_small, ad_lo, bd, p.idesc, 1);
                             }
                         } else {
                             umma_f16(d_tmem, ad, bd, p.idesc, accumulate);
@@ -342,10 +372,11 @@ __global__ void __launch_bounds__(TcConfig<IN_KIND, BN, OUT>::kThreads, 1)
                         stage = 0;
                         phase ^= 1;
                     }
+                    if (kc == Cfg::kChunkKB - 1 || kb == p.k_blocks - 1) {
+                        umma_commit(&tfull[acc]);
+                        iter++;
+                    }
                 }
-                if (!ok)
-                    break;
-                umma_commit(&tfull[acc]);
             }
             // Wait until every MMA this thread issued has completed, so TMEM
             // and the shared-memory ring can be released safely.
@@ -359,18 +390,58 @@ __global__ void __launch_bounds__(TcConfig<IN_KIND, BN, OUT>::kThreads, 1)
         const int quad = warp & 3;               // TMEM lane quadrant this warp may access
         uint8_t *stage_buf = smem + Cfg::kEpiOffset + ew * 2 * Cfg::kEpiBufBytes;
         int buf = 0;
-        long long iter = 0;
-        for (long long t = blockIdx.x; t < p.tiles; t += gridDim.x, iter++) {
-            const int acc = static_cast<int>(iter & 1);
-            const uint32_t acc_phase = static_cast<uint32_t>((iter >> 1) & 1);
-            // the whole warp must agree before the .sync.aligned TMEM loads
-            const bool got = __all_sync(0xffffffffu, mbar_wait(&tfull[acc], acc_phase, abort));
-            if (!got) {
-                if (lane == 0)
-                    record_failure(abort, p.status, DEV_TIMEOUT_EPILOGUE);
-                break;
+        long long iter = 0;   // accumulator slot uses
+        bool ok = true;
+
+        // Bias/activation, conversion, swizzled staging and the TMA store of
+        // one 32-row x 128-byte box of this warp's rows.
+        auto emit = [&](float (&v)[Cfg::kEpiCols], int col0, int row0, const int (&c)[3]) {
+            if (p.bias != nullptr || p.act != ACT_NONE) {
+                // Same arithmetic as the unfused plan: the matmul result is
+                // rounded to the output dtype, then bias add and activation
+                // run in float and round once.
+#pragma unroll
+                for (int i = 0; i < Cfg::kEpiCols; i++) {
+                    float x = OutTraits<OUT>::round_trip(v[i]);
+                    const int col = col0 + i;
+                    if (p.bias != nullptr && col < p.N)
+                        x += OutTraits<OUT>::load(p.bias, col);
+                    v[i] = apply_activation(x, p.act);
+                }
             }
-            tc_fence_after();
+            uint8_t *sbuf = stage_buf + buf * Cfg::kEpiBufBytes;
+            if (lane == 0)
+                bulk_wait_group_read<1>();   // the store that last used sbuf has read it
+            __syncwarp();
+            uint8_t *row = sbuf + lane * 128;
+#pragma unroll
+            for (int j = 0; j < 8; j++) {
+                uint4 q;
+                if constexpr (OUT == OUT_F32) {
+                    q.x = __float_as_uint(v[4 * j + 0]);
+                    q.y = __float_as_uint(v[4 * j + 1]);
+                    q.z = __float_as_uint(v[4 * j + 2]);
+                    q.w = __float_as_uint(v[4 * j + 3]);
+                } else {
+                    q.x = pack2(v[8 * j + 0], v[8 * j + 1], OUT);
+                    q.y = pack2(v[8 * j + 2], v[8 * j + 3], OUT);
+                    q.z = pack2(v[8 * j + 4], v[8 * j + 5], OUT);
+                    q.w = pack2(v[8 * j + 6], v[8 * j + 7], OUT);
+                }
+                // 128-byte swizzle: 16-byte chunk j of row r lives at j ^ (r % 8)
+                *reinterpret_cast<uint4 *>(row + ((j ^ (lane & 7)) << 4)) = q;
+            }
+            fence_proxy_async_smem();
+            __syncwarp();
+            // boxes entirely past N or M hold nothing to write
+            if (lane == 0 && col0 < p.N && row0 < p.M) {
+                tma_store_5d(&tma_c, sbuf, col0, row0, c[0], c[1], c[2]);
+                bulk_commit_group();
+            }
+            buf ^= 1;
+        };
+
+        for (long long t = blockIdx.x; ok && t < p.tiles; t += gridDim.x) {
             const int nb = static_cast<int>(t % p.n_blocks);
             const long long r = t / p.n_blocks;
             const int mb = static_cast<int>(r % p.m_blocks);
@@ -378,73 +449,91 @@ __global__ void __launch_bounds__(TcConfig<IN_KIND, BN, OUT>::kThreads, 1)
             int c[3];
             decode_batch(batch, p, c);
             const int m0 = mb * Cfg::BM, n0 = nb * BN;
-            const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) +
-                                   static_cast<uint32_t>(acc * BN);
-#pragma unroll 1
-            for (int ch = 0; ch < Cfg::kEpiChunks; ch++) {
-                float v[Cfg::kEpiCols];
-                {
+            const int row0 = m0 + quad * 32;
+            const uint32_t lane_base = tmem_base + (static_cast<uint32_t>(quad * 32) << 16);
+            if constexpr (Cfg::kSplit3) {
+                // drain every K chunk into round-to-nearest float registers
+                float accv[BN];
+#pragma unroll
+                for (int i = 0; i < BN; i++)
+                    accv[i] = 0.0f;
+                const int nchunks = (p.k_blocks + Cfg::kChunkKB - 1) / Cfg::kChunkKB;
+                for (int ck = 0; ck < nchunks; ck++, iter++) {
+                    const int acc = static_cast<int>(iter & 1);
+                    const uint32_t acc_phase = static_cast<uint32_t>((iter >> 1) & 1);
+                    const bool got =
+                        __all_sync(0xffffffffu, mbar_wait(&tfull[acc], acc_phase, abort));
+                    if (!got) {
+                        if (lane == 0)
+                            record_failure(abort, p.status, DEV_TIMEOUT_EPILOGUE);
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t t_acc = lane_base + static_cast<uint32_t>(acc * Cfg::kAccCols);
                     uint32_t r32[32];
 #pragma unroll
-                    for (int h = 0; h < Cfg::kEpiCols / 32; h++) {
-                        tmem_ld_32x32b_x32(t_row + ch * Cfg::kEpiCols + h * 32, r32);
+                    for (int h = 0; h < BN / 32; h++) {
+                        tmem_ld_32x32b_x32(t_acc + h * 32, r32);
                         tmem_ld_wait();
 #pragma unroll
                         for (int i = 0; i < 32; i++)
-                            v[h * 32 + i] = __uint_as_float(r32[i]);
+                            accv[h * 32 + i] += __uint_as_float(r32[i]);
+                        tmem_ld_32x32b_x32(t_acc + BN + h * 32, r32);
+                        tmem_ld_wait();
+#pragma unroll
+                        for (int i = 0; i < 32; i++)
+                            accv[h * 32 + i] += __uint_as_float(r32[i]);
                     }
-                }
-                if (ch == Cfg::kEpiChunks - 1) {
-                    // accumulator fully read: hand it back to the MMA warp
                     tc_fence_before();
                     __syncwarp();
                     if (lane == 0)
                         mbar_arrive(&tempty[acc]);
                 }
-                const int col0 = n0 + ch * Cfg::kEpiCols;
-                if (p.bias != nullptr || p.act != ACT_NONE) {
-                    // Same arithmetic as the unfused plan: the matmul result is
-                    // rounded to the output dtype, then bias add and activation
-                    // run in float and round once.
+                if (!ok)
+                    break;
 #pragma unroll
-                    for (int i = 0; i < Cfg::kEpiCols; i++) {
-                        float x = OutTraits<OUT>::round_trip(v[i]);
-                        const int col = col0 + i;
-                        if (p.bias != nullptr && col < p.N)
-                            x += OutTraits<OUT>::load(p.bias, col);
-                        v[i] = apply_activation(x, p.act);
-                    }
-                }
-                uint8_t *sbuf = stage_buf + buf * Cfg::kEpiBufBytes;
-                if (lane == 0)
-                    bulk_wait_group_read<1>();   // the store that last used sbuf has read it
-                __syncwarp();
-                uint8_t *row = sbuf + lane * 128;
+                for (int ch = 0; ch < Cfg::kEpiChunks; ch++) {
+                    float v[Cfg::kEpiCols];
 #pragma unroll
-                for (int j = 0; j < 8; j++) {
-                    uint4 q;
-                    if constexpr (OUT == OUT_F32) {
-                        q.x = __float_as_uint(v[4 * j + 0]);
-                        q.y = __float_as_uint(v[4 * j + 1]);
-                        q.z = __float_as_uint(v[4 * j + 2]);
-                        q.w = __float_as_uint(v[4 * j + 3]);
-                    } else {
-                        q.x = pack2(v[8 * j + 0], v[8 * j + 1], OUT);
-                        q.y = pack2(v[8 * j + 2], v[8 * j + 3], OUT);
-                        q.z = pack2(v[8 * j + 4], v[8 * j + 5], OUT);
-                        q.w = pack2(v[8 * j + 6], v[8 * j + 7], OUT);
+                    for (int i = 0; i < Cfg::kEpiCols; i++)
+                        v[i] = accv[ch * Cfg::kEpiCols + i];
+                    emit(v, n0 + ch * Cfg::kEpiCols, row0, c);
+                }
+            } else {
+                const int acc = static_cast<int>(iter & 1);
+                const uint32_t acc_phase = static_cast<uint32_t>((iter >> 1) & 1);
+                iter++;
+                // the whole warp must agree before the .sync.aligned TMEM loads
+                const bool got = __all_sync(0xffffffffu, mbar_wait(&tfull[acc], acc_phase, abort));
+                if (!got) {
+                    if (lane == 0)
+                        record_failure(abort, p.status, DEV_TIMEOUT_EPILOGUE);
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t t_acc = lane_base + static_cast<uint32_t>(acc * Cfg::kAccCols);
+#pragma unroll 1
+                for (int ch = 0; ch < Cfg::kEpiChunks; ch++) {
+                    float v[Cfg::kEpiCols];
+                    uint32_t r32[32];
+#pragma unroll
+                    for (int h = 0; h < Cfg::kEpiCols / 32; h++) {
+                        tmem_ld_32x32b_x32(t_acc + ch * Cfg::kEpiCols + h * 32, r32);
+                        tmem_ld_wait();
+#pragma unroll
+                        for (int i = 0; i < 32; i++)
+                            v[h * 32 + i] = __uint_as_float(r32[i]);
                     }
-                    // 128-byte swizzle: 16-byte chunk j of row r lives at j ^ (r % 8)
-                    *reinterpret_cast<uint4 *>(row + ((j ^ (lane & 7)) << 4)) = q;
+                    if (ch == Cfg::kEpiChunks - 1) {
+                        // accumulator fully read: hand it back to the MMA warp
+                        tc_fence_before();
+                        __syncwarp();
+                        if (lane == 0)
+                            mbar_arrive(&tempty[acc]);
+                    }
+                    emit(v, n0 + ch * Cfg::kEpiCols, row0, c);
                 }
-                fence_proxy_async_smem();
-                __syncwarp();
-                // boxes entirely past N or M hold nothing to write
-                if (lane == 0 && col0 < p.N && m0 + quad * 32 < p.M) {
-                    tma_store_5d(&tma_c, sbuf, col0, m0 + quad * 32, c[0], c[1], c[2]);
-                    bulk_commit_group();
-                }
-                buf ^= 1;
             }
         }
         if (lane == 0)

@@ -223,18 +223,23 @@ __device__ __forceinline__ void tmem_ld_wait()
 
 // ---------------------------------------------------------------- descriptors
 // Shared-memory matrix descriptor (tcgen05 "matrix descriptor"): start address,
-// leading and stride byte offsets (16-byte units), version 1 (sm_100), and the
-// 128-byte swizzle layout (encoding 2).  Tiles are 1024-byte aligned, so the
-// base offset field stays 0.
-__device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t saddr, uint32_t lbo_bytes,
-                                                    uint32_t sbo_bytes)
+// leading and stride byte offsets (16-byte units), version 1 (sm_100) and the
+// layout type: 2 = 128-byte swizzle with 16-byte atoms (K-major tiles and
+// MN-major 16-bit tiles), 1 = 128-byte swizzle with 32-byte atoms (the only
+// layout tcgen05 accepts for MN-major 32-bit / TF32 tiles).  Tiles are
+// 1024-byte aligned, so the base offset field stays 0.
+constexpr uint32_t kLayoutSw128 = 2;
+constexpr uint32_t kLayoutSw128Base32B = 1;
+
+__device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t lbo_bytes,
+                                              uint32_t sbo_bytes, uint32_t layout)
 {
     uint64_t d = 0;
     d |= static_cast<uint64_t>((saddr >> 4) & 0x3fffu);
     d |= static_cast<uint64_t>((lbo_bytes >> 4) & 0x3fffu) << 16;
     d |= static_cast<uint64_t>((sbo_bytes >> 4) & 0x3fffu) << 32;
     d |= 1ull << 46;
-    d |= 2ull << 61;
+    d |= static_cast<uint64_t>(layout) << 61;
     return d;
 }
 

@@ -61,6 +61,8 @@ def oracle():
                                             P(ctypes.c_int), P(ctypes.c_int), ctypes.c_int]
         lib.orc_host_matmul_range.argtypes = [P(OrcTensor), P(OrcTensor), ctypes.c_void_p,
                                               ctypes.c_size_t, ctypes.c_size_t, ctypes.c_int]
+        lib.orc_host_matmul_f64_range.argtypes = [P(OrcTensor), P(OrcTensor), ctypes.c_void_p,
+                                                  ctypes.c_size_t, ctypes.c_size_t, ctypes.c_int]
         lib.orc_host_threads.restype = ctypes.c_int
         _ORC = lib
     return _ORC
@@ -199,6 +201,26 @@ def host_matmul_range(a, b, dtype, first, count, threads):
                                           first, count, threads):
         raise ValueError("range outside the product")
     return out
+
+
+def host_matmul_f64_range(a, b, dtype, first, count, threads):
+    ta = _tensor(*a, dtype)
+    tb = _tensor(*b, dtype)
+    out = np.zeros(count, dtype=np.float64)
+    if not oracle().orc_host_matmul_f64_range(ctypes.byref(ta), ctypes.byref(tb),
+                                              out.ctypes.data, first, count, threads):
+        raise ValueError("range outside the product")
+    return out
+
+
+def absolute(op, dtype):
+    """The operand with every element replaced by its magnitude."""
+    storage, shape, strides, offset = op
+    if dtype in ("float16", "bfloat16"):
+        s = storage & np.uint16(0x7fff)
+    else:
+        s = np.abs(storage)
+    return (s, shape, strides, offset)
 
 
 def dense(storage, shape):
