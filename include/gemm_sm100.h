@@ -208,8 +208,10 @@ int cuda_matmul_epilogue_nd_launcher(
 const char *gemm_sm100_last_kernel(void);
 
 /* Selects the kernel family for this thread's later launches and returns the
- * previous setting: 0 = automatic, 1 = tensor-core kernel whenever the layout
- * allows it (ignoring the size heuristic), 2 = CUDA-core kernel only. */
+ * previous setting: 0 = automatic, 1 = single-CTA tensor-core kernel whenever
+ * the layout allows it (ignoring the size heuristic), 2 = CUDA-core kernel
+ * only, 3 = 2-CTA tensor-core kernel for float16/bfloat16 whenever the layout
+ * allows it (other dtypes as 1). */
 int gemm_sm100_set_path(int path);
 
 /* Reads (and with clear != 0 resets) the device status word of `device`:

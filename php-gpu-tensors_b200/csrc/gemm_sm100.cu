@@ -17,6 +17,7 @@
 
 #include "gemm_simt.cuh"
 #include "gemm_tc.cuh"
+#include "gemm_tc2.cuh"
 
 #include <cudaTypedefs.h>
 
@@ -83,6 +84,7 @@ struct DeviceState {
     int cc_major, cc_minor;
     int *status;                   // this device's copy of g_device_status
     unsigned long long attr_mask;  // kernels whose shared-memory limit has been raised
+    int pair_clusters[4];          // co-resident 2-CTA clusters per pair kernel (0 = unknown)
 };
 std::mutex g_mutex;
 DeviceState g_devices[kMaxDevices];
@@ -324,7 +326,7 @@ void add_batch_dims(MapDims &m, const TcBatch &tb, const long long (&bs)[3], int
     }
 }
 
-uint32_t make_idesc(int fmt, int a_mn, int b_mn, int bn)
+uint32_t make_idesc(int fmt, int a_mn, int b_mn, int bn, int bm = 128)
 {
     return (1u << 4)                                       // D: f32
            | (static_cast<uint32_t>(fmt) << 7)             // A format
@@ -332,7 +334,7 @@ uint32_t make_idesc(int fmt, int a_mn, int b_mn, int bn)
            | (static_cast<uint32_t>(a_mn) << 15)           // A MN-major
            | (static_cast<uint32_t>(b_mn) << 16)           // B MN-major
            | (static_cast<uint32_t>(bn >> 3) << 17)        // N / 8
-           | (static_cast<uint32_t>(128 >> 4) << 24);      // M / 16
+           | (static_cast<uint32_t>(bm >> 4) << 24);       // M / 16
 }
 
 enum KernelId : int {
@@ -343,6 +345,8 @@ enum KernelId : int {
     KID_TF32_128,
     KID_TF32_256,
     KID_F32X3_128,
+    KID_BF16_PAIR,
+    KID_F16_PAIR,
 };
 
 const char *kernel_name(int kid)
@@ -355,6 +359,8 @@ const char *kernel_name(int kid)
     case KID_TF32_128: return "tc-tf32-128x128";
     case KID_TF32_256: return "tc-tf32-128x256";
     case KID_F32X3_128: return "tc-3xtf32-128x128";
+    case KID_BF16_PAIR: return "tc2-bf16-256x256";
+    case KID_F16_PAIR: return "tc2-f16-256x256";
     default: return "tc-unknown";
     }
 }
@@ -382,6 +388,49 @@ cudaError_t launch_tc_kernel(DeviceState *ds, int kid, const CUtensorMap &ma,
     p.status = ds->status;
     const long long grid = std::min<long long>(p.tiles, ds->sms);
     kernel<<<static_cast<unsigned>(grid), Cfg::kThreads, Cfg::kSmemBytes, stream>>>(ma, mb, mc, p);
+    return cudaGetLastError();
+}
+
+// Cluster launch of the 2-CTA kernel: at most as many clusters as can be
+// co-resident (one CTA per SM), two CTAs each.
+template <int IN, int OUT>
+cudaError_t launch_tc2_kernel(DeviceState *ds, int kid, int slot, const CUtensorMap &ma,
+                              const CUtensorMap &mb, const CUtensorMap &mc, TcParams &p,
+                              cudaStream_t stream)
+{
+    using Cfg = Tc2Config<IN, OUT>;
+    auto kernel = tc2_gemm_kernel<IN, OUT>;
+    if (!ensure_smem_attr(ds, kid, kernel, Cfg::kSmemBytes))
+        return cudaErrorInvalidConfiguration;
+    cudaLaunchAttribute attr;
+    attr.id = cudaLaunchAttributeClusterDimension;
+    attr.val.clusterDim.x = 2;
+    attr.val.clusterDim.y = 1;
+    attr.val.clusterDim.z = 1;
+    cudaLaunchConfig_t cfg = {};
+    cfg.blockDim = dim3(Cfg::kThreads);
+    cfg.dynamicSmemBytes = Cfg::kSmemBytes;
+    cfg.stream = stream;
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
+    int clusters = 0;
+    {
+        std::lock_guard<std::mutex> lock(g_mutex);
+        clusters = ds->pair_clusters[slot];
+    }
+    if (clusters == 0) {
+        cfg.gridDim = dim3(static_cast<unsigned>(ds->sms & ~1));
+        if (cudaOccupancyMaxActiveClusters(&clusters, kernel, &cfg) != cudaSuccess || clusters < 1)
+            clusters = ds->sms / 2;
+        std::lock_guard<std::mutex> lock(g_mutex);
+        ds->pair_clusters[slot] = clusters;
+    }
+    p.status = ds->status;
+    const long long n = std::min<long long>(p.tiles, clusters);
+    cfg.gridDim = dim3(static_cast<unsigned>(2 * n));
+    const cudaError_t err = cudaLaunchKernelEx(&cfg, kernel, ma, mb, mc, p);
+    if (err != cudaSuccess)
+        return err;
     return cudaGetLastError();
 }
 
@@ -443,13 +492,22 @@ int try_tc(const Problem &P, DeviceState *ds, cudaStream_t stream, int *kid_out)
             bn = (P.N <= 128 || tiles256 < ds->sms / 2) ? 128 : 256;
         }
     }
+    // 16-bit products with enough 256x256 tiles to fill the co-resident
+    // clusters run on the 2-CTA kernel (or whenever path 3 asks for it).
+    bool pair = false;
+    if (!fp32 && P.forced_bn == 0) {
+        const long long tiles_pair = P.batches * ((P.M + 255) / 256) * ((P.N + 255) / 256);
+        pair = t_path == 3 || (t_path != 1 && tiles_pair >= ds->sms / 2);
+    }
+    if (pair)
+        bn = 256;
     if (fp32)
         kid = t_precision == CUDA_MATMUL_PRECISION_FP32_STRICT ? KID_F32X3_128
                                                                 : (bn == 256 ? KID_TF32_256 : KID_TF32_128);
     else if (P.dt == DT_BF16)
-        kid = bn == 256 ? KID_BF16_256 : KID_BF16_128;
+        kid = pair ? KID_BF16_PAIR : (bn == 256 ? KID_BF16_256 : KID_BF16_128);
     else
-        kid = bn == 256 ? KID_F16_256 : KID_F16_128;
+        kid = pair ? KID_F16_PAIR : (bn == 256 ? KID_F16_256 : KID_F16_128);
 
     const int bk = 128 / es;            // K elements per stage
     const int chunk = 128 / es;         // MN elements per 128-byte row
@@ -477,7 +535,7 @@ int try_tc(const Problem &P, DeviceState *ds, cudaStream_t stream, int *kid_out)
     } else {
         mb.ext[0] = P.K; mb.stride[0] = 1;
         mb.ext[1] = P.N; mb.stride[1] = P.b_sn;
-        box_b[0] = bk; box_b[1] = bn;
+        box_b[0] = bk; box_b[1] = pair ? bn / 2 : bn;   // each CTA of a pair loads half of N
     }
     mb.rank = 2;
     mc.ext[0] = P.N; mc.stride[0] = 1;
@@ -503,7 +561,7 @@ int try_tc(const Problem &P, DeviceState *ds, cudaStream_t stream, int *kid_out)
     p.M = P.M;
     p.N = P.N;
     p.K = P.K;
-    p.m_blocks = static_cast<int>(m_blocks);
+    p.m_blocks = static_cast<int>(pair ? (P.M + 255) / 256 : m_blocks);
     p.n_blocks = (P.N + bn - 1) / bn;
     p.k_blocks = (P.K + bk - 1) / bk;
     p.tiles = P.batches * p.m_blocks * p.n_blocks;
@@ -513,7 +571,7 @@ int try_tc(const Problem &P, DeviceState *ds, cudaStream_t stream, int *kid_out)
     p.a_mn_major = a_mn;
     p.b_mn_major = b_mn;
     const int fmt = fp32 ? 2 : (P.dt == DT_BF16 ? 1 : 0);
-    p.idesc = make_idesc(fmt, a_mn, b_mn, bn);
+    p.idesc = make_idesc(fmt, a_mn, b_mn, bn, pair ? 256 : 128);
     p.bias = P.bias;
     p.act = P.act;
 
@@ -525,6 +583,8 @@ int try_tc(const Problem &P, DeviceState *ds, cudaStream_t stream, int *kid_out)
     case KID_F16_256: err = launch_tc_kernel<IN_F16, 256, OUT_F16>(ds, kid, tma_a, tma_b, tma_c, p, stream); break;
     case KID_TF32_128: err = launch_tc_kernel<IN_TF32, 128, OUT_F32>(ds, kid, tma_a, tma_b, tma_c, p, stream); break;
     case KID_TF32_256: err = launch_tc_kernel<IN_TF32, 256, OUT_F32>(ds, kid, tma_a, tma_b, tma_c, p, stream); break;
+    case KID_BF16_PAIR: err = launch_tc2_kernel<IN_BF16, OUT_BF16>(ds, kid, 0, tma_a, tma_b, tma_c, p, stream); break;
+    case KID_F16_PAIR: err = launch_tc2_kernel<IN_F16, OUT_F16>(ds, kid, 1, tma_a, tma_b, tma_c, p, stream); break;
     default: err = launch_tc_kernel<IN_F32X3, 128, OUT_F32>(ds, kid, tma_a, tma_b, tma_c, p, stream); break;
     }
     if (err != cudaSuccess) {
@@ -870,7 +930,7 @@ PT_API const char *gemm_sm100_last_kernel(void) { return t_last_kernel; }
 PT_API int gemm_sm100_set_path(int path)
 {
     const int prev = t_path;
-    if (path >= 0 && path <= 2)
+    if (path >= 0 && path <= 3)
         t_path = path;
     return prev;
 }

@@ -416,8 +416,10 @@ def cuda_tune_matmul(left, right):
 
 
 def set_kernel_path(path):
-    """0 automatic, 1 tensor-core kernel whenever the layout allows, 2 CUDA cores only."""
-    return library().gemm_sm100_set_path({"auto": 0, "tensor-core": 1, "simt": 2}[path])
+    """0 automatic, 1 single-CTA tensor-core kernel whenever the layout allows,
+    2 CUDA cores only, 3 2-CTA tensor-core kernel (16-bit) whenever allowed."""
+    return library().gemm_sm100_set_path(
+        {"auto": 0, "tensor-core": 1, "simt": 2, "tensor-core-pair": 3}[path])
 
 
 def device_status(device=0, clear=True):

@@ -89,7 +89,7 @@ def check_fp32(gpu, a, b, what, first=None, count=None):
 
 
 # ------------------------------------------------------------------ golden
-@pytest.mark.parametrize("path", ["auto", "tensor-core", "simt"])
+@pytest.mark.parametrize("path", ["auto", "tensor-core", "tensor-core-pair", "simt"])
 def test_golden_vectors(golden, path):
     P.set_kernel_path(path)
     for case in golden["cases"]:
@@ -180,7 +180,7 @@ CASES = [
 
 
 @pytest.mark.parametrize("dtype", ["bfloat16", "float16", "float32"])
-@pytest.mark.parametrize("path", ["auto", "tensor-core"])
+@pytest.mark.parametrize("path", ["auto", "tensor-core", "tensor-core-pair"])
 @pytest.mark.parametrize("case", CASES, ids=[c[0] for c in CASES])
 def test_seeded_parity(case, path, dtype):
     name, ashape, bshape, at, bt, pad = case
@@ -192,6 +192,8 @@ def test_seeded_parity(case, path, dtype):
     b = padded(bv, bshape, pad, dtype, bt)
     c = to_device(a, dtype).matmul(to_device(b, dtype))
     what = (name, path, P.cuda_get_backend_info()["kernel"])
+    if path == "tensor-core-pair" and dtype != "float32" and what[2].startswith("tc"):
+        assert what[2].startswith("tc2-"), what
     if dtype == "float32":
         check_fp32(c.to_numpy(), a, b, what)
     else:
@@ -299,10 +301,12 @@ def test_config2_full_size_integer_exact():
     g = torch.Generator().manual_seed(2)
     a = torch.randint(-3, 4, (64, 1024, 1024), generator=g).to(torch.bfloat16)
     b = torch.randint(-3, 4, (64, 1024, 1024), generator=g).to(torch.bfloat16)
-    c = P.CudaArray.from_torch(a.cuda()).matmul(P.CudaArray.from_torch(b.cuda()))
-    assert P.cuda_get_backend_info()["kernel"].startswith("tc-bf16")
     exact = torch.bmm(a.double().cuda(), b.double().cuda()).float().to(torch.bfloat16)
-    assert torch.equal(c.to_torch().view(torch.int16), exact.view(torch.int16))
+    for path, prefix in (("auto", "tc"), ("tensor-core", "tc-bf16"), ("tensor-core-pair", "tc2-bf16")):
+        P.set_kernel_path(path)
+        c = P.CudaArray.from_torch(a.cuda()).matmul(P.CudaArray.from_torch(b.cuda()))
+        assert P.cuda_get_backend_info()["kernel"].startswith(prefix), path
+        assert torch.equal(c.to_torch().view(torch.int16), exact.view(torch.int16)), path
     assert P.device_status() == 0
 
 
@@ -336,7 +340,7 @@ def test_config3_fp16_transposed_bias_tanh():
     a, x = to_device(a_op, "float16"), to_device(x_op, "float16")
     bdev = to_device(O.dense(O.to_storage(bias, "float16"), [N]), "float16")
     fused = a.matmul_epilogue(x.transpose(), bdev, "tanh")
-    assert P.cuda_get_backend_info()["kernel"].startswith("tc-f16")
+    assert P.cuda_get_backend_info()["kernel"].startswith(("tc-f16", "tc2-f16"))
     plain = a.matmul(x.transpose())
     unfused = torch.tanh(plain.to_torch().float() + bdev.to_torch().float()).half().float()
     assert torch.all((fused.to_torch().float() - unfused).abs() <= 2.0 ** -10)
