@@ -1,0 +1,198 @@
+// FP64 batched GEMM on the DMMA pipe (mma.sync.m16n8k4 .f64).
+//
+// New scope: the reference rejects float64 matmul.  Block tile 128 x 128 x 16,
+// 8 warps in a 2 x 4 grid, each warp owning 64 x 32 outputs as 4 x 4 m16n8
+// fragments (64 fp64 accumulators per thread).  Operand tiles move through a
+// 3-stage cp.async ring into row-major shared tiles whose row pitches
+// (20 doubles for A, 132 for B) make every fragment read of a half-warp hit
+// distinct banks.  A K-contiguous A and an N-contiguous B with 16-byte aligned
+// rows use 16-byte cp.async copies with zero fill at the edges; any other
+// layout goes through the same ring with element loads.
+#pragma once
+
+#include "gemm_simt.cuh"
+
+namespace ptg {
+
+constexpr int kF64BM = 128, kF64BN = 128, kF64BK = 16;
+constexpr int kF64Stages = 3;
+constexpr int kF64PitchA = kF64BK + 4;    // doubles per A row in shared memory
+constexpr int kF64PitchB = kF64BN + 4;    // doubles per B row
+constexpr int kF64StageA = kF64BM * kF64PitchA;
+constexpr int kF64StageB = kF64BK * kF64PitchB;
+constexpr int kF64SmemBytes = kF64Stages * (kF64StageA + kF64StageB) * 8;
+
+__device__ __forceinline__ void cp_async16(void *dst, const void *src, bool valid)
+{
+    const uint32_t d = smem_addr(dst);
+    const int n = valid ? 16 : 0;   // 0 source bytes: the 16 destination bytes are zero-filled
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(d), "l"(src), "r"(n)
+                 : "memory");
+}
+
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+__device__ __forceinline__ void dmma_16x8x4(double (&d)[4], const double (&a)[2], double b)
+{
+    asm volatile(
+        "mma.sync.aligned.m16n8k4.row.col.f64.f64.f64.f64"
+        " {%0, %1, %2, %3}, {%4, %5}, {%6}, {%0, %1, %2, %3};"
+        : "+d"(d[0]), "+d"(d[1]), "+d"(d[2]), "+d"(d[3])
+        : "d"(a[0]), "d"(a[1]), "d"(b));
+}
+
+// Fills one ring stage with the A tile [m0, m0+128) x [k0, k0+16) and the B
+// tile [k0, k0+16) x [n0, n0+128).
+__device__ __forceinline__ void f64_load_stage(const SimtParams &p, double *sa, double *sb,
+                                               long long oa, long long ob, int m0, int n0, int k0,
+                                               bool a_vec, bool b_vec)
+{
+    const double *A = static_cast<const double *>(p.a);
+    const double *B = static_cast<const double *>(p.b);
+    const int tid = threadIdx.x;
+    if (a_vec) {
+        // 128 rows x 8 pairs of k
+#pragma unroll
+        for (int r = 0; r < 4; r++) {
+            const int e = tid + 256 * r;
+            const int row = e >> 3, kp = (e & 7) * 2;
+            const int m = m0 + row, k = k0 + kp;
+            const bool ok = m < p.M && k < p.K;   // K even: a pair is all in or all out
+            const double *src = ok ? A + oa + static_cast<long long>(m) * p.a_sm + k : A;
+            cp_async16(sa + row * kF64PitchA + kp, src, ok);
+        }
+    } else {
+#pragma unroll
+        for (int r = 0; r < 8; r++) {
+            const int e = tid + 256 * r;
+            const int row = e >> 4, kk = e & 15;
+            const int m = m0 + row, k = k0 + kk;
+            sa[row * kF64PitchA + kk] =
+                (m < p.M && k < p.K) ? A[oa + static_cast<long long>(m) * p.a_sm +
+                                         static_cast<long long>(k) * p.a_sk]
+                                     : 0.0;
+        }
+    }
+    if (b_vec) {
+        // 16 k rows x 64 pairs of n
+#pragma unroll
+        for (int r = 0; r < 4; r++) {
+            const int e = tid + 256 * r;
+            const int kr = e >> 6, np = (e & 63) * 2;
+            const int k = k0 + kr, n = n0 + np;
+            const bool ok = k < p.K && n < p.N;   // N even: a pair is all in or all out
+            const double *src = ok ? B + ob + static_cast<long long>(k) * p.b_sk + n : B;
+            cp_async16(sb + kr * kF64PitchB + np, src, ok);
+        }
+    } else {
+#pragma unroll
+        for (int r = 0; r < 8; r++) {
+            const int e = tid + 256 * r;
+            const int kr = e >> 7, col = e & 127;
+            const int k = k0 + kr, n = n0 + col;
+            sb[kr * kF64PitchB + col] =
+                (k < p.K && n < p.N) ? B[ob + static_cast<long long>(k) * p.b_sk +
+                                         static_cast<long long>(n) * p.b_sn]
+                                     : 0.0;
+        }
+    }
+}
+
+__global__ void __launch_bounds__(256, 1) f64_dmma_kernel(const SimtParams p, int a_vec, int b_vec)
+{
+    extern __shared__ __align__(16) double f64_smem[];
+    double *sa_all = f64_smem;
+    double *sb_all = f64_smem + kF64Stages * kF64StageA;
+
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int g = lane >> 2, t = lane & 3;
+    const int wm = (warp >> 2) * 64, wn = (warp & 3) * 32;
+    const int n0 = blockIdx.x * kF64BN;
+    const int m_blocks = (p.M + kF64BM - 1) / kF64BM;
+    const int k_blocks = (p.K + kF64BK - 1) / kF64BK;
+
+    for (long long batch = blockIdx.z; batch < p.batches; batch += gridDim.z)
+    for (int mb = blockIdx.y; mb < m_blocks; mb += gridDim.y) {
+        const int m0 = mb * kF64BM;
+        long long oa = 0, ob = 0, oc = 0, rem = batch;
+        for (int d = p.nbd - 1; d >= 0; d--) {
+            const long long coord = rem % p.bshape[d];
+            rem /= p.bshape[d];
+            oa += coord * p.a_bs[d];
+            ob += coord * p.b_bs[d];
+            oc += coord * p.c_bs[d];
+        }
+        double acc[4][4][4];
+#pragma unroll
+        for (int i = 0; i < 4; i++)
+#pragma unroll
+            for (int j = 0; j < 4; j++)
+#pragma unroll
+                for (int r = 0; r < 4; r++)
+                    acc[i][j][r] = 0.0;
+
+        __syncthreads();   // the previous tile's readers are done with the ring
+#pragma unroll
+        for (int s = 0; s < kF64Stages - 1; s++) {
+            if (s < k_blocks)
+                f64_load_stage(p, sa_all + s * kF64StageA, sb_all + s * kF64StageB, oa, ob, m0,
+                               n0, s * kF64BK, a_vec, b_vec);
+            cp_async_commit();
+        }
+        for (int kb = 0; kb < k_blocks; kb++) {
+            cp_async_wait<kF64Stages - 2>();
+            __syncthreads();
+            const int nxt = kb + kF64Stages - 1;
+            if (nxt < k_blocks)
+                f64_load_stage(p, sa_all + (nxt % kF64Stages) * kF64StageA,
+                               sb_all + (nxt % kF64Stages) * kF64StageB, oa, ob, m0, n0,
+                               nxt * kF64BK, a_vec, b_vec);
+            cp_async_commit();
+            const double *sa = sa_all + (kb % kF64Stages) * kF64StageA;
+            const double *sb = sb_all + (kb % kF64Stages) * kF64StageB;
+#pragma unroll
+            for (int kk = 0; kk < kF64BK; kk += 4) {
+                double af[4][2], bf[4];
+#pragma unroll
+                for (int i = 0; i < 4; i++) {
+                    af[i][0] = sa[(wm + i * 16 + g) * kF64PitchA + kk + t];
+                    af[i][1] = sa[(wm + i * 16 + g + 8) * kF64PitchA + kk + t];
+                }
+#pragma unroll
+                for (int j = 0; j < 4; j++)
+                    bf[j] = sb[(kk + t) * kF64PitchB + wn + j * 8 + g];
+#pragma unroll
+                for (int i = 0; i < 4; i++)
+#pragma unroll
+                    for (int j = 0; j < 4; j++)
+                        dmma_16x8x4(acc[i][j], af[i], bf[j]);
+            }
+        }
+        cp_async_wait<0>();
+
+        double *C = static_cast<double *>(p.c);
+        const double *bias = static_cast<const double *>(p.bias);
+#pragma unroll
+        for (int i = 0; i < 4; i++)
+#pragma unroll
+            for (int j = 0; j < 4; j++)
+#pragma unroll
+                for (int r = 0; r < 4; r++) {
+                    const int m = m0 + wm + i * 16 + g + (r >> 1) * 8;
+                    const int n = n0 + wn + j * 8 + t * 2 + (r & 1);
+                    if (m < p.M && n < p.N) {
+                        double v = acc[i][j][r];
+                        if (bias != nullptr || p.act != ACT_NONE) {
+                            if (bias != nullptr) v += bias[n];
+                            v = apply_activation_d(v, p.act);
+                        }
+                        C[oc + static_cast<long long>(m) * p.c_sm + static_cast<long long>(n) * p.c_sn] = v;
+                    }
+                }
+    }
+}
+
+} // namespace ptg

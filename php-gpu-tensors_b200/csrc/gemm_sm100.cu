@@ -15,6 +15,7 @@
 // Launches are asynchronous on the caller's stream and allocate nothing.
 #include "gemm_sm100.h"
 
+#include "gemm_f64.cuh"
 #include "gemm_simt.cuh"
 #include "gemm_tc.cuh"
 #include "gemm_tc2.cuh"
@@ -347,6 +348,7 @@ enum KernelId : int {
     KID_F32X3_128,
     KID_BF16_PAIR,
     KID_F16_PAIR,
+    KID_F64_DMMA,
 };
 
 const char *kernel_name(int kid)
@@ -361,6 +363,7 @@ const char *kernel_name(int kid)
     case KID_F32X3_128: return "tc-3xtf32-128x128";
     case KID_BF16_PAIR: return "tc2-bf16-256x256";
     case KID_F16_PAIR: return "tc2-f16-256x256";
+    case KID_F64_DMMA: return "dmma-f64-128x128";
     default: return "tc-unknown";
     }
 }
@@ -595,8 +598,33 @@ int try_tc(const Problem &P, DeviceState *ds, cudaStream_t stream, int *kid_out)
     return 1;
 }
 
-template <typename T>
-cudaError_t launch_simt(const Problem &P, cudaStream_t stream)
+SimtParams simt_params(const Problem &P);
+
+bool aligned16(const void *p) { return reinterpret_cast<uintptr_t>(p) % 16 == 0; }
+
+// FP64 on the DMMA pipe.  16-byte cp.async copies need a contiguous inner
+// axis, an even extent along it, and even (16-byte) strides everywhere else.
+cudaError_t launch_f64_dmma(const Problem &P, DeviceState *ds, cudaStream_t stream)
+{
+    const SimtParams s = simt_params(P);
+    bool a_vec = P.a_sk == 1 && P.K % 2 == 0 && (P.a_sm % 2 == 0 || P.M == 1) && aligned16(P.a);
+    bool b_vec = P.b_sn == 1 && P.N % 2 == 0 && (P.b_sk % 2 == 0 || P.K == 1) && aligned16(P.b);
+    for (int d = 0; d < P.nbd; d++) {
+        a_vec = a_vec && P.a_bs[d] % 2 == 0;
+        b_vec = b_vec && P.b_bs[d] % 2 == 0;
+    }
+    if (!ensure_smem_attr(ds, KID_F64_DMMA, f64_dmma_kernel, kF64SmemBytes))
+        return cudaErrorInvalidConfiguration;
+    const long long mb = (P.M + kF64BM - 1) / kF64BM;
+    const long long nb = (P.N + kF64BN - 1) / kF64BN;
+    dim3 grid(static_cast<unsigned>(std::min<long long>(nb, 2147483647ll)),
+              static_cast<unsigned>(std::min<long long>(mb, 65535)),
+              static_cast<unsigned>(std::min<long long>(P.batches, 65535)));
+    f64_dmma_kernel<<<grid, 256, kF64SmemBytes, stream>>>(s, a_vec ? 1 : 0, b_vec ? 1 : 0);
+    return cudaGetLastError();
+}
+
+SimtParams simt_params(const Problem &P)
 {
     SimtParams s;
     std::memset(&s, 0, sizeof(s));
@@ -622,6 +650,13 @@ cudaError_t launch_simt(const Problem &P, cudaStream_t stream)
     s.c_sn = P.c_sn;
     s.bias = P.bias;
     s.act = P.act;
+    return s;
+}
+
+template <typename T>
+cudaError_t launch_simt(const Problem &P, cudaStream_t stream)
+{
+    const SimtParams s = simt_params(P);
     const long long mb = (P.M + kSimtTile - 1) / kSimtTile;
     const long long nb = (P.N + kSimtTile - 1) / kSimtTile;
     dim3 grid(static_cast<unsigned>(std::min<long long>(nb, 2147483647ll)),
@@ -661,7 +696,19 @@ int run(Problem &P, cudaStream_t stream)
         return 0;
     }
     const double work = static_cast<double>(P.M) * P.N * P.K * static_cast<double>(P.batches);
-    const bool want_tc = P.K > 0 && t_path != 2 && (t_path == 1 || work >= kTcMinWork);
+    const bool want_tc = P.K > 0 && t_path != 2 && (t_path == 1 || t_path == 3 || work >= kTcMinWork);
+    if (want_tc && P.dt == DT_F64 && ds->cc_major == 10) {
+        const cudaError_t err = launch_f64_dmma(P, ds, stream);
+        if (err != cudaSuccess) {
+            set_status(static_cast<int>(err));
+            return 0;
+        }
+        t_info.builtin_matmul_calls++;
+        t_info.last_matmul = family_name(P.dt);
+        t_info.last_blas_status = 0;
+        t_last_kernel = kernel_name(KID_F64_DMMA);
+        return 1;
+    }
     if (want_tc) {
         int kid = -1;
         const int r = try_tc(P, ds, stream, &kid);

@@ -202,8 +202,10 @@ def test_seeded_parity(case, path, dtype):
 
 
 @pytest.mark.parametrize("case", CASES, ids=[c[0] for c in CASES])
-def test_float64_bit_exact(case):
+def test_float64_cuda_cores_bit_exact(case):
+    """The CUDA-core kernel runs the oracle's fma sequence: identical bits."""
     name, ashape, bshape, at, bt, pad = case
+    P.set_kernel_path("simt")
     av = O.seeded(ashape, 5, "uniform")
     bv = O.seeded(bshape, 6, "uniform")
     a = padded(av, ashape, pad, "float64", at)
@@ -212,6 +214,53 @@ def test_float64_bit_exact(case):
     c = to_device(a, "float64").matmul(to_device(b, "float64"), allow_float64=True)
     assert np.array_equal(c.to_numpy().reshape(-1), ref.reshape(-1)), name
     assert P.cuda_get_backend_info()["lastMatmul"] == "builtin-f64"
+    assert P.cuda_get_backend_info()["kernel"] == "simt-f64"
+
+
+def check_fp64(gpu, a, b, what, first=None, count=None):
+    """float64 acceptance: normwise rel-err <= 1e-12 against the double twin of
+    the oracle loop (BASELINE), and per element within 2*K*2^-53*(|A|.|B|)_ij,
+    twice the classical float64 dot-product bound (both sides round)."""
+    K = a[1][-1]
+    th = O.oracle().orc_host_threads()
+    aa, ab = O.absolute(a, "float64"), O.absolute(b, "float64")
+    if first is None:
+        ref = O.host_matmul_f64(a, b, "float64", th).reshape(-1)
+        absp = O.host_matmul_f64(aa, ab, "float64", th).reshape(-1)
+    else:
+        ref = O.host_matmul_f64_range(a, b, "float64", first, count, th)
+        absp = O.host_matmul_f64_range(aa, ab, "float64", first, count, th)
+    g = np.asarray(gpu, dtype=np.float64).reshape(-1)
+    assert np.all(np.abs(g - ref) <= 2 * K * 2.0 ** -53 * absp + 1e-300), what
+    if ref.size:
+        assert np.max(np.abs(g - ref)) / max(1.0, np.max(np.abs(ref))) <= TOL_NORM["float64"], what
+
+
+@pytest.mark.parametrize("case", CASES, ids=[c[0] for c in CASES])
+def test_float64_dmma(case):
+    name, ashape, bshape, at, bt, pad = case
+    P.set_kernel_path("tensor-core")
+    av = O.seeded(ashape, 7, "uniform")
+    bv = O.seeded(bshape, 8, "uniform")
+    a = padded(av, ashape, pad, "float64", at)
+    b = padded(bv, bshape, pad, "float64", bt)
+    c = to_device(a, "float64").matmul(to_device(b, "float64"), allow_float64=True)
+    assert P.cuda_get_backend_info()["kernel"] == "dmma-f64-128x128"
+    check_fp64(c.to_numpy(), a, b, name)
+
+
+def test_config5b_fp64_full_size_sampled():
+    """float64 [8192,8192] x [8192,8192], U[-1,1): the single-GPU product (each
+    rank's N-split column block is a slice of it) on sampled rows."""
+    n = 8192
+    a = O.dense(O.seeded([n, n], 50, "uniform").astype(np.float64), [n, n])
+    b = O.dense(O.seeded([n, n], 51, "uniform").astype(np.float64), [n, n])
+    c = to_device(a, "float64").matmul(to_device(b, "float64"), allow_float64=True)
+    assert P.cuda_get_backend_info()["kernel"] == "dmma-f64-128x128"
+    out = c.to_numpy().reshape(-1)
+    for row in (0, 4097, n - 1):
+        check_fp64(out[row * n:(row + 1) * n], a, b, row, row * n, n)
+    assert P.device_status() == 0
 
 
 def test_fp32_strict_against_fp64_config1():
