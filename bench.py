@@ -1,7 +1,7 @@
 """Batched GEMM throughput of libgemm_sm100.so on B200 (driver contract).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload config2|config5a]
+                    [--workload config2|config5a|config5b]
 
 One step = one batched product of the workload, one launch of the
 library's kernel:
@@ -12,6 +12,10 @@ library's kernel:
            collective, scaling is weak.
   config5a BASELINE config 5a: bf16 [512,2048,2048]^2 split along the batch
            axis over the N ranks (strong scaling, 512/N batches per rank).
+  config5b BASELINE config 5b: float64 [8192,8192]^2 split along N over the
+           ranks; every step ends with the NCCL all-gather of the column
+           blocks and the permute into the row-major result on every rank
+           (strong scaling).
 value     whole-job TFLOP/s (2*M*N*K*batches over all ranks / max-over-ranks
           device time), inputs resident in HBM; inputs (>= 384 MB per step)
           exceed the 126 MB L2, so no flush is needed between steps.
@@ -40,6 +44,8 @@ sys.path.insert(0, PKG)
 WORKLOADS = {
     "config2": {"batches": 64, "M": 1024, "N": 1024, "K": 1024, "split": False},
     "config5a": {"batches": 512, "M": 2048, "N": 2048, "K": 2048, "split": True},
+    "config5b": {"batches": 1, "M": 8192, "N": 8192, "K": 8192, "split": True, "nsplit": True,
+                 "dtype": "float64"},
 }
 METRIC = "batched GEMM TFLOP/s (bf16/fp32/fp64) at 1/2/4/8 B200, % of dense TC peak"
 FALLBACK_PEAK_TFLOPS = 1590.0
@@ -65,8 +71,23 @@ def dist_env():
 
 
 def shard(w, rank, world):
-    b = w["batches"] // world if w["split"] else w["batches"]
-    return b
+    """Batches this rank computes: the batch axis is partitioned for the
+    strong-scaling workloads, replicated per rank for config2 (weak)."""
+    if not w["split"] or w.get("nsplit"):
+        return w["batches"]
+    base, extra = divmod(w["batches"], world)
+    return base + (1 if rank < extra else 0)
+
+
+def max_over_ranks(x, world, device=None):
+    """Max of a host float over all ranks (the bench's timing rule)."""
+    if world == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
 
 
 def peaks():
@@ -198,6 +219,81 @@ def run_reference(args, w):
 
 
 # ------------------------------------------------------------------ GPU side
+def run_nsplit(args, w):
+    """config5b: float64 N-split product + all-gather + permute per step."""
+    import torch
+    import phptensors as P
+
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    lib = P.library()
+    M, N, K = w["M"], w["N"], w["K"]
+    lo, hi = P.nsplit_columns(N, rank, world)
+    gen = torch.Generator(device="cuda").manual_seed(77)
+    a = torch.rand(M, K, device="cuda", generator=gen, dtype=torch.float64) * 2 - 1
+    b = torch.rand(K, N, device="cuda", generator=gen, dtype=torch.float64) * 2 - 1
+    b_local = b[:, lo:hi].contiguous()
+    del b
+    comm = P.MgpuComm(rank, world)
+    A = P.CudaArray.from_torch(a)
+    Bl = P.CudaArray.from_torch(b_local)
+    ws = torch.empty(M * N * 8, dtype=torch.uint8, device="cuda")
+    stream = torch.cuda.current_stream()
+
+    def barrier():
+        if world > 1:
+            import torch.distributed as dist
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    for _ in range(args.warmup):
+        C = P.nsplit_matmul(comm, A, Bl, N, ws)
+    kernel = P.cuda_get_backend_info()["kernel"]
+    barrier()
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    sampler = ClockSampler(local)
+    with sampler:
+        barrier()
+        start.record(stream)
+        for _ in range(args.steps):
+            C = P.nsplit_matmul(comm, A, Bl, N, ws)
+        stop.record(stream)
+        torch.cuda.synchronize()
+    ms_local = start.elapsed_time(stop)
+    barrier()
+    ms = max_over_ranks(ms_local, world, "cuda")
+    if lib.gemm_sm100_device_status(local, 1) != 0:
+        raise RuntimeError("device status after the timed region")
+    flop = 2.0 * M * N * K
+    value = flop * args.steps / (ms / 1e3) / 1e12
+    if rank == 0:
+        peak, peak_src = peaks()
+        line = {
+            "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "f64", "data": "synthetic U[-1,1) on device",
+            "config": {"workload": "config5b", "M": M, "N": N, "K": K,
+                       "parallelism": "N-split x%d + NCCL all-gather + permute" % world,
+                       "kernel": kernel,
+                       "allgather_bytes_received_per_rank": M * (N - (hi - lo)) * 8},
+            "cpu_baseline": None, "e2e": None,
+            "gpu_launches": args.steps * 2,
+            "clocks": sampler.summary(),
+        }
+        print(json.dumps(line), flush=True)
+    comm.close()
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def run_ours(args, w):
     import torch
     import phptensors as P
@@ -237,13 +333,6 @@ def run_ours(args, w):
             dist.barrier()
         torch.cuda.synchronize()
 
-    def max_over_ranks(x):
-        if world == 1:
-            return x
-        import torch.distributed as dist
-        t = torch.tensor([x], device="cuda", dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
 
     for _ in range(args.warmup):
         step()
@@ -260,7 +349,7 @@ def run_ours(args, w):
         torch.cuda.synchronize()
     ms_local = start.elapsed_time(stop)
     barrier()
-    ms = max_over_ranks(ms_local)
+    ms = max_over_ranks(ms_local, world, "cuda")
     status = lib.gemm_sm100_device_status(local, 1)
     if status != 0:
         raise RuntimeError("device status %d after the timed region" % status)
@@ -294,7 +383,7 @@ def run_ours(args, w):
         e2e_step()
     stop.record(stream)
     torch.cuda.synchronize()
-    e2e_ms = max_over_ranks(start.elapsed_time(stop))
+    e2e_ms = max_over_ranks(start.elapsed_time(stop), world, "cuda")
     e2e_value = flop_rank * world * e2e_steps / (e2e_ms / 1e3) / 1e12
 
     cpu = None
@@ -341,6 +430,8 @@ def main():
     w = WORKLOADS[args.workload]
     if args.impl == "reference":
         run_reference(args, w)
+    elif w.get("nsplit"):
+        run_nsplit(args, w)
     else:
         run_ours(args, w)
 

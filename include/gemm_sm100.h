@@ -226,6 +226,42 @@ const char *gemm_sm100_algorithm_name(int algorithm_id);
 /* Library version, major * 10000 + minor * 100 + patch. */
 int gemm_sm100_version(void);
 
+/* ------------------------------------------------------------------ */
+/* Multi-GPU, one process per GPU (new scope: the reference is        */
+/* single-GPU).  Batched products shard along the batch axis with no  */
+/* collective; a single large product splits along N and all-gathers  */
+/* the column blocks with NCCL over NVLink.                           */
+/* ------------------------------------------------------------------ */
+typedef struct gemm_mgpu_comm gemm_mgpu_comm;
+#define GEMM_MGPU_UNIQUE_ID_BYTES 128
+
+/* Rank 0 creates the communicator id (128 bytes) and hands it to the other
+ * ranks by any host channel.  Returns 1, or 0 when NCCL cannot be loaded. */
+int gemm_mgpu_unique_id(unsigned char *id);
+
+/* Joins the communicator on the CURRENT device.  Collective over all ranks. */
+int gemm_mgpu_comm_init(const unsigned char *id, int nranks, int rank, gemm_mgpu_comm **comm);
+
+void gemm_mgpu_comm_destroy(gemm_mgpu_comm *comm);
+
+/* Gather-buffer bytes gemm_mgpu_nsplit_matmul needs (M * N elements), or 0
+ * when N is not a multiple of nranks. */
+size_t gemm_mgpu_nsplit_workspace_bytes(int nranks, dtype_t dtype, int M, int N);
+
+/* C[M, N] = A[M, K] . B[K, N] split along N over the communicator's ranks:
+ * every rank passes all of A and its column block b_local = B[:, r*N/G,
+ * (r+1)*N/G) (both strided 2-D views, element strides), and receives the
+ * whole row-major contiguous C.  Enqueued on `stream`: the rank's block is
+ * computed into slot r of `workspace`, the slots are all-gathered in place
+ * (ncclAllGather), and a permute kernel writes C.  dtype FLOAT64, FLOAT32,
+ * FLOAT16 or BFLOAT16; N % nranks == 0.  Returns 1 / 0 (last_blas_status has
+ * the CUDA error or GEMM_SM100_STATUS_NCCL). */
+int gemm_mgpu_nsplit_matmul(gemm_mgpu_comm *comm, dtype_t dtype,
+                            const void *a, size_t a_s0, size_t a_s1,
+                            const void *b_local, size_t b_s0, size_t b_s1,
+                            void *c, int M, int N, int K,
+                            void *workspace, size_t workspace_bytes, cudaStream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

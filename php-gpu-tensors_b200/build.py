@@ -3,8 +3,9 @@
     python php-gpu-tensors_b200/build.py            # library + oracle
     python php-gpu-tensors_b200/build.py --force    # rebuild everything
 
-The library is the CUDA translation unit csrc/gemm_sm100.cu (kernels and the
-launcher ABI) plus the C++ host layer host/tensor_matmul.cpp, compiled by
+The library is the CUDA translation units csrc/gemm_sm100.cu (kernels and the
+launcher ABI) and csrc/mgpu.cu (multi-GPU entry points, NCCL loaded at run
+time) plus the C++ host layer host/tensor_matmul.cpp, compiled by
 nvcc for compute_100a/sm_100a only, linked with the static CUDA runtime and an export
 map so that only the C ABI of include/gemm_sm100.h is visible.  nvcc
 cross-compiles without a GPU.  The oracle (test infrastructure) is built by
@@ -22,7 +23,8 @@ CSRC = os.path.join(PKG, "csrc")
 INCLUDE = os.path.join(ROOT, "include")
 LIB = os.path.join(PKG, "libgemm_sm100.so")
 HOST = os.path.join(PKG, "host")
-SOURCES = [os.path.join(CSRC, "gemm_sm100.cu"), os.path.join(HOST, "tensor_matmul.cpp")]
+SOURCES = [os.path.join(CSRC, "gemm_sm100.cu"), os.path.join(CSRC, "mgpu.cu"),
+           os.path.join(HOST, "tensor_matmul.cpp")]
 EXPORTS = os.path.join(CSRC, "exports.map")
 
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
@@ -61,7 +63,7 @@ def build_library(force=False, verbose=False):
         "-shared", "-I", INCLUDE, "-I", CSRC,
         "-Xlinker", "--version-script=" + EXPORTS,
         "-o", tmp,
-    ] + SOURCES
+    ] + SOURCES + ["-ldl"]
     if verbose:
         print(" ".join(cmd), flush=True)
     subprocess.run(cmd, check=True)

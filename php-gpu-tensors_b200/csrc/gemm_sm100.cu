@@ -769,6 +769,9 @@ int nd_entry(int dt, const void *a, const void *b, void *c, int *shape_a, size_t
 
 } // namespace
 
+// Internal (hidden) hook for the other translation units of the library.
+void ptg_set_last_status(int code) { set_status(code); }
+
 // ============================================================ C ABI
 
 PT_API void cuda_blas_shutdown(void)

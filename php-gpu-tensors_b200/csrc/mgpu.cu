@@ -1,0 +1,230 @@
+// Multi-GPU entry points of libgemm_sm100.so (one process per GPU).
+//
+// The reference has no multi-GPU code; this is new scope.  A single large
+// product is split along N: rank r holds all of A and the column block
+// B[:, r*N/G, (r+1)*N/G) and computes C[:, block] with the ordinary launchers
+// into slot r of a [G][M][N/G] gather buffer; an in-place NCCL all-gather over
+// NVLink fills every slot on every rank, and an HBM-bound permute kernel lays
+// the slots out as the row-major [M, N] result.  Batched products need no
+// collective at all: ranks take disjoint batch ranges.
+//
+// NCCL is loaded at run time (the copy the process already mapped, e.g. the
+// one PyTorch ships, else libnccl.so.2 from the loader path), so the library
+// has no link-time NCCL dependency and single-GPU users never load it.
+#include "gemm_sm100.h"
+
+#include <nccl.h>
+
+#include <dlfcn.h>
+
+#include <cstdint>
+#include <cstring>
+#include <mutex>
+
+#define PT_API extern "C" __attribute__((visibility("default")))
+
+// Set by the multi-GPU entry points on failure (defined in gemm_sm100.cu).
+void ptg_set_last_status(int code);
+
+namespace {
+
+struct NcclApi {
+    bool loaded = false;
+    void *handle = nullptr;
+    ncclResult_t (*get_unique_id)(ncclUniqueId *) = nullptr;
+    ncclResult_t (*comm_init_rank)(ncclComm_t *, int, ncclUniqueId, int) = nullptr;
+    ncclResult_t (*comm_destroy)(ncclComm_t) = nullptr;
+    ncclResult_t (*all_gather)(const void *, void *, size_t, ncclDataType_t, ncclComm_t,
+                               cudaStream_t) = nullptr;
+};
+
+NcclApi g_nccl;
+std::mutex g_nccl_mutex;
+
+bool nccl()
+{
+    std::lock_guard<std::mutex> lock(g_nccl_mutex);
+    if (g_nccl.loaded)
+        return g_nccl.handle != nullptr;
+    g_nccl.loaded = true;
+    void *h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_NOLOAD);
+    if (!h)
+        h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_LOCAL);
+    if (!h)
+        return false;
+    g_nccl.get_unique_id = reinterpret_cast<decltype(g_nccl.get_unique_id)>(dlsym(h, "ncclGetUniqueId"));
+    g_nccl.comm_init_rank = reinterpret_cast<decltype(g_nccl.comm_init_rank)>(dlsym(h, "ncclCommInitRank"));
+    g_nccl.comm_destroy = reinterpret_cast<decltype(g_nccl.comm_destroy)>(dlsym(h, "ncclCommDestroy"));
+    g_nccl.all_gather = reinterpret_cast<decltype(g_nccl.all_gather)>(dlsym(h, "ncclAllGather"));
+    if (!g_nccl.get_unique_id || !g_nccl.comm_init_rank || !g_nccl.comm_destroy ||
+        !g_nccl.all_gather) {
+        dlclose(h);
+        return false;
+    }
+    g_nccl.handle = h;
+    return true;
+}
+
+size_t element_bytes(dtype_t dt)
+{
+    switch (dt) {
+    case DTYPE_FLOAT64: return 8;
+    case DTYPE_FLOAT32: return 4;
+    case DTYPE_FLOAT16:
+    case DTYPE_BFLOAT16: return 2;
+    default: return 0;
+    }
+}
+
+// out[m][r * nb + j] = ws[r][m][j], in 16-byte units (vec) or elements.
+template <typename T>
+__global__ void nsplit_permute_kernel(const T *__restrict__ ws, T *__restrict__ out, int ranks,
+                                      long long rows, long long nb)
+{
+    const long long total = static_cast<long long>(ranks) * rows * nb;
+    for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
+         i += static_cast<long long>(gridDim.x) * blockDim.x) {
+        const long long j = i % nb;
+        const long long m = (i / nb) % rows;
+        const long long r = i / (nb * rows);
+        out[m * (nb * ranks) + r * nb + j] = ws[i];
+    }
+}
+
+} // namespace
+
+struct gemm_mgpu_comm {
+    ncclComm_t nccl;
+    int nranks;
+    int rank;
+    int device;
+};
+
+PT_API int gemm_mgpu_unique_id(unsigned char *id)
+{
+    if (!id || !nccl()) {
+        ptg_set_last_status(GEMM_SM100_STATUS_NCCL);
+        return 0;
+    }
+    ncclUniqueId uid;
+    if (g_nccl.get_unique_id(&uid) != ncclSuccess) {
+        ptg_set_last_status(GEMM_SM100_STATUS_NCCL);
+        return 0;
+    }
+    std::memcpy(id, uid.internal, GEMM_MGPU_UNIQUE_ID_BYTES);
+    return 1;
+}
+
+PT_API int gemm_mgpu_comm_init(const unsigned char *id, int nranks, int rank,
+                               gemm_mgpu_comm **comm)
+{
+    if (!id || !comm || nranks < 1 || rank < 0 || rank >= nranks || !nccl()) {
+        ptg_set_last_status(GEMM_SM100_STATUS_NCCL);
+        return 0;
+    }
+    int device = -1;
+    if (cudaGetDevice(&device) != cudaSuccess) {
+        ptg_set_last_status(GEMM_SM100_STATUS_NO_DEVICE);
+        return 0;
+    }
+    ncclUniqueId uid;
+    std::memcpy(uid.internal, id, GEMM_MGPU_UNIQUE_ID_BYTES);
+    ncclComm_t c = nullptr;
+    if (g_nccl.comm_init_rank(&c, nranks, uid, rank) != ncclSuccess) {
+        ptg_set_last_status(GEMM_SM100_STATUS_NCCL);
+        return 0;
+    }
+    *comm = new gemm_mgpu_comm{c, nranks, rank, device};
+    return 1;
+}
+
+PT_API void gemm_mgpu_comm_destroy(gemm_mgpu_comm *comm)
+{
+    if (!comm)
+        return;
+    if (comm->nccl && nccl())
+        g_nccl.comm_destroy(comm->nccl);
+    delete comm;
+}
+
+PT_API size_t gemm_mgpu_nsplit_workspace_bytes(int nranks, dtype_t dtype, int M, int N)
+{
+    if (nranks < 1 || M < 0 || N < 0 || N % nranks != 0)
+        return 0;
+    return static_cast<size_t>(M) * static_cast<size_t>(N) * element_bytes(dtype);
+}
+
+PT_API int gemm_mgpu_nsplit_matmul(gemm_mgpu_comm *comm, dtype_t dtype, const void *a,
+                                   size_t a_s0, size_t a_s1, const void *b_local, size_t b_s0,
+                                   size_t b_s1, void *c, int M, int N, int K, void *workspace,
+                                   size_t workspace_bytes, cudaStream_t stream)
+{
+    const size_t es = element_bytes(dtype);
+    if (!comm || es == 0 || M < 0 || N < 0 || K < 0 || N % comm->nranks != 0)
+        return 0;
+    if (M == 0 || N == 0)
+        return 1;
+    const int G = comm->nranks;
+    const int nb = N / G;
+    const size_t slot = static_cast<size_t>(M) * nb;
+    if (!workspace || !c || workspace_bytes < slot * G * es)
+        return 0;
+    // 1. this rank's column block into its slot of the gather buffer
+    void *mine = static_cast<char *>(workspace) + slot * comm->rank * es;
+    int sa[2] = {M, K}, sb[2] = {K, nb}, sc[2] = {M, nb};
+    size_t ta[2] = {a_s0, a_s1}, tb[2] = {b_s0, b_s1}, tc[2] = {static_cast<size_t>(nb), 1};
+    int ok;
+    if (dtype == DTYPE_FLOAT64)
+        ok = cuda_f64_matmul_nd_launcher(static_cast<double *>(const_cast<void *>(a)),
+                                         static_cast<double *>(const_cast<void *>(b_local)),
+                                         static_cast<double *>(mine), sa, ta, 2, sb, tb, 2, sc,
+                                         tc, 2, stream);
+    else if (dtype == DTYPE_FLOAT32)
+        ok = cuda_batched_matmul_nd_launcher(static_cast<float *>(const_cast<void *>(a)),
+                                             static_cast<float *>(const_cast<void *>(b_local)),
+                                             static_cast<float *>(mine), sa, ta, 2, sb, tb, 2, sc,
+                                             tc, 2, stream);
+    else
+        ok = cuda_low_precision_matmul_nd_launcher(const_cast<void *>(a),
+                                                   const_cast<void *>(b_local), mine, dtype, sa,
+                                                   ta, 2, sb, tb, 2, sc, tc, 2, stream);
+    if (!ok)
+        return 0;
+    // 2. in-place all-gather of every rank's block over NVLink
+    if (G > 1) {
+        if (!nccl() || g_nccl.all_gather(mine, workspace, slot * es, ncclUint8, comm->nccl,
+                                         stream) != ncclSuccess) {
+            ptg_set_last_status(GEMM_SM100_STATUS_NCCL);
+            return 0;
+        }
+    }
+    // 3. [G][M][nb] -> [M][G * nb]
+    const long long total = static_cast<long long>(slot) * G;
+    const int threads = 256;
+    const long long want = (total + threads - 1) / threads;
+    const int blocks = static_cast<int>(want < 148 * 16 ? want : 148 * 16);
+    switch (es) {
+    case 8:
+        if ((nb % 2) == 0 && (reinterpret_cast<uintptr_t>(c) % 16) == 0)
+            nsplit_permute_kernel<uint4><<<blocks, threads, 0, stream>>>(
+                static_cast<const uint4 *>(workspace), static_cast<uint4 *>(c), G, M, nb / 2);
+        else
+            nsplit_permute_kernel<uint2><<<blocks, threads, 0, stream>>>(
+                static_cast<const uint2 *>(workspace), static_cast<uint2 *>(c), G, M, nb);
+        break;
+    case 4:
+        nsplit_permute_kernel<uint32_t><<<blocks, threads, 0, stream>>>(
+            static_cast<const uint32_t *>(workspace), static_cast<uint32_t *>(c), G, M, nb);
+        break;
+    default:
+        nsplit_permute_kernel<uint16_t><<<blocks, threads, 0, stream>>>(
+            static_cast<const uint16_t *>(workspace), static_cast<uint16_t *>(c), G, M, nb);
+        break;
+    }
+    const cudaError_t err = cudaGetLastError();
+    if (err != cudaSuccess) {
+        ptg_set_last_status(static_cast<int>(err));
+        return 0;
+    }
+    return 1;
+}

@@ -106,6 +106,17 @@ _SIGNATURES = {
     "gemm_sm100_device_status": (ctypes.c_int, [ctypes.c_int, ctypes.c_int]),
     "gemm_sm100_algorithm_name": (ctypes.c_char_p, [ctypes.c_int]),
     "gemm_sm100_version": (ctypes.c_int, []),
+    "gemm_mgpu_unique_id": (ctypes.c_int, [ctypes.c_void_p]),
+    "gemm_mgpu_comm_init": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_int,
+                                           ctypes.POINTER(ctypes.c_void_p)]),
+    "gemm_mgpu_comm_destroy": (None, [ctypes.c_void_p]),
+    "gemm_mgpu_nsplit_workspace_bytes": (ctypes.c_size_t, [ctypes.c_int, ctypes.c_int,
+                                                           ctypes.c_int, ctypes.c_int]),
+    "gemm_mgpu_nsplit_matmul": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p,
+                                               ctypes.c_size_t, ctypes.c_size_t, ctypes.c_void_p,
+                                               ctypes.c_size_t, ctypes.c_size_t, ctypes.c_void_p,
+                                               ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                               ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]),
     "pt_last_error": (ctypes.c_char_p, []),
     "pt_matmul_result_shape": (ctypes.c_int, [ctypes.POINTER(PtTensor)] * 2 +
                                [ctypes.POINTER(ctypes.c_int), ctypes.POINTER(ctypes.c_int)]),
@@ -424,3 +435,70 @@ def set_kernel_path(path):
 
 def device_status(device=0, clear=True):
     return library().gemm_sm100_device_status(device, 1 if clear else 0)
+
+
+# ---------------------------------------------------------------- multi-GPU
+class MgpuComm:
+    """NCCL communicator of the library for one process per GPU.
+
+    Rank 0 creates the id with gemm_mgpu_unique_id; it reaches the other ranks
+    through the already-initialised torch.distributed process group (host
+    plumbing only), and every rank joins on its current device.
+    """
+
+    def __init__(self, rank, world):
+        import torch.distributed as dist
+        lib = library()
+        idbuf = (ctypes.c_ubyte * 128)()
+        if rank == 0 and not lib.gemm_mgpu_unique_id(idbuf):
+            raise RuntimeException("NCCL is unavailable for the multi-GPU entry points")
+        obj = [bytes(idbuf)]
+        if world > 1:
+            dist.broadcast_object_list(obj, src=0)
+        idbuf = (ctypes.c_ubyte * 128).from_buffer_copy(obj[0])
+        handle = ctypes.c_void_p()
+        if not lib.gemm_mgpu_comm_init(idbuf, world, rank, ctypes.byref(handle)):
+            raise RuntimeException("gemm_mgpu_comm_init failed (status %d)"
+                                   % cuda_get_backend_info()["lastBlasStatus"])
+        self.handle, self.rank, self.world = handle, rank, world
+
+    def close(self):
+        if self.handle:
+            library().gemm_mgpu_comm_destroy(self.handle)
+            self.handle = None
+
+
+def nsplit_columns(N, rank, world):
+    """Column block [lo, hi) of rank `rank` in an N-split product."""
+    if N % world:
+        raise InvalidArgumentException("N-split needs N divisible by the number of ranks")
+    nb = N // world
+    return rank * nb, (rank + 1) * nb
+
+
+def nsplit_matmul(comm, a, b_local, N, workspace=None):
+    """C = A . B with B split along N: `b_local` is this rank's column block;
+    every rank receives the whole row-major C (gemm_mgpu_nsplit_matmul)."""
+    lib = library()
+    torch = _torch()
+    M, K = a.getShape()
+    if b_local.getShape() != [K, N // comm.world] or a.dtype() != b_local.dtype():
+        raise InvalidArgumentException("b_local must be this rank's [K, N / ranks] block")
+    dt = a.dtype()
+    need = lib.gemm_mgpu_nsplit_workspace_bytes(comm.world, DTYPE_CODES[dt], M, N)
+    if need == 0 and M * N > 0:
+        raise InvalidArgumentException("N-split needs N divisible by the number of ranks")
+    if workspace is None:
+        workspace = torch.empty(max(need, 16), dtype=torch.uint8, device="cuda")
+    c = CudaArray(torch.empty(max(M * N, 1), dtype=_torch_dtype(dt), device="cuda"), [M, N],
+                  dtype=dt)
+    es = ELEMENT_BYTES[dt]
+    ok = lib.gemm_mgpu_nsplit_matmul(
+        comm.handle, DTYPE_CODES[dt], a._storage.data_ptr() + a._offset * es, a._strides[0],
+        a._strides[1], b_local._storage.data_ptr() + b_local._offset * es, b_local._strides[0],
+        b_local._strides[1], c._storage.data_ptr(), M, N, K, workspace.data_ptr(),
+        workspace.numel(), current_stream())
+    if not ok:
+        raise RuntimeException("N-split matmul failed (status %d)"
+                               % cuda_get_backend_info()["lastBlasStatus"])
+    return c
