@@ -173,6 +173,7 @@ int cuda_low_precision_matmul_nd_launcher(
 #define GEMM_SM100_STATUS_NO_DRIVER 9002   /* driver entry point unavailable */
 #define GEMM_SM100_STATUS_NO_DEVICE 9003   /* no current CUDA device / not sm_100 */
 #define GEMM_SM100_STATUS_NCCL 9004        /* NCCL failure (multi-GPU entry points) */
+#define GEMM_SM100_STATUS_SCRATCH_LIMIT 9005 /* product larger than the library-owned buffer */
 
 /* FP64 C = A.B with the batched launcher's shape/broadcast rules.  New scope:
  * the reference rejects float64 matmul (src/cuda_array/ca_private.c:1099-1106). */
@@ -261,6 +262,35 @@ int gemm_mgpu_nsplit_matmul(gemm_mgpu_comm *comm, dtype_t dtype,
                             const void *b_local, size_t b_s0, size_t b_s1,
                             void *c, int M, int N, int K,
                             void *workspace, size_t workspace_bytes, cudaStream_t stream);
+
+/* Size of the library-owned gather buffer of gemm_mgpu_nsplit_matmul_noalloc:
+ * 32 MiB of device memory on every GPU that loads the library, held until the
+ * process exits. */
+#define GEMM_MGPU_NSPLIT_SCRATCH_BYTES (32u << 20)
+
+/* gemm_mgpu_nsplit_matmul for callers that cannot allocate device memory when
+ * they multiply -- a thread that is capturing a CUDA graph (cudaMalloc is not
+ * allowed there), or a program whose device memory all belongs to its own
+ * pool and that must not call cudaMalloc/cudaFree (cudaFree synchronises the
+ * device).  No counterpart in the reference; this entry point allocates
+ * nothing.  Instead of a caller workspace it uses a buffer inside the library
+ * (GEMM_MGPU_NSPLIT_SCRATCH_BYTES per device), so M * N elements of `dtype`
+ * must fit in it; larger products return 0 with last_blas_status =
+ * GEMM_SM100_STATUS_SCRATCH_LIMIT and enqueue nothing.  The first call on a
+ * device looks up the buffer's device address (once per device, with the
+ * communicator's device current): make that first call before any stream
+ * capture.  All calls share the one buffer and it keeps the last call's
+ * contents; every call overwrites the part it uses before reading it, so
+ * nothing has to start at zero.  Calls whose work overlaps on the GPU (other
+ * streams, or other threads on the same device) race on the buffer: issue
+ * them on one stream.  With more than one rank the call runs an NCCL
+ * all-gather on the communicator; NCCL sets up its connection buffers on a
+ * communicator's first collective, so run one collective on it (e.g. one
+ * gemm_mgpu_nsplit_matmul) at set-up time. */
+int gemm_mgpu_nsplit_matmul_noalloc(gemm_mgpu_comm *comm, dtype_t dtype,
+                                    const void *a, size_t a_s0, size_t a_s1,
+                                    const void *b_local, size_t b_s0, size_t b_s1,
+                                    void *c, int M, int N, int K, cudaStream_t stream);
 
 #ifdef __cplusplus
 }

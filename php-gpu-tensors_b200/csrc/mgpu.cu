@@ -228,3 +228,69 @@ PT_API int gemm_mgpu_nsplit_matmul(gemm_mgpu_comm *comm, dtype_t dtype, const vo
     }
     return 1;
 }
+
+// ---------------------------------------------------------------- no-alloc variant
+//
+// Some callers cannot allocate device memory at the moment they multiply:
+// code that is being captured into a CUDA graph (cudaMalloc is not allowed
+// from a capturing thread), or a host program whose device memory is entirely
+// owned by its own pool allocator and must never see a cudaMalloc/cudaFree
+// (cudaFree also synchronises the whole device).  For them the N-split
+// product can use a gather buffer that lives in the library itself: a fixed
+// array in device memory, reserved on every GPU that loads the library and
+// held until the process exits.
+
+namespace {
+
+// The library-owned gather buffer (one copy per device).
+static __device__ __align__(256) unsigned char g_nsplit_scratch[GEMM_MGPU_NSPLIT_SCRATCH_BYTES];
+
+constexpr int kScratchDevices = 64;
+void *g_scratch_addr[kScratchDevices];   // device address of g_nsplit_scratch, per device
+std::mutex g_scratch_mutex;
+
+// The host-side name g_nsplit_scratch is only a stand-in for the array, not a
+// device address; the address a kernel or NCCL may use comes from
+// cudaGetSymbolAddress, taken once per device with that device current.
+void *scratch_address(int device)
+{
+    if (device < 0 || device >= kScratchDevices)
+        return nullptr;
+    std::lock_guard<std::mutex> lock(g_scratch_mutex);
+    if (!g_scratch_addr[device]) {
+        void *p = nullptr;
+        if (cudaGetSymbolAddress(&p, g_nsplit_scratch) != cudaSuccess)
+            return nullptr;
+        g_scratch_addr[device] = p;
+    }
+    return g_scratch_addr[device];
+}
+
+} // namespace
+
+PT_API int gemm_mgpu_nsplit_matmul_noalloc(gemm_mgpu_comm *comm, dtype_t dtype, const void *a,
+                                           size_t a_s0, size_t a_s1, const void *b_local,
+                                           size_t b_s0, size_t b_s1, void *c, int M, int N,
+                                           int K, cudaStream_t stream)
+{
+    const size_t es = element_bytes(dtype);
+    if (!comm || es == 0 || M < 0 || N < 0 || K < 0)
+        return 0;
+    const size_t need = static_cast<size_t>(M) * static_cast<size_t>(N) * es;
+    if (need > GEMM_MGPU_NSPLIT_SCRATCH_BYTES) {
+        ptg_set_last_status(GEMM_SM100_STATUS_SCRATCH_LIMIT);
+        return 0;
+    }
+    int device = -1;
+    if (cudaGetDevice(&device) != cudaSuccess || device != comm->device) {
+        ptg_set_last_status(GEMM_SM100_STATUS_NO_DEVICE);
+        return 0;
+    }
+    void *scratch = scratch_address(device);
+    if (!scratch) {
+        ptg_set_last_status(GEMM_SM100_STATUS_NO_DEVICE);
+        return 0;
+    }
+    return gemm_mgpu_nsplit_matmul(comm, dtype, a, a_s0, a_s1, b_local, b_s0, b_s1, c, M, N, K,
+                                   scratch, GEMM_MGPU_NSPLIT_SCRATCH_BYTES, stream);
+}

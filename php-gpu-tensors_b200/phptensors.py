@@ -117,6 +117,13 @@ _SIGNATURES = {
                                                ctypes.c_size_t, ctypes.c_size_t, ctypes.c_void_p,
                                                ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                                ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]),
+    "gemm_mgpu_nsplit_matmul_noalloc": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int,
+                                                       ctypes.c_void_p, ctypes.c_size_t,
+                                                       ctypes.c_size_t, ctypes.c_void_p,
+                                                       ctypes.c_size_t, ctypes.c_size_t,
+                                                       ctypes.c_void_p, ctypes.c_int,
+                                                       ctypes.c_int, ctypes.c_int,
+                                                       ctypes.c_void_p]),
     "pt_last_error": (ctypes.c_char_p, []),
     "pt_matmul_result_shape": (ctypes.c_int, [ctypes.POINTER(PtTensor)] * 2 +
                                [ctypes.POINTER(ctypes.c_int), ctypes.POINTER(ctypes.c_int)]),
