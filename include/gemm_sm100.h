@@ -208,6 +208,10 @@ int cuda_matmul_epilogue_nd_launcher(
  * "tc-bf16-128x256", "tc-3xtf32-128x128", "simt-f32"; "none" before any. */
 const char *gemm_sm100_last_kernel(void);
 
+/* Grid size (CTAs), CTA size (threads) and cluster size of the last
+ * tensor-core launch on this thread (0 before any); any pointer may be NULL. */
+void gemm_sm100_last_launch(int *grid, int *block, int *cluster);
+
 /* Selects the kernel family for this thread's later launches and returns the
  * previous setting: 0 = automatic, 1 = single-CTA tensor-core kernel whenever
  * the layout allows it (ignoring the size heuristic), 2 = CUDA-core kernel

@@ -83,6 +83,27 @@ int pt_tensor_matmul_backward(const pt_tensor *a, const pt_tensor *b, const pt_t
                               const pt_tensor *grad_a, const pt_tensor *grad_b,
                               cudaStream_t stream);
 
+/* Batched C = A . B between HOST buffers, streamed through the current
+ * device: the batch axis is cut into `chunks` pieces whose host-to-device
+ * copies, products and device-to-host copies overlap on three streams, so the
+ * PCIe transfers in both directions run concurrently with each other and
+ * with the tensor cores (the CudaArray::fromBuffer -> matmul -> toBuffer
+ * sequence, pipelined).  A is [batches, M, K], B is [batches, K, N] (or one
+ * [K, N] matrix shared by every batch when b_shared != 0), C is
+ * [batches, M, N], all row-major contiguous host memory of `dtype`
+ * (FLOAT32/FLOAT16/BFLOAT16, or FLOAT64 with PT_MATMUL_ALLOW_FLOAT64 in
+ * flags).  Host buffers should be page-locked (cudaHostAlloc or
+ * cudaHostRegister) for the copies to overlap.  The three streams and the
+ * device staging (two chunk slots) are created on the first call and kept,
+ * per host thread and device, for later calls; pt_host_release() frees them.
+ * Blocks until C is on the host; returns PT_OK or a PT_* error with
+ * pt_last_error() set. */
+int pt_host_matmul(const void *a, const void *b, void *c, dtype_t dtype, int batches, int M,
+                   int N, int K, int b_shared, int chunks, int flags);
+
+/* Frees this thread's pt_host_matmul streams and staging (synchronises them). */
+void pt_host_release(void);
+
 #ifdef __cplusplus
 }
 #endif

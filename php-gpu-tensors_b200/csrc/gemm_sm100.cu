@@ -67,6 +67,7 @@ thread_local cuda_backend_info t_info = {};
 thread_local int t_precision = CUDA_MATMUL_PRECISION_FP32_STRICT;
 thread_local int t_path = 0;
 thread_local const char *t_last_kernel = "none";
+thread_local int t_last_grid = 0, t_last_block = 0, t_last_cluster = 0;
 
 struct TunedPlan {
     int rows, inner, cols;
@@ -391,6 +392,9 @@ cudaError_t launch_tc_kernel(DeviceState *ds, int kid, const CUtensorMap &ma,
     p.status = ds->status;
     const long long grid = std::min<long long>(p.tiles, ds->sms);
     kernel<<<static_cast<unsigned>(grid), Cfg::kThreads, Cfg::kSmemBytes, stream>>>(ma, mb, mc, p);
+    t_last_grid = static_cast<int>(grid);
+    t_last_block = Cfg::kThreads;
+    t_last_cluster = 1;
     return cudaGetLastError();
 }
 
@@ -432,6 +436,9 @@ cudaError_t launch_tc2_kernel(DeviceState *ds, int kid, int slot, const CUtensor
     const long long n = std::min<long long>(p.tiles, clusters);
     cfg.gridDim = dim3(static_cast<unsigned>(2 * n));
     const cudaError_t err = cudaLaunchKernelEx(&cfg, kernel, ma, mb, mc, p);
+    t_last_grid = static_cast<int>(2 * n);
+    t_last_block = Cfg::kThreads;
+    t_last_cluster = 2;
     if (err != cudaSuccess)
         return err;
     return cudaGetLastError();
@@ -976,6 +983,13 @@ PT_API int cuda_blas_tune_matmul(float *a, float *b, float *c, int rows, int inn
 }
 
 PT_API const char *gemm_sm100_last_kernel(void) { return t_last_kernel; }
+
+PT_API void gemm_sm100_last_launch(int *grid, int *block, int *cluster)
+{
+    if (grid) *grid = t_last_grid;
+    if (block) *block = t_last_block;
+    if (cluster) *cluster = t_last_cluster;
+}
 
 PT_API int gemm_sm100_set_path(int path)
 {

@@ -234,3 +234,203 @@ PT_API int pt_tensor_matmul_backward(const pt_tensor *a, const pt_tensor *b,
     }
     return ok();
 }
+
+namespace {
+
+// Streams, events and device staging of the host-buffer pipeline, kept per
+// host thread and device across calls (allocation and stream creation cost
+// far more than a chunk's copies).
+struct HostPipeline {
+    int device = -1;
+    cudaStream_t s_in = nullptr, s_comp = nullptr, s_out = nullptr;
+    cudaEvent_t in_done[2] = {}, compute_done[2] = {}, out_done[2] = {};
+    void *stage = nullptr;   // [slot 0: a | b | c][slot 1: a | b | c][shared b]
+    size_t stage_bytes = 0;
+};
+
+thread_local HostPipeline t_pipe;
+
+void release_pipeline(HostPipeline &p)
+{
+    if (p.device < 0)
+        return;
+    int prev = -1;
+    cudaGetDevice(&prev);
+    cudaSetDevice(p.device);
+    if (p.s_in) cudaStreamSynchronize(p.s_in);
+    if (p.s_comp) cudaStreamSynchronize(p.s_comp);
+    if (p.s_out) cudaStreamSynchronize(p.s_out);
+    if (p.stage) cudaFree(p.stage);
+    for (int i = 0; i < 2; i++) {
+        if (p.in_done[i]) cudaEventDestroy(p.in_done[i]);
+        if (p.compute_done[i]) cudaEventDestroy(p.compute_done[i]);
+        if (p.out_done[i]) cudaEventDestroy(p.out_done[i]);
+    }
+    if (p.s_in) cudaStreamDestroy(p.s_in);
+    if (p.s_comp) cudaStreamDestroy(p.s_comp);
+    if (p.s_out) cudaStreamDestroy(p.s_out);
+    if (prev >= 0)
+        cudaSetDevice(prev);
+    p = HostPipeline();
+}
+
+// Makes the pipeline ready on the current device with at least `bytes` of
+// staging.  Returns a cudaError_t.
+cudaError_t prepare_pipeline(size_t bytes)
+{
+    int dev = -1;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess)
+        return e;
+    HostPipeline &p = t_pipe;
+    if (p.device != dev) {
+        release_pipeline(p);
+        p.device = dev;
+        if ((e = cudaStreamCreateWithFlags(&p.s_in, cudaStreamNonBlocking)) != cudaSuccess ||
+            (e = cudaStreamCreateWithFlags(&p.s_comp, cudaStreamNonBlocking)) != cudaSuccess ||
+            (e = cudaStreamCreateWithFlags(&p.s_out, cudaStreamNonBlocking)) != cudaSuccess)
+            return e;
+        for (int i = 0; i < 2; i++)
+            if ((e = cudaEventCreateWithFlags(&p.in_done[i], cudaEventDisableTiming)) != cudaSuccess ||
+                (e = cudaEventCreateWithFlags(&p.compute_done[i], cudaEventDisableTiming)) !=
+                    cudaSuccess ||
+                (e = cudaEventCreateWithFlags(&p.out_done[i], cudaEventDisableTiming)) != cudaSuccess)
+                return e;
+    }
+    if (p.stage_bytes < bytes) {
+        if (p.stage) {
+            cudaStreamSynchronize(p.s_in);
+            cudaStreamSynchronize(p.s_comp);
+            cudaStreamSynchronize(p.s_out);
+            cudaFree(p.stage);
+            p.stage = nullptr;
+            p.stage_bytes = 0;
+        }
+        if ((e = cudaMalloc(&p.stage, bytes)) != cudaSuccess)
+            return e;
+        p.stage_bytes = bytes;
+    }
+    return cudaSuccess;
+}
+
+size_t round256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
+
+} // namespace
+
+PT_API void pt_host_release(void)
+{
+    release_pipeline(t_pipe);
+}
+
+PT_API int pt_host_matmul(const void *a, const void *b, void *c, dtype_t dtype, int batches, int M,
+                          int N, int K, int b_shared, int chunks, int flags)
+{
+    if (!supported_dtype(dtype, flags))
+        return fail(PT_INVALID_ARGUMENT,
+                    "matmul requires matching float32, float16 or bfloat16 operands");
+    if (batches < 0 || M < 0 || N < 0 || K < 0 ||
+        (!a && static_cast<long long>(M) * K != 0) || (!b && static_cast<long long>(K) * N != 0) ||
+        (!c && static_cast<long long>(M) * N != 0))
+        return fail(PT_INVALID_ARGUMENT, "Matrix multiplication failed - incompatible dimensions");
+    if (batches == 0 || M == 0 || N == 0)
+        return ok();
+    const size_t es = element_size(dtype);
+    if (chunks < 1)
+        chunks = 1;
+    if (chunks > batches)
+        chunks = batches;
+    const int per = (batches + chunks - 1) / chunks;   // batches per chunk (last may be shorter)
+    const size_t a_b = static_cast<size_t>(M) * K * es;   // bytes per batch
+    const size_t b_b = static_cast<size_t>(K) * N * es;
+    const size_t c_b = static_cast<size_t>(M) * N * es;
+    const size_t sa = round256(a_b * per), sb = b_shared ? 0 : round256(b_b * per);
+    const size_t sc = round256(c_b * per), slot_bytes = sa + sb + sc;
+    const size_t shared_b = b_shared ? round256(b_b) : 0;
+
+    cudaError_t e = prepare_pipeline(2 * slot_bytes + shared_b);
+    if (e != cudaSuccess)
+        return fail(PT_RUNTIME, "Host matmul staging set-up failed (CUDA error %d)",
+                    static_cast<int>(e));
+    HostPipeline &p = t_pipe;
+    char *stage = static_cast<char *>(p.stage);
+    char *b_dev = stage + 2 * slot_bytes;
+    int status = PT_OK;
+    auto cuda_ok = [&](cudaError_t err) {
+        if (err == cudaSuccess)
+            return true;
+        if (status == PT_OK)
+            status = fail(PT_RUNTIME, "Host matmul failed (CUDA error %d)", static_cast<int>(err));
+        return false;
+    };
+    // the previous call on this thread is complete (it synchronised), so the
+    // staging is free; start with the shared B
+    bool good = !b_shared ||
+                cuda_ok(cudaMemcpyAsync(b_dev, b, b_b, cudaMemcpyHostToDevice, p.s_comp));
+
+    for (int i = 0; good && i < chunks; i++) {
+        const int b0 = i * per;
+        const int nb = (b0 + per <= batches) ? per : batches - b0;
+        if (nb <= 0)
+            break;
+        const int k = i & 1;
+        char *a_s = stage + k * slot_bytes, *b_s = a_s + sa, *c_s = b_s + sb;
+        if (i >= 2) {
+            // slot reuse: the product of chunk i-2 has read its inputs and its
+            // result has been copied out
+            good = cuda_ok(cudaStreamWaitEvent(p.s_in, p.compute_done[k], 0)) &&
+                   cuda_ok(cudaStreamWaitEvent(p.s_comp, p.out_done[k], 0));
+        }
+        good = good &&
+               cuda_ok(cudaMemcpyAsync(a_s, static_cast<const char *>(a) + a_b * b0, a_b * nb,
+                                       cudaMemcpyHostToDevice, p.s_in)) &&
+               (b_shared ||
+                cuda_ok(cudaMemcpyAsync(b_s, static_cast<const char *>(b) + b_b * b0, b_b * nb,
+                                        cudaMemcpyHostToDevice, p.s_in))) &&
+               cuda_ok(cudaEventRecord(p.in_done[k], p.s_in)) &&
+               cuda_ok(cudaStreamWaitEvent(p.s_comp, p.in_done[k], 0));
+        if (!good)
+            break;
+        pt_tensor ta, tb, tc;
+        std::memset(&ta, 0, sizeof(ta));
+        ta.data = a_s;
+        ta.dtype = dtype;
+        ta.ndims = 3;
+        ta.shape[0] = nb; ta.shape[1] = M; ta.shape[2] = K;
+        contiguous_strides(ta.shape, 3, ta.strides);
+        tb = ta;
+        if (b_shared) {
+            tb.data = b_dev;
+            tb.ndims = 2;
+            tb.shape[0] = K; tb.shape[1] = N;
+            contiguous_strides(tb.shape, 2, tb.strides);
+        } else {
+            tb.data = b_s;
+            tb.shape[1] = K; tb.shape[2] = N;
+            contiguous_strides(tb.shape, 3, tb.strides);
+        }
+        tc = ta;
+        tc.data = c_s;
+        tc.shape[1] = M; tc.shape[2] = N;
+        contiguous_strides(tc.shape, 3, tc.strides);
+        const int st = pt_tensor_matmul_into(&ta, &tb, &tc, flags, p.s_comp);
+        if (st != PT_OK) {
+            status = st;
+            good = false;
+            break;
+        }
+        good = cuda_ok(cudaEventRecord(p.compute_done[k], p.s_comp)) &&
+               cuda_ok(cudaStreamWaitEvent(p.s_out, p.compute_done[k], 0)) &&
+               cuda_ok(cudaMemcpyAsync(static_cast<char *>(c) + c_b * b0, c_s, c_b * nb,
+                                       cudaMemcpyDeviceToHost, p.s_out)) &&
+               cuda_ok(cudaEventRecord(p.out_done[k], p.s_out));
+    }
+    // drain all three streams (also on the error path) before returning
+    const cudaError_t e1 = cudaStreamSynchronize(p.s_in);
+    const cudaError_t e2 = cudaStreamSynchronize(p.s_comp);
+    const cudaError_t e3 = cudaStreamSynchronize(p.s_out);
+    if (good)
+        good = cuda_ok(e1) && cuda_ok(e2) && cuda_ok(e3);
+    if (good && status == PT_OK)
+        return ok();
+    return status;
+}

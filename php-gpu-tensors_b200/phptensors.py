@@ -103,6 +103,7 @@ _SIGNATURES = {
         [ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p]),
     "gemm_sm100_last_kernel": (ctypes.c_char_p, []),
     "gemm_sm100_set_path": (ctypes.c_int, [ctypes.c_int]),
+    "gemm_sm100_last_launch": (None, [ctypes.POINTER(ctypes.c_int)] * 3),
     "gemm_sm100_device_status": (ctypes.c_int, [ctypes.c_int, ctypes.c_int]),
     "gemm_sm100_algorithm_name": (ctypes.c_char_p, [ctypes.c_int]),
     "gemm_sm100_version": (ctypes.c_int, []),
@@ -124,6 +125,8 @@ _SIGNATURES = {
                                                        ctypes.c_void_p, ctypes.c_int,
                                                        ctypes.c_int, ctypes.c_int,
                                                        ctypes.c_void_p]),
+    "pt_host_matmul": (ctypes.c_int, [ctypes.c_void_p] * 3 + [ctypes.c_int] * 8),
+    "pt_host_release": (None, []),
     "pt_last_error": (ctypes.c_char_p, []),
     "pt_matmul_result_shape": (ctypes.c_int, [ctypes.POINTER(PtTensor)] * 2 +
                                [ctypes.POINTER(ctypes.c_int), ctypes.POINTER(ctypes.c_int)]),
@@ -369,6 +372,28 @@ class CudaArray:
         return t.numpy()
 
 
+def host_matmul(a, b, c, chunks=8, allow_float64=False):
+    """Batched product between HOST torch tensors (pinned for overlap):
+    a [batches, M, K], b [batches, K, N] or [K, N] (shared), c [batches, M, N]
+    are filled through pt_host_matmul, whose copies and products overlap."""
+    torch = _torch()
+    rev = {torch.float32: "float32", torch.float64: "float64", torch.float16: "float16",
+           torch.bfloat16: "bfloat16"}
+    dt = rev[a.dtype]
+    if not (a.is_contiguous() and b.is_contiguous() and c.is_contiguous()):
+        raise InvalidArgumentException("host_matmul needs contiguous row-major host tensors")
+    batches, M, K = a.shape
+    shared = b.dim() == 2
+    N = b.shape[-1]
+    if (b.shape[-2] != K or list(c.shape) != [batches, M, N]
+            or (not shared and b.shape[0] != batches)):
+        raise InvalidArgumentException("Matrix multiplication failed - incompatible dimensions")
+    _raise_for(library().pt_host_matmul(
+        a.data_ptr(), b.data_ptr(), c.data_ptr(), DTYPE_CODES[dt], batches, M, N, K,
+        1 if shared else 0, chunks, PT_MATMUL_ALLOW_FLOAT64 if allow_float64 else 0))
+    return c
+
+
 def _shape_args(x):
     nd = len(x._shape)
     shape = (ctypes.c_int * MAX_DIMS)(*x._shape)
@@ -438,6 +463,13 @@ def set_kernel_path(path):
     2 CUDA cores only, 3 2-CTA tensor-core kernel (16-bit) whenever allowed."""
     return library().gemm_sm100_set_path(
         {"auto": 0, "tensor-core": 1, "simt": 2, "tensor-core-pair": 3}[path])
+
+
+def last_launch():
+    """(grid, block, cluster) of the last tensor-core launch on this thread."""
+    g, b, c = ctypes.c_int(), ctypes.c_int(), ctypes.c_int()
+    library().gemm_sm100_last_launch(ctypes.byref(g), ctypes.byref(b), ctypes.byref(c))
+    return g.value, b.value, c.value
 
 
 def device_status(device=0, clear=True):

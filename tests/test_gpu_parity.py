@@ -446,3 +446,22 @@ def test_k_zero_and_empty_batch_on_device():
     assert a.matmul(b).toArray() == [[0.0, 0.0, 0.0], [0.0, 0.0, 0.0]]
     e = P.CudaArray.zeros([0, 2, 3]).matmul(P.CudaArray.ones([3, 2]))
     assert e.getShape() == [0, 2, 2]
+
+
+@pytest.mark.parametrize("dtype", ["bfloat16", "float32"])
+@pytest.mark.parametrize("shared", [False, True])
+def test_host_matmul_streams_equal_device_product(dtype, shared):
+    """pt_host_matmul (host buffers in and out, chunked and overlapped) gives
+    the same bits as the product of the same operands on the device."""
+    tdt = TORCH_DT[dtype]
+    g = torch.Generator().manual_seed(9)
+    batches, M, N, K = 7, 200, 136, 264
+    a = torch.randn(batches, M, K, generator=g).to(tdt).pin_memory()
+    b = (torch.randn(K, N, generator=g) if shared
+         else torch.randn(batches, K, N, generator=g)).to(tdt).pin_memory()
+    c = torch.empty(batches, M, N, dtype=tdt).pin_memory()
+    P.host_matmul(a, b, c, chunks=3)
+    ref = P.CudaArray.from_torch(a.cuda()).matmul(P.CudaArray.from_torch(b.cuda())).to_torch()
+    assert torch.equal(c, ref.cpu())
+    with pytest.raises(P.InvalidArgumentException):
+        P.host_matmul(a, b, torch.empty(batches, M, N + 1, dtype=tdt))
