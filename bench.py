@@ -59,6 +59,8 @@ def parse():
     p.add_argument("--warmup", type=int, default=10)
     p.add_argument("--impl", default="ours", choices=["ours", "reference"])
     p.add_argument("--workload", default="config2", choices=sorted(WORKLOADS))
+    p.add_argument("--nsplit", default="fused", choices=["fused", "nccl"],
+                   help="config5b exchange: fused peer stores, or NCCL all-gather + permute")
     p.add_argument("--cpu-seconds", type=float, default=8.0,
                    help="target duration of the bounded CPU baseline sample")
     return p.parse_args()
@@ -243,7 +245,13 @@ def run_nsplit(args, w):
     comm = P.MgpuComm(rank, world)
     A = P.CudaArray.from_torch(a)
     Bl = P.CudaArray.from_torch(b_local)
-    ws = torch.empty(M * N * 8, dtype=torch.uint8, device="cuda")
+    fused = args.nsplit == "fused"
+    if fused:
+        win = P.MgpuWindow(comm, M, N)
+        step = lambda: P.nsplit_matmul_fused(win, A, Bl)
+    else:
+        ws = torch.empty(M * N * 8, dtype=torch.uint8, device="cuda")
+        step = lambda: P.nsplit_matmul(comm, A, Bl, N, ws)
     stream = torch.cuda.current_stream()
 
     def barrier():
@@ -253,7 +261,7 @@ def run_nsplit(args, w):
         torch.cuda.synchronize()
 
     for _ in range(args.warmup):
-        C = P.nsplit_matmul(comm, A, Bl, N, ws)
+        step()
     kernel = P.cuda_get_backend_info()["kernel"]
     barrier()
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -262,7 +270,7 @@ def run_nsplit(args, w):
         barrier()
         start.record(stream)
         for _ in range(args.steps):
-            C = P.nsplit_matmul(comm, A, Bl, N, ws)
+            step()
         stop.record(stream)
         torch.cuda.synchronize()
     ms_local = start.elapsed_time(stop)
@@ -280,17 +288,23 @@ def run_nsplit(args, w):
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
             "dtype": "f64", "data": "synthetic U[-1,1) on device",
             "config": {"workload": "config5b", "M": M, "N": N, "K": K,
-                       "parallelism": "N-split x%d + NCCL all-gather + permute" % world,
+                       "parallelism": ("N-split x%d, exchange fused into the GEMM epilogue "
+                                       "(peer stores over NVLink)" % world) if fused else
+                                      ("N-split x%d + NCCL all-gather + permute" % world),
                        "kernel": kernel,
                        "allgather_bytes_received_per_rank": M * (N - (hi - lo)) * 8},
             "cpu_baseline": None, "e2e": None,
-            "gpu_launches": args.steps * 2,
+            "gpu_launches": args.steps * (1 if fused else 2),
             "clocks": sampler.summary(),
         }
         print(json.dumps(line), flush=True)
-    comm.close()
     if world > 1:
         import torch.distributed as dist
+        dist.barrier()
+    if fused:
+        win.close()
+    comm.close()
+    if world > 1:
         dist.barrier()
         dist.destroy_process_group()
 

@@ -267,6 +267,28 @@ int gemm_mgpu_nsplit_matmul(gemm_mgpu_comm *comm, dtype_t dtype,
                             void *c, int M, int N, int K,
                             void *workspace, size_t workspace_bytes, cudaStream_t stream);
 
+/* A result buffer mapped into every rank (CUDA IPC over NVLink / NVSwitch)
+ * for the fused N-split product.  Collective: each rank gets `bytes` of
+ * device memory (returned in *local; freed by gemm_mgpu_window_destroy) that
+ * every peer can store into.  At most 8 ranks. */
+typedef struct gemm_mgpu_window gemm_mgpu_window;
+int gemm_mgpu_window_create(gemm_mgpu_comm *comm, size_t bytes, gemm_mgpu_window **win,
+                            void **local);
+void gemm_mgpu_window_destroy(gemm_mgpu_window *win);
+
+/* The float64 N-split product with the exchange fused into the GEMM: the
+ * epilogue of this rank's column-block product stores every finished output
+ * row into all ranks' windows at this rank's column offset, so the transfer
+ * overlaps the remaining tiles, and no gather buffer or permute exists.
+ * After the call's work completes on `stream` (a one-element NCCL all-reduce
+ * follows the kernel), every rank's window holds the whole row-major C
+ * [M, N].  dtype FLOAT64; N divisible by the rank count with an even block
+ * width; M * N * 8 <= the window's bytes.  Returns 1 / 0. */
+int gemm_mgpu_nsplit_matmul_fused(gemm_mgpu_window *win, dtype_t dtype,
+                                  const void *a, size_t a_s0, size_t a_s1,
+                                  const void *b_local, size_t b_s0, size_t b_s1,
+                                  int M, int N, int K, cudaStream_t stream);
+
 /* Size of the library-owned gather buffer of gemm_mgpu_nsplit_matmul_noalloc:
  * 32 MiB of device memory on every GPU that loads the library, held until the
  * process exits. */

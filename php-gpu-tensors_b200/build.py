@@ -44,6 +44,7 @@ def nvcc_path():
 
 def _sources():
     return (glob.glob(os.path.join(CSRC, "*.cu")) + glob.glob(os.path.join(CSRC, "*.cuh")) +
+            glob.glob(os.path.join(CSRC, "*.h")) +
             glob.glob(os.path.join(HOST, "*.cpp")) +
             glob.glob(os.path.join(INCLUDE, "*.h")) + [EXPORTS, os.path.abspath(__file__)])
 

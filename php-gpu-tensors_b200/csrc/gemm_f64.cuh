@@ -11,6 +11,7 @@
 #pragma once
 
 #include "gemm_simt.cuh"
+#include "internal.h"
 
 namespace ptg {
 
@@ -101,7 +102,13 @@ __device__ __forceinline__ void f64_load_stage(const SimtParams &p, double *sa, 
     }
 }
 
-__global__ void __launch_bounds__(256, 1) f64_dmma_kernel(const SimtParams p, int a_vec, int b_vec)
+// PEER = false: the plain product into p.c.  PEER = true: the N-split
+// product whose epilogue stores each output row straight into all ranks'
+// results over NVLink (peer pointers in `po`), 16 bytes per thread,
+// consecutive threads on consecutive columns.
+template <bool PEER>
+__global__ void __launch_bounds__(256, 1)
+    f64_dmma_kernel_t(const SimtParams p, int a_vec, int b_vec, const F64PeerOut po)
 {
     extern __shared__ __align__(16) double f64_smem[];
     double *sa_all = f64_smem;
@@ -173,6 +180,44 @@ __global__ void __launch_bounds__(256, 1) f64_dmma_kernel(const SimtParams p, in
         }
         cp_async_wait<0>();
 
+        if constexpr (PEER) {
+            // Stage half a tile (64 rows x 128 columns) in the ring at a time,
+            // then copy rows out to every destination.
+            __syncthreads();
+            double *st = f64_smem;
+            for (int h = 0; h < 2; h++) {
+                if ((warp >> 2) == h) {
+#pragma unroll
+                    for (int i = 0; i < 4; i++)
+#pragma unroll
+                        for (int j = 0; j < 4; j++)
+#pragma unroll
+                            for (int r = 0; r < 4; r++) {
+                                const int row = i * 16 + g + (r >> 1) * 8;
+                                const int col = wn + j * 8 + t * 2 + (r & 1);
+                                st[row * kF64PitchB + col] = acc[i][j][r];
+                            }
+                }
+                __syncthreads();
+                for (int idx = threadIdx.x; idx < 64 * (kF64BN / 2); idx += 256) {
+                    const int row = idx / (kF64BN / 2), pair = idx % (kF64BN / 2);
+                    const int m = m0 + h * 64 + row, n = n0 + 2 * pair;
+                    if (m < p.M && n < p.N) {
+                        const double2 v = *reinterpret_cast<const double2 *>(
+                            st + row * kF64PitchB + 2 * pair);
+                        const long long off = static_cast<long long>(m) * po.ldc + po.col_off + n;
+                        for (int d = 0; d < po.ndst; d++)
+                            *reinterpret_cast<double2 *>(po.dst[d] + off) = v;
+                    }
+                }
+                __syncthreads();
+            }
+            // make this thread's peer stores visible system-wide before the
+            // kernel can be observed complete
+            __threadfence_system();
+            continue;
+        }
+
         double *C = static_cast<double *>(p.c);
         const double *bias = static_cast<const double *>(p.bias);
 #pragma unroll
@@ -194,5 +239,8 @@ __global__ void __launch_bounds__(256, 1) f64_dmma_kernel(const SimtParams p, in
                 }
     }
 }
+
+// The plain product.
+inline constexpr auto f64_dmma_kernel = f64_dmma_kernel_t<false>;
 
 } // namespace ptg

@@ -350,6 +350,7 @@ enum KernelId : int {
     KID_BF16_PAIR,
     KID_F16_PAIR,
     KID_F64_DMMA,
+    KID_F64_DMMA_PEER,
 };
 
 const char *kernel_name(int kid)
@@ -627,7 +628,9 @@ cudaError_t launch_f64_dmma(const Problem &P, DeviceState *ds, cudaStream_t stre
     dim3 grid(static_cast<unsigned>(std::min<long long>(nb, 2147483647ll)),
               static_cast<unsigned>(std::min<long long>(mb, 65535)),
               static_cast<unsigned>(std::min<long long>(P.batches, 65535)));
-    f64_dmma_kernel<<<grid, 256, kF64SmemBytes, stream>>>(s, a_vec ? 1 : 0, b_vec ? 1 : 0);
+    F64PeerOut none;
+    std::memset(&none, 0, sizeof(none));
+    f64_dmma_kernel<<<grid, 256, kF64SmemBytes, stream>>>(s, a_vec ? 1 : 0, b_vec ? 1 : 0, none);
     return cudaGetLastError();
 }
 
@@ -778,6 +781,44 @@ int nd_entry(int dt, const void *a, const void *b, void *c, int *shape_a, size_t
 
 // Internal (hidden) hook for the other translation units of the library.
 void ptg_set_last_status(int code) { set_status(code); }
+
+// Internal (hidden, declared in internal.h), used by csrc/mgpu.cu.
+cudaError_t ptg_launch_f64_peer(const double *a, size_t a_s0, size_t a_s1, const double *b,
+                                size_t b_s0, size_t b_s1, int M, int nb, int K,
+                                const F64PeerOut &po, cudaStream_t stream)
+{
+    DeviceState *ds = device_state();
+    if (!ds)
+        return cudaErrorNoDevice;
+    int sa[2] = {M, K}, sb[2] = {K, nb}, sc[2] = {M, nb};
+    size_t ta[2] = {a_s0, a_s1}, tb[2] = {b_s0, b_s1}, tc[2] = {static_cast<size_t>(nb), 1};
+    Problem P;
+    const int v = build_problem(DT_F64, a, b, po.dst[0], sa, ta, 2, sb, tb, 2, sc, tc, 2, &P);
+    if (v == 0)
+        return cudaErrorInvalidValue;
+    if (v == 2)
+        return cudaSuccess;
+    const SimtParams s = simt_params(P);
+    const bool a_vec = P.a_sk == 1 && P.K % 2 == 0 && (P.a_sm % 2 == 0 || P.M == 1) &&
+                       reinterpret_cast<uintptr_t>(a) % 16 == 0;
+    const bool b_vec = P.b_sn == 1 && P.N % 2 == 0 && (P.b_sk % 2 == 0 || P.K == 1) &&
+                       reinterpret_cast<uintptr_t>(b) % 16 == 0;
+    auto kernel = f64_dmma_kernel_t<true>;
+    if (!ensure_smem_attr(ds, KID_F64_DMMA_PEER, kernel, kF64SmemBytes))
+        return cudaErrorInvalidConfiguration;
+    const long long mb = (P.M + kF64BM - 1) / kF64BM;
+    const long long nbk = (P.N + kF64BN - 1) / kF64BN;
+    dim3 grid(static_cast<unsigned>(nbk), static_cast<unsigned>(std::min<long long>(mb, 65535)), 1);
+    kernel<<<grid, 256, kF64SmemBytes, stream>>>(s, a_vec ? 1 : 0, b_vec ? 1 : 0, po);
+    const cudaError_t err = cudaGetLastError();
+    if (err == cudaSuccess) {
+        t_info.builtin_matmul_calls++;
+        t_info.last_matmul = "builtin-f64";
+        t_info.last_blas_status = 0;
+        t_last_kernel = "dmma-f64-128x128-peer";
+    }
+    return err;
+}
 
 // ============================================================ C ABI
 

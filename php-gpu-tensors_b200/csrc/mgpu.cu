@@ -12,6 +12,7 @@
 // one PyTorch ships, else libnccl.so.2 from the loader path), so the library
 // has no link-time NCCL dependency and single-GPU users never load it.
 #include "gemm_sm100.h"
+#include "internal.h"
 
 #include <nccl.h>
 
@@ -23,8 +24,7 @@
 
 #define PT_API extern "C" __attribute__((visibility("default")))
 
-// Set by the multi-GPU entry points on failure (defined in gemm_sm100.cu).
-void ptg_set_last_status(int code);
+
 
 namespace {
 
@@ -36,6 +36,8 @@ struct NcclApi {
     ncclResult_t (*comm_destroy)(ncclComm_t) = nullptr;
     ncclResult_t (*all_gather)(const void *, void *, size_t, ncclDataType_t, ncclComm_t,
                                cudaStream_t) = nullptr;
+    ncclResult_t (*all_reduce)(const void *, void *, size_t, ncclDataType_t, ncclRedOp_t,
+                               ncclComm_t, cudaStream_t) = nullptr;
 };
 
 NcclApi g_nccl;
@@ -56,8 +58,9 @@ bool nccl()
     g_nccl.comm_init_rank = reinterpret_cast<decltype(g_nccl.comm_init_rank)>(dlsym(h, "ncclCommInitRank"));
     g_nccl.comm_destroy = reinterpret_cast<decltype(g_nccl.comm_destroy)>(dlsym(h, "ncclCommDestroy"));
     g_nccl.all_gather = reinterpret_cast<decltype(g_nccl.all_gather)>(dlsym(h, "ncclAllGather"));
+    g_nccl.all_reduce = reinterpret_cast<decltype(g_nccl.all_reduce)>(dlsym(h, "ncclAllReduce"));
     if (!g_nccl.get_unique_id || !g_nccl.comm_init_rank || !g_nccl.comm_destroy ||
-        !g_nccl.all_gather) {
+        !g_nccl.all_gather || !g_nccl.all_reduce) {
         dlclose(h);
         return false;
     }
@@ -293,4 +296,126 @@ PT_API int gemm_mgpu_nsplit_matmul_noalloc(gemm_mgpu_comm *comm, dtype_t dtype, 
     }
     return gemm_mgpu_nsplit_matmul(comm, dtype, a, a_s0, a_s1, b_local, b_s0, b_s1, c, M, N, K,
                                    scratch, GEMM_MGPU_NSPLIT_SCRATCH_BYTES, stream);
+}
+
+// ---------------------------------------------------------------- fused N-split
+//
+// The N-split product with the exchange inside the GEMM: every rank's result
+// buffer is mapped into every other rank (CUDA IPC over NVLink / NVSwitch), and
+// the epilogue of the rank's column-block product stores each finished output
+// row into all ranks' results directly.  No gather buffer, no permute; the
+// peer stores overlap the remaining tiles' tensor-core work.  A one-element
+// NCCL all-reduce after the kernel orders every rank's stores before any rank
+// goes on to read its result.
+
+struct gemm_mgpu_window {
+    gemm_mgpu_comm *comm;
+    void *local;
+    size_t bytes;
+    void *peer[8];
+    int *sync;   // one int for the completion all-reduce
+};
+
+PT_API int gemm_mgpu_window_create(gemm_mgpu_comm *comm, size_t bytes, gemm_mgpu_window **win,
+                                   void **local)
+{
+    if (!comm || !win || !local || comm->nranks > 8 || bytes == 0 || !nccl()) {
+        ptg_set_last_status(GEMM_SM100_STATUS_NCCL);
+        return 0;
+    }
+    const int G = comm->nranks, rank = comm->rank;
+    gemm_mgpu_window *w = new gemm_mgpu_window();
+    w->comm = comm;
+    w->bytes = bytes;
+    unsigned char *xdev = nullptr;
+    cudaStream_t s = nullptr;
+    cudaIpcMemHandle_t mine;
+    unsigned char all[8 * sizeof(cudaIpcMemHandle_t)];
+    const size_t hb = sizeof(cudaIpcMemHandle_t);
+    bool good = cudaMalloc(&w->local, bytes) == cudaSuccess &&
+                cudaMalloc(&w->sync, 16) == cudaSuccess &&
+                cudaMemset(w->sync, 0, 16) == cudaSuccess &&
+                cudaIpcGetMemHandle(&mine, w->local) == cudaSuccess &&
+                cudaMalloc(&xdev, hb * G) == cudaSuccess &&
+                cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking) == cudaSuccess &&
+                cudaMemcpyAsync(xdev + hb * rank, &mine, hb, cudaMemcpyHostToDevice, s) ==
+                    cudaSuccess;
+    if (good && G > 1)
+        good = g_nccl.all_gather(xdev + hb * rank, xdev, hb, ncclUint8, comm->nccl, s) ==
+               ncclSuccess;
+    good = good && cudaMemcpyAsync(all, xdev, hb * G, cudaMemcpyDeviceToHost, s) == cudaSuccess &&
+           cudaStreamSynchronize(s) == cudaSuccess;
+    for (int g = 0; good && g < G; g++) {
+        if (g == rank) {
+            w->peer[g] = w->local;
+            continue;
+        }
+        cudaIpcMemHandle_t h;
+        std::memcpy(&h, all + hb * g, hb);
+        good = cudaIpcOpenMemHandle(&w->peer[g], h, cudaIpcMemLazyEnablePeerAccess) == cudaSuccess;
+    }
+    if (s) cudaStreamDestroy(s);
+    if (xdev) cudaFree(xdev);
+    if (!good) {
+        ptg_set_last_status(static_cast<int>(cudaGetLastError()));
+        for (int g = 0; g < G; g++)
+            if (g != rank && w->peer[g])
+                cudaIpcCloseMemHandle(w->peer[g]);
+        if (w->local) cudaFree(w->local);
+        if (w->sync) cudaFree(w->sync);
+        delete w;
+        return 0;
+    }
+    *win = w;
+    *local = w->local;
+    return 1;
+}
+
+PT_API void gemm_mgpu_window_destroy(gemm_mgpu_window *win)
+{
+    if (!win)
+        return;
+    cudaDeviceSynchronize();
+    for (int g = 0; g < win->comm->nranks; g++)
+        if (g != win->comm->rank && win->peer[g])
+            cudaIpcCloseMemHandle(win->peer[g]);
+    cudaFree(win->local);
+    cudaFree(win->sync);
+    delete win;
+}
+
+PT_API int gemm_mgpu_nsplit_matmul_fused(gemm_mgpu_window *win, dtype_t dtype, const void *a,
+                                         size_t a_s0, size_t a_s1, const void *b_local,
+                                         size_t b_s0, size_t b_s1, int M, int N, int K,
+                                         cudaStream_t stream)
+{
+    if (!win || dtype != DTYPE_FLOAT64 || M < 0 || N < 0 || K < 0)
+        return 0;
+    gemm_mgpu_comm *comm = win->comm;
+    const int G = comm->nranks;
+    if (N % G != 0 || (N / G) % 2 != 0 ||
+        static_cast<size_t>(M) * static_cast<size_t>(N) * 8 > win->bytes)
+        return 0;
+    if (M == 0 || N == 0)
+        return 1;
+    ptg::F64PeerOut po;
+    std::memset(&po, 0, sizeof(po));
+    for (int g = 0; g < G; g++)
+        po.dst[g] = static_cast<double *>(win->peer[g]);
+    po.ndst = G;
+    po.ldc = N;
+    po.col_off = static_cast<long long>(comm->rank) * (N / G);
+    const cudaError_t err = ptg_launch_f64_peer(
+        static_cast<const double *>(a), a_s0, a_s1, static_cast<const double *>(b_local), b_s0,
+        b_s1, M, N / G, K, po, stream);
+    if (err != cudaSuccess) {
+        ptg_set_last_status(static_cast<int>(err));
+        return 0;
+    }
+    if (G > 1 && g_nccl.all_reduce(win->sync, win->sync, 1, ncclInt32, ncclSum, comm->nccl,
+                                   stream) != ncclSuccess) {
+        ptg_set_last_status(GEMM_SM100_STATUS_NCCL);
+        return 0;
+    }
+    return 1;
 }

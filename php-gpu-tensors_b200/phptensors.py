@@ -125,6 +125,16 @@ _SIGNATURES = {
                                                        ctypes.c_void_p, ctypes.c_int,
                                                        ctypes.c_int, ctypes.c_int,
                                                        ctypes.c_void_p]),
+    "gemm_mgpu_window_create": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_size_t,
+                                               ctypes.POINTER(ctypes.c_void_p),
+                                               ctypes.POINTER(ctypes.c_void_p)]),
+    "gemm_mgpu_window_destroy": (None, [ctypes.c_void_p]),
+    "gemm_mgpu_nsplit_matmul_fused": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int,
+                                                     ctypes.c_void_p, ctypes.c_size_t,
+                                                     ctypes.c_size_t, ctypes.c_void_p,
+                                                     ctypes.c_size_t, ctypes.c_size_t,
+                                                     ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                                     ctypes.c_void_p]),
     "pt_host_matmul": (ctypes.c_int, [ctypes.c_void_p] * 3 + [ctypes.c_int] * 8),
     "pt_host_release": (None, []),
     "pt_last_error": (ctypes.c_char_p, []),
@@ -541,3 +551,52 @@ def nsplit_matmul(comm, a, b_local, N, workspace=None):
         raise RuntimeException("N-split matmul failed (status %d)"
                                % cuda_get_backend_info()["lastBlasStatus"])
     return c
+
+
+class MgpuWindow:
+    """An [M, N] float64 result buffer mapped into every rank (the fused
+    N-split product writes into all of them)."""
+
+    def __init__(self, comm, M, N):
+        lib = library()
+        h, local = ctypes.c_void_p(), ctypes.c_void_p()
+        if not lib.gemm_mgpu_window_create(comm.handle, M * N * 8, ctypes.byref(h),
+                                           ctypes.byref(local)):
+            raise RuntimeException("gemm_mgpu_window_create failed (status %d)"
+                                   % cuda_get_backend_info()["lastBlasStatus"])
+        self.handle, self.local, self.comm, self.M, self.N = h, local.value, comm, M, N
+
+    def result(self):
+        """The window as a torch view (float64 [M, N]); valid after a fused call."""
+        torch = _torch()
+        n = self.M * self.N
+        holder = _CudaPointer(self.local, n * 8)
+        return torch.as_tensor(holder, device="cuda").view(torch.float64)[:n].view(self.M, self.N)
+
+    def close(self):
+        if self.handle:
+            library().gemm_mgpu_window_destroy(self.handle)
+            self.handle = None
+
+
+class _CudaPointer:
+    """__cuda_array_interface__ over raw device memory (bytes)."""
+
+    def __init__(self, ptr, nbytes):
+        self.__cuda_array_interface__ = {"shape": (nbytes,), "typestr": "|u1",
+                                         "data": (ptr, False), "version": 3}
+
+
+def nsplit_matmul_fused(window, a, b_local):
+    """Fused N-split float64 product into `window` (every rank's copy)."""
+    lib = library()
+    M, K = a.getShape()
+    es = 8
+    ok = lib.gemm_mgpu_nsplit_matmul_fused(
+        window.handle, DTYPE_CODES["float64"], a._storage.data_ptr() + a._offset * es,
+        a._strides[0], a._strides[1], b_local._storage.data_ptr() + b_local._offset * es,
+        b_local._strides[0], b_local._strides[1], M, window.N, K, current_stream())
+    if not ok:
+        raise RuntimeException("fused N-split matmul failed (status %d)"
+                               % cuda_get_backend_info()["lastBlasStatus"])
+    return window.result()

@@ -4,9 +4,10 @@ CPU (gloo, world size 2, no GPU calls): batch sharding and N-split column
 ranges tile the work exactly once, the library's N-split workspace size is
 consistent across ranks, and the bench's max-over-ranks timing rule.
 
-GPU: the N-split entry point with one rank equals the plain product bit for
-bit; with two ranks (NCCL all-gather over NVLink) every rank receives the
-full product, again bit-identical to the single-GPU product.
+GPU: the N-split entry points (NCCL all-gather + permute, and the fused
+kernel whose epilogue stores into every rank's window) with one rank equal
+the plain product bit for bit; with two ranks every rank receives the full
+product, again bit-identical to the single-GPU product.
 """
 import os
 import socket
@@ -73,6 +74,28 @@ def test_sharding_and_timing_plumbing_gloo():
 
 
 @pytest.mark.gpu
+def test_fused_nsplit_single_rank_equals_plain_product():
+    sys.path.insert(0, os.path.join(ROOT, "php-gpu-tensors_b200"))
+    import phptensors as P
+    torch.cuda.set_device(0)
+    g = torch.Generator(device="cuda").manual_seed(5)
+    M, N, K = 1000, 640, 776
+    a = torch.rand(M, K, device="cuda", generator=g, dtype=torch.float64) - 0.5
+    b = torch.rand(K, N, device="cuda", generator=g, dtype=torch.float64) - 0.5
+    comm = P.MgpuComm(0, 1)
+    win = P.MgpuWindow(comm, M, N)
+    try:
+        for _ in range(2):
+            c = P.nsplit_matmul_fused(win, P.CudaArray.from_torch(a), P.CudaArray.from_torch(b))
+            ref = P.CudaArray.from_torch(a).matmul(P.CudaArray.from_torch(b), allow_float64=True)
+            torch.cuda.synchronize()
+            assert torch.equal(c, ref.to_torch())
+    finally:
+        win.close()
+        comm.close()
+
+
+@pytest.mark.gpu
 def test_nsplit_single_rank_equals_plain_product():
     sys.path.insert(0, os.path.join(ROOT, "php-gpu-tensors_b200"))
     import phptensors as P
@@ -108,11 +131,18 @@ def _nccl_worker(rank, world, port, q):
         b = torch.rand(K, N, device="cuda", generator=g, dtype=torch.float64) - 0.5
         lo, hi = P.nsplit_columns(N, rank, world)
         comm = P.MgpuComm(rank, world)
-        c = P.nsplit_matmul(comm, P.CudaArray.from_torch(a),
-                            P.CudaArray.from_torch(b[:, lo:hi].contiguous()), N)
+        bl = P.CudaArray.from_torch(b[:, lo:hi].contiguous())
+        c = P.nsplit_matmul(comm, P.CudaArray.from_torch(a), bl, N)
         full = P.CudaArray.from_torch(a).matmul(P.CudaArray.from_torch(b), allow_float64=True)
-        torch.cuda.synchronize()
-        q.put((rank, bool(torch.equal(c.to_torch(), full.to_torch()))))
+        win = P.MgpuWindow(comm, M, N)
+        fused_ok = True
+        for _ in range(2):
+            f = P.nsplit_matmul_fused(win, P.CudaArray.from_torch(a), bl)
+            torch.cuda.synchronize()
+            fused_ok = fused_ok and bool(torch.equal(f, full.to_torch()))
+        dist.barrier()
+        win.close()
+        q.put((rank, bool(torch.equal(c.to_torch(), full.to_torch())) and fused_ok))
     finally:
         if comm is not None:
             comm.close()
