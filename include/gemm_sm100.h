@@ -209,14 +209,16 @@ int cuda_matmul_epilogue_nd_launcher(
 const char *gemm_sm100_last_kernel(void);
 
 /* Grid size (CTAs), CTA size (threads) and cluster size of the last
- * tensor-core launch on this thread (0 before any); any pointer may be NULL. */
+ * tensor-core or few-column launch on this thread (0 before any); any pointer
+ * may be NULL. */
 void gemm_sm100_last_launch(int *grid, int *block, int *cluster);
 
 /* Selects the kernel family for this thread's later launches and returns the
  * previous setting: 0 = automatic, 1 = single-CTA tensor-core kernel whenever
  * the layout allows it (ignoring the size heuristic), 2 = CUDA-core kernel
  * only, 3 = 2-CTA tensor-core kernel for float16/bfloat16 whenever the layout
- * allows it (other dtypes as 1). */
+ * allows it (other dtypes as 1), 4 = few-column split-K CUDA-core kernel
+ * whenever N <= 32 and K >= 128 (otherwise as 0). */
 int gemm_sm100_set_path(int path);
 
 /* Reads (and with clear != 0 resets) the device status word of `device`:

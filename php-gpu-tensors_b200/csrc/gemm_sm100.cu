@@ -17,6 +17,7 @@
 
 #include "gemm_f64.cuh"
 #include "gemm_simt.cuh"
+#include "gemm_skinny.cuh"
 #include "gemm_tc.cuh"
 #include "gemm_tc2.cuh"
 
@@ -43,6 +44,7 @@ enum DType : int { DT_F32 = 0, DT_F16 = 1, DT_BF16 = 2, DT_F64 = 3 };
 
 constexpr int kMaxBatchDims = kSimtMaxBatchDims;
 constexpr double kTcMinWork = 4194304.0;   // M*N*K*batches below this: CUDA-core kernel
+constexpr int kSkinnyMinK = 128;           // shortest K for the few-column kernel
 constexpr double kTuneMinWork = 10000000.0; // matmul_kernels.cu:24 (MATMUL_LT_MIN_WORK)
 
 struct Problem {
@@ -351,6 +353,7 @@ enum KernelId : int {
     KID_F16_PAIR,
     KID_F64_DMMA,
     KID_F64_DMMA_PEER,
+    KID_SKINNY_ASYNC = 16,   // 24 ids: (float64 ? 12 : 0) + 2 * index of NB in {4,8,12,16,24,32} + A k-major
 };
 
 const char *kernel_name(int kid)
@@ -676,6 +679,78 @@ cudaError_t launch_simt(const Problem &P, cudaStream_t stream)
     return cudaGetLastError();
 }
 
+// Few-column products (N <= 32) on the split-K CUDA-core kernel.  The
+// cluster size C (1, 2, 4 or 8 CTAs splitting K) is the smallest that puts
+// about four CTAs on every SM while each CTA keeps at least four chunks.
+template <typename T, int NB>
+cudaError_t launch_skinny_nb(const Problem &P, DeviceState *ds, cudaStream_t stream)
+{
+    const SimtParams s = simt_params(P);
+    SkinnyArgs sa;
+    sa.a_k_major = P.a_sk == 1 && P.a_sm != 1 ? 1 : 0;
+    sa.b_n_major = P.b_sn == 1 ? 1 : 0;
+    const long long m_blocks = (P.M + kSkinnyBM - 1) / kSkinnyBM;
+    const long long zb = std::min<long long>(P.batches, 65535);
+    const long long chunks = (P.K + kSkinnyKC - 1) / kSkinnyKC;
+    const long long target = 4ll * ds->sms;
+    int C = 1;
+    while (C < kSkinnyMaxCluster && m_blocks * zb * C < target && chunks / (2 * C) >= 4)
+        C *= 2;
+    sa.cluster = C;
+    const long long xc = std::min<long long>(m_blocks, 1 << 20);
+    cudaLaunchConfig_t cfg;
+    std::memset(&cfg, 0, sizeof(cfg));
+    cfg.gridDim = dim3(static_cast<unsigned>(xc * C), 1, static_cast<unsigned>(zb));
+    cfg.blockDim = dim3(kSkinnyThreads, 1, 1);
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = static_cast<unsigned>(C);
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = C > 1 ? 1 : 0;
+    cudaError_t err;
+    if constexpr (sizeof(T) >= 4) {
+        // float32 / float64: the cp.async ring variant
+        constexpr int smem = skinny_async_smem_bytes<T, NB>();
+        const int base = KID_SKINNY_ASYNC + (sizeof(T) == 8 ? 12 : 0) + 2 * (NB <= 16 ? NB / 4 - 1 : NB == 24 ? 4 : 5);
+        cfg.dynamicSmemBytes = smem;
+        if (sa.a_k_major) {
+            if (!ensure_smem_attr(ds, base + 1, skinny_async_kernel<T, NB, true>, smem))
+                return cudaErrorInvalidConfiguration;
+            err = cudaLaunchKernelEx(&cfg, skinny_async_kernel<T, NB, true>, s, sa);
+        } else {
+            if (!ensure_smem_attr(ds, base, skinny_async_kernel<T, NB, false>, smem))
+                return cudaErrorInvalidConfiguration;
+            err = cudaLaunchKernelEx(&cfg, skinny_async_kernel<T, NB, false>, s, sa);
+        }
+    } else {
+        err = cudaLaunchKernelEx(&cfg, skinny_gemm_kernel<T, NB>, s, sa);
+    }
+    t_last_grid = static_cast<int>(xc * C);
+    t_last_block = kSkinnyThreads;
+    t_last_cluster = C;
+    return err != cudaSuccess ? err : cudaGetLastError();
+}
+
+// Column padding NB: 4, 8, 12, 16, 24 or 32 for float32/float64; the 16-bit
+// kernel's warp layout needs a power of two.
+template <typename T>
+cudaError_t launch_skinny(const Problem &P, DeviceState *ds, cudaStream_t stream)
+{
+    if (P.N <= 4) return launch_skinny_nb<T, 4>(P, ds, stream);
+    if (P.N <= 8) return launch_skinny_nb<T, 8>(P, ds, stream);
+    if constexpr (sizeof(T) >= 4) {
+        if (P.N <= 12) return launch_skinny_nb<T, 12>(P, ds, stream);
+        if (P.N <= 16) return launch_skinny_nb<T, 16>(P, ds, stream);
+        if (P.N <= 24) return launch_skinny_nb<T, 24>(P, ds, stream);
+    } else {
+        if (P.N <= 16) return launch_skinny_nb<T, 16>(P, ds, stream);
+    }
+    return launch_skinny_nb<T, 32>(P, ds, stream);
+}
+
 const char *family_name(int dt)
 {
     switch (dt) {
@@ -695,6 +770,42 @@ const char *simt_name(int dt)
     }
 }
 
+const char *skinny_name(int dt)
+{
+    switch (dt) {
+    case DT_F32: return "skinny-f32";
+    case DT_F64: return "skinny-f64";
+    case DT_F16: return "skinny-f16";
+    default: return "skinny-bf16";
+    }
+}
+
+// The few-column kernel.  The automatic choice takes it for float32 and
+// float64 whenever N <= 32 and K >= 128 (ahead of 128-column tensor-core
+// tiles that would be three-quarters empty and of the 3xTF32 / DMMA rates),
+// and for float16/bfloat16 only where the tensor-core kernel cannot describe
+// the layout: at full tensor-core rate even a mostly empty tile is faster
+// than the CUDA cores.
+int run_skinny(const Problem &P, DeviceState *ds, cudaStream_t stream)
+{
+    cudaError_t err;
+    switch (P.dt) {
+    case DT_F32: err = launch_skinny<float>(P, ds, stream); break;
+    case DT_F64: err = launch_skinny<double>(P, ds, stream); break;
+    case DT_F16: err = launch_skinny<__half>(P, ds, stream); break;
+    default: err = launch_skinny<__nv_bfloat16>(P, ds, stream); break;
+    }
+    if (err != cudaSuccess) {
+        set_status(static_cast<int>(err));
+        return 0;
+    }
+    t_info.builtin_matmul_calls++;
+    t_info.last_matmul = family_name(P.dt);
+    t_info.last_blas_status = 0;
+    t_last_kernel = skinny_name(P.dt);
+    return 1;
+}
+
 int run(Problem &P, cudaStream_t stream)
 {
     DeviceState *ds = device_state();
@@ -707,6 +818,11 @@ int run(Problem &P, cudaStream_t stream)
     }
     const double work = static_cast<double>(P.M) * P.N * P.K * static_cast<double>(P.batches);
     const bool want_tc = P.K > 0 && t_path != 2 && (t_path == 1 || t_path == 3 || work >= kTcMinWork);
+    const bool skinny_fit = P.N > 0 && P.N <= kSkinnyMaxN && P.M > 0 && P.batches > 0 &&
+                            P.K >= kSkinnyMinK;
+    const bool wide_acc = P.dt == DT_F32 || P.dt == DT_F64;
+    if (skinny_fit && (t_path == 4 || (t_path == 0 && wide_acc)))
+        return run_skinny(P, ds, stream);
     if (want_tc && P.dt == DT_F64 && ds->cc_major == 10) {
         const cudaError_t err = launch_f64_dmma(P, ds, stream);
         if (err != cudaSuccess) {
@@ -732,6 +848,8 @@ int run(Problem &P, cudaStream_t stream)
             return 1;
         }
     }
+    if (skinny_fit && t_path == 0)
+        return run_skinny(P, ds, stream);   // 16-bit layouts TMA cannot describe
     cudaError_t err;
     switch (P.dt) {
     case DT_F32: err = launch_simt<float>(P, stream); break;
@@ -1035,7 +1153,7 @@ PT_API void gemm_sm100_last_launch(int *grid, int *block, int *cluster)
 PT_API int gemm_sm100_set_path(int path)
 {
     const int prev = t_path;
-    if (path >= 0 && path <= 3)
+    if (path >= 0 && path <= 4)
         t_path = path;
     return prev;
 }

@@ -470,13 +470,15 @@ def cuda_tune_matmul(left, right):
 
 def set_kernel_path(path):
     """0 automatic, 1 single-CTA tensor-core kernel whenever the layout allows,
-    2 CUDA cores only, 3 2-CTA tensor-core kernel (16-bit) whenever allowed."""
+    2 CUDA cores only, 3 2-CTA tensor-core kernel (16-bit) whenever allowed,
+    4 few-column split-K kernel whenever N <= 32 and K >= 128."""
     return library().gemm_sm100_set_path(
-        {"auto": 0, "tensor-core": 1, "simt": 2, "tensor-core-pair": 3}[path])
+        {"auto": 0, "tensor-core": 1, "simt": 2, "tensor-core-pair": 3, "skinny": 4}[path])
 
 
 def last_launch():
-    """(grid, block, cluster) of the last tensor-core launch on this thread."""
+    """(grid, block, cluster) of the last tensor-core or few-column launch on
+    this thread."""
     g, b, c = ctypes.c_int(), ctypes.c_int(), ctypes.c_int()
     library().gemm_sm100_last_launch(ctypes.byref(g), ctypes.byref(b), ctypes.byref(c))
     return g.value, b.value, c.value

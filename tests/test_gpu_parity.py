@@ -176,11 +176,18 @@ CASES = [
     ("broadcast_b", [3, 2, 136, 40], [2, 40, 264], False, False, 0),
     ("rank4_transposed", [2, 3, 72, 64], [2, 3, 64, 80], True, True, 0),
     ("long_k", [64, 4104], [4104, 48], False, False, 0),
+    # few columns (N <= 32): the split-K kernel's layouts and ragged chunks
+    ("few_cols", [300, 1000], [1000, 10], False, False, 0),
+    ("few_cols_a_transposed", [200, 2050], [2050, 3], True, False, 0),
+    ("few_cols_b_transposed", [65, 777], [777, 17], False, True, 3),
+    ("few_cols_broadcast", [4, 70, 520], [1, 520, 6], True, False, 0),
 ]
+
+SKINNY_CASES = [c for c in CASES if c[2][-1] <= 32 and c[2][-2] >= 128]
 
 
 @pytest.mark.parametrize("dtype", ["bfloat16", "float16", "float32"])
-@pytest.mark.parametrize("path", ["auto", "tensor-core", "tensor-core-pair"])
+@pytest.mark.parametrize("path", ["auto", "tensor-core", "tensor-core-pair", "skinny"])
 @pytest.mark.parametrize("case", CASES, ids=[c[0] for c in CASES])
 def test_seeded_parity(case, path, dtype):
     name, ashape, bshape, at, bt, pad = case
@@ -194,6 +201,8 @@ def test_seeded_parity(case, path, dtype):
     what = (name, path, P.cuda_get_backend_info()["kernel"])
     if path == "tensor-core-pair" and dtype != "float32" and what[2].startswith("tc"):
         assert what[2].startswith("tc2-"), what
+    if path == "skinny" and case in SKINNY_CASES:
+        assert what[2].startswith("skinny-"), what
     if dtype == "float32":
         check_fp32(c.to_numpy(), a, b, what)
     else:
@@ -317,20 +326,56 @@ def test_autotuning_schema():
     assert t["precision"] == "tf32" and t["candidateCount"] == 2
 
 
+@pytest.mark.parametrize("case", SKINNY_CASES, ids=[c[0] for c in SKINNY_CASES])
+def test_float64_skinny(case):
+    name, ashape, bshape, at, bt, pad = case
+    P.set_kernel_path("skinny")
+    av = O.seeded(ashape, 9, "uniform")
+    bv = O.seeded(bshape, 10, "uniform")
+    a = padded(av, ashape, pad, "float64", at)
+    b = padded(bv, bshape, pad, "float64", bt)
+    c = to_device(a, "float64").matmul(to_device(b, "float64"), allow_float64=True)
+    assert P.cuda_get_backend_info()["kernel"] == "skinny-f64"
+    check_fp64(c.to_numpy(), a, b, name)
+
+
+@pytest.mark.parametrize("dtype", ["bfloat16", "float32", "float64"])
+def test_skinny_split_k_is_deterministic(dtype):
+    """The split-K kernel adds its partial sums in a fixed order: repeated
+    products are bit-identical, whatever the cluster size the launch picks."""
+    P.set_kernel_path("skinny")
+    g = torch.Generator(device="cuda").manual_seed(17)
+    for M, N, K in ((1024, 10, 4096), (4096, 10, 1024), (33, 32, 40000), (5000, 1, 300),
+                    (300, 14, 5000)):
+        a = torch.randn(K, M, device="cuda", generator=g, dtype=torch.float64).to(TORCH_DT[dtype])
+        b = torch.randn(K, N, device="cuda", generator=g, dtype=torch.float64).to(TORCH_DT[dtype])
+        A = P.CudaArray.from_torch(a).transpose()
+        B = P.CudaArray.from_torch(b)
+        first = A.matmul(B, allow_float64=True).to_torch()
+        assert P.cuda_get_backend_info()["kernel"].startswith("skinny-")
+        for _ in range(3):
+            assert torch.equal(A.matmul(B, allow_float64=True).to_torch(), first), (M, N, K)
+        ref = a.double().t() @ b.double()
+        err = ((first.double() - ref).abs().max() / ref.abs().max()).item()
+        assert err <= {"bfloat16": 1e-2, "float32": 1e-5, "float64": 1e-12}[dtype], (M, N, K, err)
+    assert P.device_status() == 0
+
+
 # ------------------------------------------------------------------ epilogue
 @pytest.mark.parametrize("dtype", ["float16", "bfloat16", "float32"])
 @pytest.mark.parametrize("act", ["tanh", "relu", "sigmoid", "none"])
-def test_fused_epilogue_matches_unfused_plan(dtype, act):
+@pytest.mark.parametrize("N", [328, 24])
+def test_fused_epilogue_matches_unfused_plan(dtype, act, N):
     """act(round(A.B) + bias) equals the unfused matmul step followed by the
     elementwise step computed in float (src/fusion_codegen.c:3-27)."""
-    M, K, N = 300, 264, 328
+    M, K = 300, 264
     av = O.seeded([M, K], 21, "uniform", -0.5, 0.5)
     xv = O.seeded([N, K], 22, "uniform", -0.5, 0.5)
     bias = O.seeded([N], 23, "normal", std=0.1)
     a = to_device(O.dense(O.to_storage(av, dtype), [M, K]), dtype)
     x = to_device(O.dense(O.to_storage(xv, dtype), [N, K]), dtype)
     bdev = to_device(O.dense(O.to_storage(bias, dtype), [N]), dtype)
-    for path in ("tensor-core", "simt"):
+    for path in ("tensor-core", "simt") + (("skinny",) if N <= 32 else ()):
         P.set_kernel_path(path)
         fused = a.matmul_epilogue(x.transpose(), bdev, act).to_torch().float()
         plain = a.matmul(x.transpose()).to_torch().float()
