@@ -12,7 +12,7 @@
 //                activation, convert, stage 32x(128 B) boxes in swizzled shared
 //                memory and write them with TMA stores.  Double-buffered TMEM
 //                lets the epilogue of tile i overlap the mainloop of tile i+1.
-//   warps 6..9   (SPLIT3 only) split each FP32 tile into TF32 hi/lo parts so
+//   warps 6..13  (SPLIT3 only) split each FP32 tile into TF32 hi/lo parts so
 //                the MMA warp can issue hi*hi + hi*lo + lo*hi (3xTF32).
 // Tiles (batch, m-block, n-block) are distributed round-robin over a grid of
 // at most one CTA per SM.  Batch is folded into the tile index and into rank-5
@@ -143,18 +143,19 @@ struct TcConfig {
     static constexpr int kEpiChunks = BN / kEpiCols;
     static constexpr int kEpiBufBytes = 32 * 128;         // 32 rows x 128 B
     static constexpr int kEpiWarps = 4;
-    static constexpr int kSplitWarps = kSplit3 ? 4 : 0;
+    static constexpr int kSplitWarps = kSplit3 ? 8 : 0;
     static constexpr int kThreads = 32 * (2 + kEpiWarps + kSplitWarps);
-    // Accumulator columns per tile: 3xTF32 keeps the small cross terms
-    // (hi*lo + lo*hi) in a second accumulator so that the FP32 accumulator of
-    // the dominant hi*hi term sees a third of the per-instruction roundings.
-    static constexpr int kAccCols = (kSplit3 ? 2 : 1) * BN;
-    // 3xTF32: k-blocks accumulated in TMEM before the epilogue drains the
-    // slot into float registers (bounds the accumulator's per-instruction
-    // rounding to 3 * kChunkKB * kKSteps steps per chunk).  Other kinds keep
-    // one slot for the whole tile.
+    static constexpr int kAccCols = BN;
+    // 3xTF32: k-blocks accumulated in a TMEM slot before the epilogue drains
+    // it, with round-to-nearest float adds, into a running total kept in a
+    // third TMEM region (columns [2 * BN, 3 * BN)).  This bounds the tensor
+    // core's per-instruction accumulator rounding to 3 * kChunkKB * kKSteps
+    // steps on a chunk-sized partial sum.  Other kinds keep one slot for the
+    // whole tile.
     static constexpr int kChunkKB = kSplit3 ? 4 : (1 << 30);
-    static constexpr int kTmemCols = 2 * kAccCols;        // double-buffered
+    static constexpr int kTotalCol = 2 * kAccCols;
+    static constexpr int kTmemUsed = (kSplit3 ? 3 : 2) * kAccCols;
+    static constexpr int kTmemCols = kTmemUsed <= 256 ? 256 : 512;   // power of two
     static constexpr int kRingBytes = kStages * kStageBytes;
     static constexpr int kEpiOffset = kRingBytes;
     static constexpr int kBarOffset = kEpiOffset + kEpiWarps * 2 * kEpiBufBytes;
@@ -164,7 +165,7 @@ struct TcConfig {
     static_assert(kStages >= 2, "pipeline needs at least two stages");
     static_assert(BN % kEpiCols == 0, "epilogue box must divide BN");
     static_assert(kSmemBytes <= 232448, "shared memory budget exceeded");
-    static_assert(kTmemCols <= 512, "TMEM holds 512 columns");
+    static_assert(kTmemUsed <= 512, "TMEM holds 512 columns");
 };
 
 __device__ __forceinline__ void decode_batch(long long b, const TcParams &p, int (&c)[3])
@@ -311,7 +312,7 @@ __global__ void __launch_bounds__(TcConfig<IN_KIND, BN, OUT>::kThreads, 1)
             uint32_t phase = 0;
             long long iter = 0;   // accumulator slot uses
             int acc = 0;
-            uint32_t d_tmem = 0, d_small = 0;
+            uint32_t d_tmem = 0;
             bool ok = true;
             const uint32_t smem_base = smem_addr(smem);
             for (long long t = blockIdx.x; ok && t < p.tiles; t += gridDim.x) {
@@ -327,7 +328,6 @@ __global__ void __launch_bounds__(TcConfig<IN_KIND, BN, OUT>::kThreads, 1)
                         }
                         tc_fence_after();
                         d_tmem = tmem_base + static_cast<uint32_t>(acc * Cfg::kAccCols);
-                        d_small = d_tmem + BN;   // 3xTF32 cross terms
                     }
                     uint64_t *gate = Cfg::kSplit3 ? &ready[stage] : &full[stage];
                     if (!mbar_wait(gate, phase, abort)) {
@@ -360,8 +360,8 @@ __global__ void __launch_bounds__(TcConfig<IN_KIND, BN, OUT>::kThreads, 1)
                                     smem_desc(sa + Cfg::kLoadBytes + a_off, a_lbo, a_sbo, a_lay);
                                 const uint64_t bd_lo =
                                     smem_desc(sb + Cfg::kLoadBytes + b_off, b_lbo, b_sbo, b_lay);
-                                umma_tf32(d_small, ad, bd_lo, p.idesc, accumulate);
-                                umma_tf32(d_small, ad_lo, bd, p.idesc, 1);
+                                umma_tf32(d_tmem, ad, bd_lo, p.idesc, 1);
+                                umma_tf32(d_tmem, ad_lo, bd, p.idesc, 1);
                             }
                         } else {
                             umma_f16(d_tmem, ad, bd, p.idesc, accumulate);
@@ -452,12 +452,12 @@ __global__ void __launch_bounds__(TcConfig<IN_KIND, BN, OUT>::kThreads, 1)
             const int row0 = m0 + quad * 32;
             const uint32_t lane_base = tmem_base + (static_cast<uint32_t>(quad * 32) << 16);
             if constexpr (Cfg::kSplit3) {
-                // drain every K chunk into round-to-nearest float registers
-                float accv[BN];
-#pragma unroll
-                for (int i = 0; i < BN; i++)
-                    accv[i] = 0.0f;
+                // Drain every K chunk, adding it with round-to-nearest float
+                // adds into the running total in TMEM; the last chunk's sums
+                // go straight to the output.
+                static_assert(OUT == OUT_F32 && Cfg::kEpiCols == 32, "3xTF32 writes float32");
                 const int nchunks = (p.k_blocks + Cfg::kChunkKB - 1) / Cfg::kChunkKB;
+                const uint32_t t_total = lane_base + static_cast<uint32_t>(Cfg::kTotalCol);
                 for (int ck = 0; ck < nchunks; ck++, iter++) {
                     const int acc = static_cast<int>(iter & 1);
                     const uint32_t acc_phase = static_cast<uint32_t>((iter >> 1) & 1);
@@ -471,35 +471,45 @@ __global__ void __launch_bounds__(TcConfig<IN_KIND, BN, OUT>::kThreads, 1)
                     }
                     tc_fence_after();
                     const uint32_t t_acc = lane_base + static_cast<uint32_t>(acc * Cfg::kAccCols);
-                    uint32_t r32[32];
-#pragma unroll
+                    const bool last = ck == nchunks - 1;
+#pragma unroll 1
                     for (int h = 0; h < BN / 32; h++) {
+                        uint32_t r32[32], t32[32];
                         tmem_ld_32x32b_x32(t_acc + h * 32, r32);
+                        if (ck > 0)
+                            tmem_ld_32x32b_x32(t_total + h * 32, t32);
                         tmem_ld_wait();
+                        float v[32];
 #pragma unroll
                         for (int i = 0; i < 32; i++)
-                            accv[h * 32 + i] += __uint_as_float(r32[i]);
-                        tmem_ld_32x32b_x32(t_acc + BN + h * 32, r32);
-                        tmem_ld_wait();
+                            v[i] = (ck > 0 ? __uint_as_float(t32[i]) : 0.0f) +
+                                   __uint_as_float(r32[i]);
+                        if (!last) {
 #pragma unroll
-                        for (int i = 0; i < 32; i++)
-                            accv[h * 32 + i] += __uint_as_float(r32[i]);
+                            for (int i = 0; i < 32; i++)
+                                t32[i] = __float_as_uint(v[i]);
+                            tmem_st_32x32b_x32(t_total + h * 32, t32);
+                        } else {
+                            if (h == BN / 32 - 1) {
+                                // slot fully read: hand it back to the MMA warp
+                                tc_fence_before();
+                                __syncwarp();
+                                if (lane == 0)
+                                    mbar_arrive(&tempty[acc]);
+                            }
+                            emit(v, n0 + h * 32, row0, c);
+                        }
                     }
-                    tc_fence_before();
-                    __syncwarp();
-                    if (lane == 0)
-                        mbar_arrive(&tempty[acc]);
+                    if (!last) {
+                        tmem_st_wait();
+                        tc_fence_before();
+                        __syncwarp();
+                        if (lane == 0)
+                            mbar_arrive(&tempty[acc]);
+                    }
                 }
                 if (!ok)
                     break;
-#pragma unroll
-                for (int ch = 0; ch < Cfg::kEpiChunks; ch++) {
-                    float v[Cfg::kEpiCols];
-#pragma unroll
-                    for (int i = 0; i < Cfg::kEpiCols; i++)
-                        v[i] = accv[ch * Cfg::kEpiCols + i];
-                    emit(v, n0 + ch * Cfg::kEpiCols, row0, c);
-                }
             } else {
                 const int acc = static_cast<int>(iter & 1);
                 const uint32_t acc_phase = static_cast<uint32_t>((iter >> 1) & 1);
