@@ -46,6 +46,7 @@ constexpr int kMaxBatchDims = kSimtMaxBatchDims;
 constexpr double kTcMinWork = 4194304.0;   // M*N*K*batches below this: CUDA-core kernel
 constexpr int kSkinnyMinK = 128;           // shortest K for the few-column kernel
 constexpr int kStrictMinK = 16;            // shortest K for 3xTF32 (strict float32)
+constexpr int kSplitMinKBlocks = 8;        // k-blocks per split-K rank, at least
 constexpr double kTuneMinWork = 10000000.0; // matmul_kernels.cu:24 (MATMUL_LT_MIN_WORK)
 
 struct Problem {
@@ -395,12 +396,47 @@ cudaError_t launch_tc_kernel(DeviceState *ds, int kid, const CUtensorMap &ma,
     if (!ensure_smem_attr(ds, kid, kernel, Cfg::kSmemBytes))
         return cudaErrorInvalidConfiguration;
     p.status = ds->status;
-    const long long grid = std::min<long long>(p.tiles, ds->sms);
-    kernel<<<static_cast<unsigned>(grid), Cfg::kThreads, Cfg::kSmemBytes, stream>>>(ma, mb, mc, p);
+    // Split-K when the tiles fill less than half of the SMs: the largest G in
+    // {4, 2} whose clusters still fit one CTA per SM, leaving every rank at
+    // least kSplitMinKBlocks k-blocks and a whole number of epilogue boxes.
+    int G = 1;
+    if (p.tiles < ds->sms / 2) {
+        for (int g : {4, 2}) {
+            if (p.tiles * g <= ds->sms && p.k_blocks >= kSplitMinKBlocks * g &&
+                (BN / g) % Cfg::kEpiCols == 0) {
+                G = g;
+                break;
+            }
+        }
+    }
+    p.ksplit = G;
+    long long grid;
+    cudaError_t err;
+    if (G > 1) {
+        grid = p.tiles * G;
+        cudaLaunchAttribute attr;
+        attr.id = cudaLaunchAttributeClusterDimension;
+        attr.val.clusterDim.x = static_cast<unsigned>(G);
+        attr.val.clusterDim.y = 1;
+        attr.val.clusterDim.z = 1;
+        cudaLaunchConfig_t cfg;
+        std::memset(&cfg, 0, sizeof(cfg));
+        cfg.gridDim = dim3(static_cast<unsigned>(grid), 1, 1);
+        cfg.blockDim = dim3(Cfg::kThreads, 1, 1);
+        cfg.dynamicSmemBytes = Cfg::kSmemBytes;
+        cfg.stream = stream;
+        cfg.attrs = &attr;
+        cfg.numAttrs = 1;
+        err = cudaLaunchKernelEx(&cfg, kernel, ma, mb, mc, p);
+    } else {
+        grid = std::min<long long>(p.tiles, ds->sms);
+        kernel<<<static_cast<unsigned>(grid), Cfg::kThreads, Cfg::kSmemBytes, stream>>>(ma, mb, mc, p);
+        err = cudaSuccess;
+    }
     t_last_grid = static_cast<int>(grid);
     t_last_block = Cfg::kThreads;
-    t_last_cluster = 1;
-    return cudaGetLastError();
+    t_last_cluster = G;
+    return err != cudaSuccess ? err : cudaGetLastError();
 }
 
 // Cluster launch of the 2-CTA kernel: at most as many clusters as can be

@@ -15,7 +15,13 @@
 //   warps 6..13  (SPLIT3 only) split each FP32 tile into TF32 hi/lo parts so
 //                the MMA warp can issue hi*hi + hi*lo + lo*hi (3xTF32).
 // Tiles (batch, m-block, n-block) are distributed round-robin over a grid of
-// at most one CTA per SM.  Batch is folded into the tile index and into rank-5
+// at most one CTA per SM.  Split-K (p.ksplit = G > 1, for problems with too
+// few tiles to fill the GPU): a cluster of G CTAs shares one tile, CTA rank r
+// taking the r-th contiguous range of k-blocks.  When its MMAs have drained,
+// each CTA writes its FP32 partial tile into its (now idle) shared-memory
+// ring; after a cluster barrier rank r adds the G partials of its BN/G
+// columns over DSMEM in rank order and runs the epilogue on them, so the
+// result is deterministic and needs no global workspace.  Batch is folded into the tile index and into rank-5
 // tensor maps, so rows past M or columns past N of one batch are clipped by
 // TMA and never touch a neighbouring batch.  Every wait is bounded; a timeout
 // sets the CTA's abort flag and a device status word and the kernel drains
@@ -56,6 +62,7 @@ struct TcParams {
     const void *bias; // [N] in the output dtype, or null
     int act;
     int *status;      // device status word
+    int ksplit;       // CTAs per tile splitting K (cluster size), 1 = none
 };
 
 __device__ __forceinline__ float apply_activation(float v, int act)
@@ -162,6 +169,10 @@ struct TcConfig {
     // full, empty, ready per stage; tmem full/empty x2; drain
     static constexpr int kNumBars = 3 * kStages + 4 + 1;
     static constexpr int kSmemBytes = kBarOffset + kNumBars * 8 + 16 + 1024;
+    // split-K partial tile [BM][BN + 4] floats at the start of the ring (the
+    // 4-float pad keeps 16-byte row accesses of 8 lanes on distinct banks)
+    static constexpr int kPartPitch = BN + 4;
+    static_assert(BM * kPartPitch * 4 <= kRingBytes, "split-K partial tile fits in the ring");
     static_assert(kStages >= 2, "pipeline needs at least two stages");
     static_assert(BN % kEpiCols == 0, "epilogue box must divide BN");
     static_assert(kSmemBytes <= 232448, "shared memory budget exceeded");
@@ -243,6 +254,15 @@ __global__ void __launch_bounds__(TcConfig<IN_KIND, BN, OUT>::kThreads, 1)
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
 
+    // Split-K: this CTA's tile and k-block range (one tile per cluster).
+    const int G = p.ksplit;
+    const int krank = G > 1 ? static_cast<int>(cluster_cta_rank()) : 0;
+    const long long t_first = G > 1 ? blockIdx.x / G : blockIdx.x;
+    const long long t_step = G > 1 ? p.tiles : gridDim.x;
+    const int kb_per = (p.k_blocks + G - 1) / G;
+    const int kb_begin = min(p.k_blocks, krank * kb_per);
+    const int kb_end = min(p.k_blocks, kb_begin + kb_per);
+
     if (warp == 0) {
         // ------------------------------------------------------------ producer
         if (lane == 0) {
@@ -250,7 +270,7 @@ __global__ void __launch_bounds__(TcConfig<IN_KIND, BN, OUT>::kThreads, 1)
             uint32_t phase = 0;
             uint32_t issued_mask = 0, parity_mask = 0;
             bool ok = true;
-            for (long long t = blockIdx.x; ok && t < p.tiles; t += gridDim.x) {
+            for (long long t = t_first; ok && t < p.tiles; t += t_step) {
                 const int nb = static_cast<int>(t % p.n_blocks);
                 const long long r = t / p.n_blocks;
                 const int mb = static_cast<int>(r % p.m_blocks);
@@ -260,7 +280,7 @@ __global__ void __launch_bounds__(TcConfig<IN_KIND, BN, OUT>::kThreads, 1)
                 operand_coords(c, p.a_slot, p.nbd, ca);
                 operand_coords(c, p.b_slot, p.nbd, cb);
                 const int m0 = mb * Cfg::BM, n0 = nb * BN;
-                for (int kb = 0; kb < p.k_blocks; kb++) {
+                for (int kb = kb_begin; kb < kb_end; kb++) {
                     if (!mbar_wait(&empty[stage], phase ^ 1, abort)) {
                         record_failure(abort, p.status, DEV_TIMEOUT_PRODUCER);
                         ok = false;
@@ -315,9 +335,9 @@ __global__ void __launch_bounds__(TcConfig<IN_KIND, BN, OUT>::kThreads, 1)
             uint32_t d_tmem = 0;
             bool ok = true;
             const uint32_t smem_base = smem_addr(smem);
-            for (long long t = blockIdx.x; ok && t < p.tiles; t += gridDim.x) {
-                for (int kb = 0; kb < p.k_blocks; kb++) {
-                    const int kc = kb % Cfg::kChunkKB;
+            for (long long t = t_first; ok && t < p.tiles; t += t_step) {
+                for (int kb = kb_begin; kb < kb_end; kb++) {
+                    const int kc = (kb - kb_begin) % Cfg::kChunkKB;
                     if (kc == 0) {
                         acc = static_cast<int>(iter & 1);
                         const uint32_t acc_phase = static_cast<uint32_t>((iter >> 1) & 1);
@@ -372,7 +392,7 @@ __global__ void __launch_bounds__(TcConfig<IN_KIND, BN, OUT>::kThreads, 1)
                         stage = 0;
                         phase ^= 1;
                     }
-                    if (kc == Cfg::kChunkKB - 1 || kb == p.k_blocks - 1) {
+                    if (kc == Cfg::kChunkKB - 1 || kb == kb_end - 1) {
                         umma_commit(&tfull[acc]);
                         iter++;
                     }
@@ -441,7 +461,18 @@ __global__ void __launch_bounds__(TcConfig<IN_KIND, BN, OUT>::kThreads, 1)
             buf ^= 1;
         };
 
-        for (long long t = blockIdx.x; ok && t < p.tiles; t += gridDim.x) {
+        // Split-K: this thread's row of the partial tile in the ring.
+        float *part_row = reinterpret_cast<float *>(smem) + (quad * 32 + lane) * Cfg::kPartPitch;
+        auto stash = [&](const float (&v)[Cfg::kEpiCols], int col) {
+#pragma unroll
+            for (int i = 0; i < Cfg::kEpiCols / 4; i++)
+                *reinterpret_cast<float4 *>(part_row + col + 4 * i) =
+                    make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+        };
+        int c_last[3] = {0, 0, 0};
+        int n0_last = 0, row0_last = 0;
+
+        for (long long t = t_first; ok && t < p.tiles; t += t_step) {
             const int nb = static_cast<int>(t % p.n_blocks);
             const long long r = t / p.n_blocks;
             const int mb = static_cast<int>(r % p.m_blocks);
@@ -451,12 +482,17 @@ __global__ void __launch_bounds__(TcConfig<IN_KIND, BN, OUT>::kThreads, 1)
             const int m0 = mb * Cfg::BM, n0 = nb * BN;
             const int row0 = m0 + quad * 32;
             const uint32_t lane_base = tmem_base + (static_cast<uint32_t>(quad * 32) << 16);
+            c_last[0] = c[0];
+            c_last[1] = c[1];
+            c_last[2] = c[2];
+            n0_last = n0;
+            row0_last = row0;
             if constexpr (Cfg::kSplit3) {
                 // Drain every K chunk, adding it with round-to-nearest float
                 // adds into the running total in TMEM; the last chunk's sums
                 // go straight to the output.
                 static_assert(OUT == OUT_F32 && Cfg::kEpiCols == 32, "3xTF32 writes float32");
-                const int nchunks = (p.k_blocks + Cfg::kChunkKB - 1) / Cfg::kChunkKB;
+                const int nchunks = (kb_end - kb_begin + Cfg::kChunkKB - 1) / Cfg::kChunkKB;
                 const uint32_t t_total = lane_base + static_cast<uint32_t>(Cfg::kTotalCol);
                 for (int ck = 0; ck < nchunks; ck++, iter++) {
                     const int acc = static_cast<int>(iter & 1);
@@ -497,7 +533,10 @@ __global__ void __launch_bounds__(TcConfig<IN_KIND, BN, OUT>::kThreads, 1)
                                 if (lane == 0)
                                     mbar_arrive(&tempty[acc]);
                             }
-                            emit(v, n0 + h * 32, row0, c);
+                            if (G > 1)
+                                stash(v, h * 32);
+                            else
+                                emit(v, n0 + h * 32, row0, c);
                         }
                     }
                     if (!last) {
@@ -542,9 +581,42 @@ __global__ void __launch_bounds__(TcConfig<IN_KIND, BN, OUT>::kThreads, 1)
                         if (lane == 0)
                             mbar_arrive(&tempty[acc]);
                     }
-                    emit(v, n0 + ch * Cfg::kEpiCols, row0, c);
+                    if (G > 1)
+                        stash(v, ch * Cfg::kEpiCols);
+                    else
+                        emit(v, n0 + ch * Cfg::kEpiCols, row0, c);
                 }
             }
+        }
+        if (G > 1) {
+            // Every rank's partial tile is in its ring; rank r finishes the
+            // columns [r * BN / G, (r + 1) * BN / G) of the tile.
+            cluster_sync();
+            if (ok && t_first < p.tiles) {
+                const uint32_t row_s = smem_addr(part_row);
+                constexpr int kSlice = BN / Cfg::kEpiCols;   // epilogue chunks per tile
+                for (int ch = krank * kSlice / G; ch < (krank + 1) * kSlice / G; ch++) {
+                    float v[Cfg::kEpiCols];
+#pragma unroll
+                    for (int i = 0; i < Cfg::kEpiCols / 4; i++) {
+                        const uint32_t off = static_cast<uint32_t>((ch * Cfg::kEpiCols + 4 * i) * 4);
+                        float4 s = ld_cluster_f4(map_to_cta(row_s + off, 0));
+                        for (int q = 1; q < G; q++) {
+                            const float4 x = ld_cluster_f4(map_to_cta(row_s + off, q));
+                            s.x += x.x;
+                            s.y += x.y;
+                            s.z += x.z;
+                            s.w += x.w;
+                        }
+                        v[4 * i] = s.x;
+                        v[4 * i + 1] = s.y;
+                        v[4 * i + 2] = s.z;
+                        v[4 * i + 3] = s.w;
+                    }
+                    emit(v, n0_last + ch * Cfg::kEpiCols, row0_last, c_last);
+                }
+            }
+            cluster_sync();   // peers are done reading this CTA's partial tile
         }
         if (lane == 0)
             bulk_wait_group<0>();
@@ -556,8 +628,8 @@ __global__ void __launch_bounds__(TcConfig<IN_KIND, BN, OUT>::kThreads, 1)
             int stage = 0;
             uint32_t phase = 0;
             bool ok = true;
-            for (long long t = blockIdx.x; ok && t < p.tiles; t += gridDim.x) {
-                for (int kb = 0; kb < p.k_blocks; kb++) {
+            for (long long t = t_first; ok && t < p.tiles; t += t_step) {
+                for (int kb = kb_begin; kb < kb_end; kb++) {
                     if (!mbar_wait(&full[stage], phase, abort)) {
                         record_failure(abort, p.status, DEV_TIMEOUT_SPLIT);
                         ok = false;
@@ -592,6 +664,11 @@ __global__ void __launch_bounds__(TcConfig<IN_KIND, BN, OUT>::kThreads, 1)
         }
     }
 
+    if (G > 1 && !(warp >= 2 && warp < 2 + Cfg::kEpiWarps)) {
+        // the epilogue warps' two split-K cluster barriers
+        cluster_sync();
+        cluster_sync();
+    }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();

@@ -290,6 +290,17 @@ __device__ __forceinline__ void cluster_sync()
     asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
 }
 
+// 16-byte load from a CTA of the cluster (shared::cluster address from mapa).
+__device__ __forceinline__ float4 ld_cluster_f4(uint32_t cluster_addr)
+{
+    float4 v;
+    asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                 : "r"(cluster_addr)
+                 : "memory");
+    return v;
+}
+
 // Arrive on an mbarrier of another CTA of the cluster (shared::cluster address).
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr)
 {

@@ -361,6 +361,65 @@ def test_skinny_split_k_is_deterministic(dtype):
     assert P.device_status() == 0
 
 
+SPLIT_K_CASES = [
+    # (name, a_shape, b_shape, a_transposed, b_transposed, dtype, expected cluster)
+    ("splitk_fp32_g4", [256, 4096], [4096, 384], False, False, "float32", 4),
+    ("splitk_fp32_batched_t", [3, 200, 2048], [3, 2048, 136], True, True, "float32", 4),
+    ("splitk_fp32_g2", [784, 4096], [4096, 1024], True, False, "float32", 2),
+    ("splitk_bf16_g2", [512, 8192], [8192, 512], False, False, "bfloat16", 2),
+    ("splitk_f16_ragged", [300, 3000], [3000, 200], False, True, "float16", 2),
+]
+
+
+@pytest.mark.parametrize("case", SPLIT_K_CASES, ids=[c[0] for c in SPLIT_K_CASES])
+def test_split_k_tensor_core(case):
+    """Few tiles, long K: a cluster of CTAs splits K and adds the partial
+    tiles over DSMEM in a fixed order -- within the dtype's bound of the
+    oracle, and bit-identical from call to call."""
+    name, ashape, bshape, at, bt, dtype, cluster = case
+    P.set_kernel_path("tensor-core")
+    seed = sum(map(ord, name))
+    a = padded(O.seeded(ashape, seed, "normal"), ashape, 0, dtype, at)
+    b = padded(O.seeded(bshape, seed + 1, "normal"), bshape, 0, dtype, bt)
+    ad, bd = to_device(a, dtype), to_device(b, dtype)
+    c = ad.matmul(bd)
+    what = (name, P.cuda_get_backend_info()["kernel"], P.last_launch())
+    assert what[1].startswith("tc-") and what[2][2] == cluster, what
+    first = c.to_torch().clone()
+    for _ in range(2):
+        assert torch.equal(ad.matmul(bd).to_torch(), first), name
+    M, N = ashape[-2], bshape[-1]
+    rows = [0, M // 2, M - 1]
+    nb = int(np.prod(ashape[:-2])) if len(ashape) > 2 else 1
+    flat = c.to_numpy().reshape(nb, M, N)
+    for bi in range(nb):
+        for r in rows:
+            first_i = (bi * M + r) * N
+            if dtype == "float32":
+                check_fp32(flat[bi, r], a, b, what, first_i, N)
+            else:
+                ref = O.host_matmul_range(a, b, dtype, first_i, N, O.oracle().orc_host_threads())
+                check_close(flat[bi, r], ref, dtype, what)
+    assert P.device_status() == 0
+
+
+def test_split_k_fused_epilogue():
+    """Bias and activation run once, on the reduced tile."""
+    P.set_kernel_path("tensor-core")
+    M, K, N = 256, 4096, 384
+    av = O.seeded([M, K], 31, "uniform", -0.5, 0.5)
+    xv = O.seeded([N, K], 32, "uniform", -0.5, 0.5)
+    bias = O.seeded([N], 33, "normal", std=0.1)
+    a = to_device(O.dense(O.to_storage(av, "float32"), [M, K]), "float32")
+    x = to_device(O.dense(O.to_storage(xv, "float32"), [N, K]), "float32")
+    bdev = to_device(O.dense(O.to_storage(bias, "float32"), [N]), "float32")
+    fused = a.matmul_epilogue(x.transpose(), bdev, "tanh").to_torch()
+    assert P.last_launch()[2] == 4
+    plain = a.matmul(x.transpose()).to_torch()
+    unfused = torch.tanh(plain + bdev.to_torch())
+    assert torch.all((fused - unfused).abs() <= 2.0 ** -22 * unfused.abs().clamp(min=1.0))
+
+
 # ------------------------------------------------------------------ epilogue
 @pytest.mark.parametrize("dtype", ["float16", "bfloat16", "float32"])
 @pytest.mark.parametrize("act", ["tanh", "relu", "sigmoid", "none"])
