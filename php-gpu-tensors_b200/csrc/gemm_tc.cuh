@@ -105,6 +105,82 @@ struct OutTraits<OUT_BF16> {
     }
 };
 
+// Fused epilogue on one warp's row chunk: v[i] is column col0 + i of this
+// lane's row.  The unfused plan's arithmetic: round to the output dtype, add
+// bias[col] in float, apply the activation.  Lane l fetches the bias of
+// columns col0 + l + 32 h (one coalesced load per 32 columns) and the values
+// are broadcast with shuffles; the bias/activation choice is made once per
+// chunk, outside the element loop.
+template <int OUT, int COLS, int ACT, bool BIAS>
+__device__ __forceinline__ void bias_act_chunk(float (&v)[COLS], const float (&bl)[COLS / 32])
+{
+#pragma unroll
+    for (int i = 0; i < COLS; i++) {
+        float x = OutTraits<OUT>::round_trip(v[i]);
+        if constexpr (BIAS)
+            x += __shfl_sync(0xffffffffu, bl[i >> 5], i & 31);
+        if constexpr (ACT == ACT_TANH)
+            x = tanhf(x);
+        else if constexpr (ACT == ACT_RELU)
+            x = x > 0.0f ? x : 0.0f;
+        else if constexpr (ACT == ACT_SIGMOID)
+            x = 1.0f / (1.0f + expf(-x));
+        v[i] = x;
+    }
+}
+
+template <int OUT, int COLS, bool BIAS>
+__device__ __forceinline__ void bias_act_dispatch(float (&v)[COLS], const float (&bl)[COLS / 32],
+                                                  int act)
+{
+    switch (act) {
+    case ACT_TANH: bias_act_chunk<OUT, COLS, ACT_TANH, BIAS>(v, bl); break;
+    case ACT_RELU: bias_act_chunk<OUT, COLS, ACT_RELU, BIAS>(v, bl); break;
+    case ACT_SIGMOID: bias_act_chunk<OUT, COLS, ACT_SIGMOID, BIAS>(v, bl); break;
+    default: bias_act_chunk<OUT, COLS, ACT_NONE, BIAS>(v, bl); break;
+    }
+}
+
+template <int OUT, int COLS>
+__device__ __forceinline__ void apply_epilogue(float (&v)[COLS], const void *bias, int act, int col0,
+                                               int N, int lane)
+{
+    if (bias != nullptr) {
+        float bl[COLS / 32];
+#pragma unroll
+        for (int h = 0; h < COLS / 32; h++) {
+            const int col = col0 + h * 32 + lane;
+            bl[h] = col < N ? OutTraits<OUT>::load(bias, col) : 0.0f;
+        }
+        bias_act_dispatch<OUT, COLS, true>(v, bl, act);
+    } else {
+        const float bl[COLS / 32] = {};
+        bias_act_dispatch<OUT, COLS, false>(v, bl, act);
+    }
+}
+
+// Compact form for the 3xTF32 kernel, whose 448 threads leave 128 registers
+// each (the unrolled variants above spilled there): the same shuffled bias,
+// the activation chosen per element.
+template <int OUT, int COLS>
+__device__ __forceinline__ void apply_epilogue_compact(float (&v)[COLS], const void *bias, int act,
+                                                       int col0, int N, int lane)
+{
+    float bl[COLS / 32];
+#pragma unroll
+    for (int h = 0; h < COLS / 32; h++) {
+        const int col = col0 + h * 32 + lane;
+        bl[h] = bias != nullptr && col < N ? OutTraits<OUT>::load(bias, col) : 0.0f;
+    }
+#pragma unroll
+    for (int i = 0; i < COLS; i++) {
+        float x = OutTraits<OUT>::round_trip(v[i]);
+        if (bias != nullptr)
+            x += __shfl_sync(0xffffffffu, bl[i >> 5], i & 31);
+        v[i] = apply_activation(x, act);
+    }
+}
+
 __device__ __forceinline__ uint32_t pack2(float lo, float hi, int out)
 {
     if (out == OUT_F16) {
@@ -417,17 +493,10 @@ __global__ void __launch_bounds__(TcConfig<IN_KIND, BN, OUT>::kThreads, 1)
         // one 32-row x 128-byte box of this warp's rows.
         auto emit = [&](float (&v)[Cfg::kEpiCols], int col0, int row0, const int (&c)[3]) {
             if (p.bias != nullptr || p.act != ACT_NONE) {
-                // Same arithmetic as the unfused plan: the matmul result is
-                // rounded to the output dtype, then bias add and activation
-                // run in float and round once.
-#pragma unroll
-                for (int i = 0; i < Cfg::kEpiCols; i++) {
-                    float x = OutTraits<OUT>::round_trip(v[i]);
-                    const int col = col0 + i;
-                    if (p.bias != nullptr && col < p.N)
-                        x += OutTraits<OUT>::load(p.bias, col);
-                    v[i] = apply_activation(x, p.act);
-                }
+                if constexpr (Cfg::kSplit3)
+                    apply_epilogue_compact<OUT, Cfg::kEpiCols>(v, p.bias, p.act, col0, p.N, lane);
+                else
+                    apply_epilogue<OUT, Cfg::kEpiCols>(v, p.bias, p.act, col0, p.N, lane);
             }
             uint8_t *sbuf = stage_buf + buf * Cfg::kEpiBufBytes;
             if (lane == 0)

@@ -286,16 +286,8 @@ __global__ void __launch_bounds__(Tc2Config<IN_KIND, OUT>::kThreads, 1)
                         mbar_arrive_cluster(map_to_cta(smem_addr(&tempty[acc]), 0));
                 }
                 const int col0 = n0 + ch * Cfg::kEpiCols;
-                if (p.bias != nullptr || p.act != ACT_NONE) {
-#pragma unroll
-                    for (int i = 0; i < Cfg::kEpiCols; i++) {
-                        float x = OutTraits<OUT>::round_trip(v[i]);
-                        const int col = col0 + i;
-                        if (p.bias != nullptr && col < p.N)
-                            x += OutTraits<OUT>::load(p.bias, col);
-                        v[i] = apply_activation(x, p.act);
-                    }
-                }
+                if (p.bias != nullptr || p.act != ACT_NONE)
+                    apply_epilogue<OUT, Cfg::kEpiCols>(v, p.bias, p.act, col0, p.N, lane);
                 uint8_t *sbuf = stage_buf + buf * Cfg::kEpiBufBytes;
                 if (lane == 0)
                     bulk_wait_group_read<1>();
