@@ -412,27 +412,23 @@ cudaError_t launch_tc_kernel(DeviceState *ds, int kid, const CUtensorMap &ma,
     p.ksplit = G;
     long long grid;
     cudaError_t err;
-    if (G > 1) {
-        grid = p.tiles * G;
-        cudaLaunchAttribute attr;
-        attr.id = cudaLaunchAttributeClusterDimension;
-        attr.val.clusterDim.x = static_cast<unsigned>(G);
-        attr.val.clusterDim.y = 1;
-        attr.val.clusterDim.z = 1;
-        cudaLaunchConfig_t cfg;
-        std::memset(&cfg, 0, sizeof(cfg));
-        cfg.gridDim = dim3(static_cast<unsigned>(grid), 1, 1);
-        cfg.blockDim = dim3(Cfg::kThreads, 1, 1);
-        cfg.dynamicSmemBytes = Cfg::kSmemBytes;
-        cfg.stream = stream;
-        cfg.attrs = &attr;
-        cfg.numAttrs = 1;
-        err = cudaLaunchKernelEx(&cfg, kernel, ma, mb, mc, p);
-    } else {
-        grid = std::min<long long>(p.tiles, ds->sms);
-        kernel<<<static_cast<unsigned>(grid), Cfg::kThreads, Cfg::kSmemBytes, stream>>>(ma, mb, mc, p);
-        err = cudaSuccess;
-    }
+    grid = G > 1 ? p.tiles * G : std::min<long long>(p.tiles, ds->sms);
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = static_cast<unsigned>(G);
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
+    cudaLaunchConfig_t cfg;
+    std::memset(&cfg, 0, sizeof(cfg));
+    cfg.gridDim = dim3(static_cast<unsigned>(grid), 1, 1);
+    cfg.blockDim = dim3(Cfg::kThreads, 1, 1);
+    cfg.dynamicSmemBytes = Cfg::kSmemBytes;
+    cfg.stream = stream;
+    cfg.attrs = attr;
+    cfg.numAttrs = G > 1 ? 2 : 1;
+    err = cudaLaunchKernelEx(&cfg, kernel, ma, mb, mc, p);
     t_last_grid = static_cast<int>(grid);
     t_last_block = Cfg::kThreads;
     t_last_cluster = G;
@@ -450,17 +446,19 @@ cudaError_t launch_tc2_kernel(DeviceState *ds, int kid, int slot, const CUtensor
     auto kernel = tc2_gemm_kernel<IN, OUT>;
     if (!ensure_smem_attr(ds, kid, kernel, Cfg::kSmemBytes))
         return cudaErrorInvalidConfiguration;
-    cudaLaunchAttribute attr;
-    attr.id = cudaLaunchAttributeClusterDimension;
-    attr.val.clusterDim.x = 2;
-    attr.val.clusterDim.y = 1;
-    attr.val.clusterDim.z = 1;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
     cudaLaunchConfig_t cfg = {};
     cfg.blockDim = dim3(Cfg::kThreads);
     cfg.dynamicSmemBytes = Cfg::kSmemBytes;
     cfg.stream = stream;
-    cfg.attrs = &attr;
-    cfg.numAttrs = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 2;
     int clusters = 0;
     {
         std::lock_guard<std::mutex> lock(g_mutex);

@@ -329,6 +329,12 @@ __global__ void __launch_bounds__(TcConfig<IN_KIND, BN, OUT>::kThreads, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
+    // Setup above overlaps the previous kernel's tail (programmatic dependent
+    // launch); global memory is touched only after it has completed.  Every
+    // CTA of this grid is resident from the start, so letting the next launch
+    // begin its setup now cannot starve this grid of SMs.
+    grid_dependency_wait();
+    grid_launch_dependents();
 
     // Split-K: this CTA's tile and k-block range (one tile per cluster).
     const int G = p.ksplit;

@@ -118,6 +118,9 @@ __global__ void __launch_bounds__(Tc2Config<IN_KIND, OUT>::kThreads, 1)
     cluster_sync();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
+    // programmatic dependent launch, as in tc_gemm_kernel
+    grid_dependency_wait();
+    grid_launch_dependents();
 
     if (warp == 0) {
         // ------------------------------------------------------------ producer (both CTAs)

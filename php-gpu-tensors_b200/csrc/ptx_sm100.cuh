@@ -269,6 +269,23 @@ __device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t lbo_bytes
 
 namespace ptg {
 
+// ---------------------------------------------------------------- launch overlap
+// Programmatic dependent launch: wait until the grids this launch depends on
+// (the previous kernel in the stream) have completed and their writes are
+// visible; a no-op when the launch did not ask for overlap.
+__device__ __forceinline__ void grid_dependency_wait()
+{
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
+// Lets the next kernel in the stream (if it was launched with programmatic
+// stream serialization) begin its own setup as SMs free up; it still waits
+// for this grid's completion before touching memory.
+__device__ __forceinline__ void grid_launch_dependents()
+{
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // ---------------------------------------------------------------- clusters
 __device__ __forceinline__ uint32_t cluster_cta_rank()
 {
