@@ -175,6 +175,23 @@ int cuda_low_precision_matmul_nd_launcher(
 #define GEMM_SM100_STATUS_NCCL 9004        /* NCCL failure (multi-GPU entry points) */
 #define GEMM_SM100_STATUS_SCRATCH_LIMIT 9005 /* product larger than the library-owned buffer */
 
+/* float32 C = A.B where A and B are float32, float16 or bfloat16 (not float16
+ * with bfloat16), with the batched launcher's shape/broadcast rules: the
+ * gradient products of the autograd matmul node for 16-bit operands
+ * (src/autograd.c:1547-1577 computes them in float32 on float32 copies made by
+ * gradient_cast, src/autograd.c:683-712).  No copy is made here: a 16-bit
+ * operand is read as it is, and with a float32 operand on the other side the
+ * tensor-core kernel splits the float32 tile into three bfloat16 parts
+ * (hi + mid + lo, 24+ significant bits) and accumulates the three exact
+ * bf16 x bf16 products in float32.  float32 x float16 runs on the CUDA cores.
+ * Returns 1 / 0 like the other launchers.  No counterpart in the reference. */
+int cuda_mixed_matmul_nd_launcher(const void *a, dtype_t a_dtype, const void *b,
+                                  dtype_t b_dtype, float *c,
+                                  int *shape_a, size_t *stride_a, int nd_a,
+                                  int *shape_b, size_t *stride_b, int nd_b,
+                                  int *shape_c, size_t *stride_c, int nd_c,
+                                  cudaStream_t stream);
+
 /* FP64 C = A.B with the batched launcher's shape/broadcast rules.  New scope:
  * the reference rejects float64 matmul (src/cuda_array/ca_private.c:1099-1106). */
 int cuda_f64_matmul_nd_launcher(

@@ -73,12 +73,20 @@ int pt_tensor_matmul(const pt_tensor *a, const pt_tensor *b, pt_tensor *result, 
 /* Frees a tensor allocated by pt_tensor_matmul (cudaFreeAsync on stream). */
 void pt_tensor_release(pt_tensor *t, cudaStream_t stream);
 
-/* The two GEMMs of the matmul backward node (src/autograd.c:1552-1577) for
- * float32 operands: grad_a = grad_c . B^T and grad_b = A^T . grad_c, with B^T
- * and A^T taken as zero-copy transposed views (last two axes swapped), into
- * preallocated contiguous results of the shapes those products have (the
- * batch-broadcast shape; the un-broadcast reduction is the caller's, as in
- * src/autograd.c:714-760).  Either result may be NULL to skip that GEMM. */
+/* The two GEMMs of the matmul backward node (src/autograd.c:1539-1585):
+ * grad_a = grad_c . B^T and grad_b = A^T . grad_c, with B^T and A^T taken as
+ * zero-copy transposed views (last two axes swapped).  A and B are float32,
+ * float16 or bfloat16 (the same type); grad_c is float32 or their type; the
+ * results are float32 (the reference's gradient dtype for 16-bit operands,
+ * src/autograd.c:1547-1548), computed without the float32 copies the
+ * reference makes (gradient_cast): cuda_mixed_matmul_nd_launcher reads the
+ * 16-bit operands as they are.  Each result has either the batch-broadcast
+ * shape of its product, or the shape of its operand when the product
+ * broadcast that operand (src/autograd.c:714-760, gradient_unbroadcast):
+ * the sum over the broadcast axes is then fused -- one GEMM over the folded
+ * (batch..., inner) axis when the tensors' strides allow it, otherwise a
+ * scratch product and a fixed-order reduction.  Either result may be NULL to
+ * skip that GEMM. */
 int pt_tensor_matmul_backward(const pt_tensor *a, const pt_tensor *b, const pt_tensor *grad_c,
                               const pt_tensor *grad_a, const pt_tensor *grad_b,
                               cudaStream_t stream);

@@ -94,8 +94,10 @@ __device__ __forceinline__ double apply_activation_d(double v, int act)
 constexpr int kSimtTile = 64;
 constexpr int kSimtBK = 16;
 
-// 16x16 threads, 64x64 output tile, 4x4 outputs per thread.
-template <typename T>
+// 16x16 threads, 64x64 output tile, 4x4 outputs per thread.  TA / TB are the
+// operand element types (widened to the result's accumulator type on load),
+// T the result's.
+template <typename T, typename TA = T, typename TB = T>
 __global__ void __launch_bounds__(256) simt_gemm_kernel(const SimtParams p)
 {
     using E = Elem<T>;
@@ -131,11 +133,11 @@ __global__ void __launch_bounds__(256) simt_gemm_kernel(const SimtParams p)
                 const int e = threadIdx.x + 256 * r;    // 0..1023
                 const int row = e >> 4, kk = e & 15;    // A: 64 rows x 16 k
                 const int m = m0 + row, k = k0 + kk;
-                sa[kk][row] = (m < p.M && k < p.K) ? Acc(E::load(p.a, oa + m * p.a_sm + k * p.a_sk))
+                sa[kk][row] = (m < p.M && k < p.K) ? Acc(Elem<TA>::load(p.a, oa + m * p.a_sm + k * p.a_sk))
                                                    : Acc(0);
                 const int kr = e >> 6, col = e & 63;    // B: 16 k x 64 cols
                 const int n = n0 + col, kb = k0 + kr;
-                sb[kr][col] = (n < p.N && kb < p.K) ? Acc(E::load(p.b, ob + kb * p.b_sk + n * p.b_sn))
+                sb[kr][col] = (n < p.N && kb < p.K) ? Acc(Elem<TB>::load(p.b, ob + kb * p.b_sk + n * p.b_sn))
                                                     : Acc(0);
             }
             __syncthreads();

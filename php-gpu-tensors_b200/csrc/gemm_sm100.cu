@@ -64,6 +64,8 @@ struct Problem {
     const void *bias;
     int act;
     int forced_bn;                 // 0 = heuristic / tuned plan
+    int a_dt, b_dt;                // operand dtypes (dt is the result's; they differ only
+                                   // for the float32-result gradient products)
 };
 
 // ------------------------------------------------------------ thread state
@@ -166,6 +168,8 @@ int build_problem(int dt, const void *a, const void *b, void *c, const int *sa, 
         return 0;
     std::memset(P, 0, sizeof(*P));
     P->dt = dt;
+    P->a_dt = dt;
+    P->b_dt = dt;
     P->a = a;
     P->b = b;
     P->c = c;
@@ -356,6 +360,10 @@ enum KernelId : int {
     KID_F64_DMMA,
     KID_F64_DMMA_PEER,
     KID_SKINNY_ASYNC = 16,   // 24 ids: (float64 ? 12 : 0) + 2 * index of NB in {4,8,12,16,24,32} + A k-major
+    KID_MIX_A = 40,          // float32 A (split into 3 bf16) x bf16 B -> float32
+    KID_MIX_B,               // bf16 A x float32 B -> float32
+    KID_BF16_F32,            // bf16 x bf16 -> float32
+    KID_F16_F32,             // f16 x f16 -> float32
 };
 
 const char *kernel_name(int kid)
@@ -371,6 +379,10 @@ const char *kernel_name(int kid)
     case KID_BF16_PAIR: return "tc2-bf16-256x256";
     case KID_F16_PAIR: return "tc2-f16-256x256";
     case KID_F64_DMMA: return "dmma-f64-128x128";
+    case KID_MIX_A: return "tc-f32xbf16-bf16x3-128x128";
+    case KID_MIX_B: return "tc-bf16xf32-bf16x3-128x128";
+    case KID_BF16_F32: return "tc-bf16-f32out-128x128";
+    case KID_F16_F32: return "tc-f16-f32out-128x128";
     default: return "tc-unknown";
     }
 }
@@ -501,7 +513,16 @@ int try_tc(const Problem &P, DeviceState *ds, cudaStream_t stream, int *kid_out)
 {
     if (P.dt == DT_F64 || ds->cc_major != 10 || !g_encode)
         return 0;
-    const int es = element_bytes(P.dt);
+    // Gradient products with a float32 result from 16-bit operand(s): the
+    // MMA runs on the 16-bit type; a float32 operand (mix_side 0 = A, 1 = B)
+    // is split into three bf16 parts by the kernel.
+    const bool wide_out = P.a_dt != P.dt || P.b_dt != P.dt;
+    const int op_dt = !wide_out ? P.dt : (P.a_dt != DT_F32 ? P.a_dt : P.b_dt);
+    const int mix_side = !wide_out ? -1 : (P.a_dt == DT_F32 ? 0 : (P.b_dt == DT_F32 ? 1 : -1));
+    if (wide_out && (P.K < kStrictMinK || (mix_side >= 0 && op_dt != DT_BF16) ||
+                     (mix_side < 0 && P.a_dt != P.b_dt)))
+        return 0;
+    const int es = element_bytes(op_dt);
     TcBatch tb;
     if (!merge_batches(P, &tb))
         return 0;
@@ -527,7 +548,7 @@ int try_tc(const Problem &P, DeviceState *ds, cudaStream_t stream, int *kid_out)
 
     // kernel selection
     int kid;
-    const bool fp32 = P.dt == DT_F32;
+    const bool fp32 = P.dt == DT_F32 && !wide_out;
     // 3xTF32 drops lo*lo and rounds lo to TF32: up to about 12 float32 ulps
     // per product, inside the K-ulp float32 dot-product bound only from K = 12
     // on.  Shorter inner axes run the exact-fma CUDA-core kernel.
@@ -553,9 +574,14 @@ int try_tc(const Problem &P, DeviceState *ds, cudaStream_t stream, int *kid_out)
         const long long tiles_pair = P.batches * ((P.M + 255) / 256) * ((P.N + 255) / 256);
         pair = t_path == 3 || (t_path != 1 && tiles_pair >= ds->sms / 2);
     }
+    if (wide_out)
+        bn = 128, pair = false;
     if (pair)
         bn = 256;
-    if (fp32)
+    if (wide_out)
+        kid = mix_side == 0 ? KID_MIX_A
+                            : mix_side == 1 ? KID_MIX_B : (op_dt == DT_BF16 ? KID_BF16_F32 : KID_F16_F32);
+    else if (fp32)
         kid = t_precision == CUDA_MATMUL_PRECISION_FP32_STRICT ? KID_F32X3_128
                                                                 : (bn == 256 ? KID_TF32_256 : KID_TF32_128);
     else if (P.dt == DT_BF16)
@@ -565,7 +591,7 @@ int try_tc(const Problem &P, DeviceState *ds, cudaStream_t stream, int *kid_out)
 
     const int bk = 128 / es;            // K elements per stage
     const int chunk = 128 / es;         // MN elements per 128-byte row
-    const int out_es = fp32 ? 4 : 2;
+    const int out_es = P.dt == DT_F32 ? 4 : 2;
     const int epi_cols = 128 / out_es;
 
     TcParams p;
@@ -602,13 +628,22 @@ int try_tc(const Problem &P, DeviceState *ds, cudaStream_t stream, int *kid_out)
     add_batch_dims(mc, tb, tb.c, c_slot);
 
     // TF32 operands stored MN-major need the 32-byte-atom 128-byte swizzle
-    const CUtensorMapSwizzle sw_a = (fp32 && a_mn) ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B
-                                                   : CU_TENSOR_MAP_SWIZZLE_128B;
-    const CUtensorMapSwizzle sw_b = (fp32 && b_mn) ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B
-                                                   : CU_TENSOR_MAP_SWIZZLE_128B;
+    CUtensorMapSwizzle sw_a = (fp32 && a_mn) ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B
+                                             : CU_TENSOR_MAP_SWIZZLE_128B;
+    CUtensorMapSwizzle sw_b = (fp32 && b_mn) ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B
+                                             : CU_TENSOR_MAP_SWIZZLE_128B;
+    // The float32 operand of a mixed product lands as one unswizzled box of
+    // 128 rows (or columns) x bk K: the kernel's split warps read it.
+    if (mix_side == 0) {
+        sw_a = CU_TENSOR_MAP_SWIZZLE_NONE;
+        if (!a_mn) { box_a[0] = bk; box_a[1] = 128; } else { box_a[0] = 128; box_a[1] = bk; }
+    } else if (mix_side == 1) {
+        sw_b = CU_TENSOR_MAP_SWIZZLE_NONE;
+        if (!b_mn) { box_b[0] = bk; box_b[1] = 128; } else { box_b[0] = 128; box_b[1] = bk; }
+    }
     CUtensorMap tma_a, tma_b, tma_c;
-    if (!encode_map(&tma_a, P.dt, P.a, ma, box_a, sw_a) ||
-        !encode_map(&tma_b, P.dt, P.b, mb, box_b, sw_b) ||
+    if (!encode_map(&tma_a, P.a_dt, P.a, ma, box_a, sw_a) ||
+        !encode_map(&tma_b, P.b_dt, P.b, mb, box_b, sw_b) ||
         !encode_map(&tma_c, P.dt, P.c, mc, box_c))
         return 0;
 
@@ -624,7 +659,7 @@ int try_tc(const Problem &P, DeviceState *ds, cudaStream_t stream, int *kid_out)
         p.bshape[d] = tb.bshape[d];
     p.a_mn_major = a_mn;
     p.b_mn_major = b_mn;
-    const int fmt = fp32 ? 2 : (P.dt == DT_BF16 ? 1 : 0);
+    const int fmt = fp32 ? 2 : (op_dt == DT_BF16 ? 1 : 0);
     p.idesc = make_idesc(fmt, a_mn, b_mn, bn, pair ? 256 : 128);
     p.bias = P.bias;
     p.act = P.act;
@@ -639,6 +674,10 @@ int try_tc(const Problem &P, DeviceState *ds, cudaStream_t stream, int *kid_out)
     case KID_TF32_256: err = launch_tc_kernel<IN_TF32, 256, OUT_F32>(ds, kid, tma_a, tma_b, tma_c, p, stream); break;
     case KID_BF16_PAIR: err = launch_tc2_kernel<IN_BF16, OUT_BF16>(ds, kid, 0, tma_a, tma_b, tma_c, p, stream); break;
     case KID_F16_PAIR: err = launch_tc2_kernel<IN_F16, OUT_F16>(ds, kid, 1, tma_a, tma_b, tma_c, p, stream); break;
+    case KID_MIX_A: err = launch_tc_kernel<IN_MIX_A, 128, OUT_F32>(ds, kid, tma_a, tma_b, tma_c, p, stream); break;
+    case KID_MIX_B: err = launch_tc_kernel<IN_MIX_B, 128, OUT_F32>(ds, kid, tma_a, tma_b, tma_c, p, stream); break;
+    case KID_BF16_F32: err = launch_tc_kernel<IN_BF16, 128, OUT_F32>(ds, kid, tma_a, tma_b, tma_c, p, stream); break;
+    case KID_F16_F32: err = launch_tc_kernel<IN_F16, 128, OUT_F32>(ds, kid, tma_a, tma_b, tma_c, p, stream); break;
     default: err = launch_tc_kernel<IN_F32X3, 128, OUT_F32>(ds, kid, tma_a, tma_b, tma_c, p, stream); break;
     }
     if (err != cudaSuccess) {
@@ -706,7 +745,7 @@ SimtParams simt_params(const Problem &P)
     return s;
 }
 
-template <typename T>
+template <typename T, typename TA = T, typename TB = T>
 cudaError_t launch_simt(const Problem &P, cudaStream_t stream)
 {
     const SimtParams s = simt_params(P);
@@ -715,7 +754,7 @@ cudaError_t launch_simt(const Problem &P, cudaStream_t stream)
     dim3 grid(static_cast<unsigned>(std::min<long long>(nb, 2147483647ll)),
               static_cast<unsigned>(std::min<long long>(mb, 65535)),
               static_cast<unsigned>(std::min<long long>(P.batches, 65535)));
-    simt_gemm_kernel<T><<<grid, 256, 0, stream>>>(s);
+    simt_gemm_kernel<T, TA, TB><<<grid, 256, 0, stream>>>(s);
     return cudaGetLastError();
 }
 
@@ -858,8 +897,9 @@ int run(Problem &P, cudaStream_t stream)
     }
     const double work = static_cast<double>(P.M) * P.N * P.K * static_cast<double>(P.batches);
     const bool want_tc = P.K > 0 && t_path != 2 && (t_path == 1 || t_path == 3 || work >= kTcMinWork);
-    const bool skinny_fit = P.N > 0 && P.N <= kSkinnyMaxN && P.M > 0 && P.batches > 0 &&
-                            P.K >= kSkinnyMinK;
+    const bool wide_out = P.a_dt != P.dt || P.b_dt != P.dt;   // float32 result, 16-bit operand(s)
+    const bool skinny_fit = !wide_out && P.N > 0 && P.N <= kSkinnyMaxN && P.M > 0 &&
+                            P.batches > 0 && P.K >= kSkinnyMinK;
     const bool wide_acc = P.dt == DT_F32 || P.dt == DT_F64;
     if (skinny_fit && (t_path == 4 || (t_path == 0 && wide_acc)))
         return run_skinny(P, ds, stream);
@@ -891,7 +931,19 @@ int run(Problem &P, cudaStream_t stream)
     if (skinny_fit && t_path == 0)
         return run_skinny(P, ds, stream);   // 16-bit layouts TMA cannot describe
     cudaError_t err;
-    switch (P.dt) {
+    if (wide_out) {
+        // float32 result: each operand widened to float on load
+        auto code = [](int dt) { return dt == DT_F32 ? 0 : (dt == DT_BF16 ? 1 : 2); };
+        switch (code(P.a_dt) * 3 + code(P.b_dt)) {
+        case 1: err = launch_simt<float, float, __nv_bfloat16>(P, stream); break;
+        case 2: err = launch_simt<float, float, __half>(P, stream); break;
+        case 3: err = launch_simt<float, __nv_bfloat16, float>(P, stream); break;
+        case 4: err = launch_simt<float, __nv_bfloat16, __nv_bfloat16>(P, stream); break;
+        case 6: err = launch_simt<float, __half, float>(P, stream); break;
+        case 8: err = launch_simt<float, __half, __half>(P, stream); break;
+        default: err = cudaErrorInvalidValue; break;
+        }
+    } else switch (P.dt) {
     case DT_F32: err = launch_simt<float>(P, stream); break;
     case DT_F64: err = launch_simt<double>(P, stream); break;
     case DT_F16: err = launch_simt<__half>(P, stream); break;
@@ -936,6 +988,61 @@ int nd_entry(int dt, const void *a, const void *b, void *c, int *shape_a, size_t
 }
 
 } // namespace
+
+namespace {
+
+// One thread per kept element; the reduced coordinates are walked in
+// row-major order.
+__global__ void reduce_axes_kernel(const float *__restrict__ src, float *__restrict__ dst,
+                                   const PtgReduceDims d, long long kept_total,
+                                   long long red_total)
+{
+    long long src_stride[10];
+    long long s = 1;
+    for (int i = d.n - 1; i >= 0; i--) {
+        src_stride[i] = s;
+        s *= d.ext[i];
+    }
+    for (long long j = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x;
+         j < kept_total; j += static_cast<long long>(gridDim.x) * blockDim.x) {
+        long long rem = j, src_off = 0, dst_off = 0;
+        for (int i = d.n - 1; i >= 0; i--) {
+            if (!d.keep[i])
+                continue;
+            const long long c = rem % d.ext[i];
+            rem /= d.ext[i];
+            src_off += c * src_stride[i];
+            dst_off += c * d.dst_stride[i];
+        }
+        float acc = 0.0f;
+        for (long long r = 0; r < red_total; r++) {
+            long long rr = r, off = 0;
+            for (int i = d.n - 1; i >= 0; i--) {
+                if (d.keep[i])
+                    continue;
+                off += (rr % d.ext[i]) * src_stride[i];
+                rr /= d.ext[i];
+            }
+            acc += src[src_off + off];
+        }
+        dst[dst_off] = acc;
+    }
+}
+
+} // namespace
+
+cudaError_t ptg_reduce_axes(const float *src, float *dst, const PtgReduceDims &d,
+                            cudaStream_t stream)
+{
+    long long kept = 1, red = 1;
+    for (int i = 0; i < d.n; i++)
+        (d.keep[i] ? kept : red) *= d.ext[i];
+    if (kept == 0)
+        return cudaSuccess;
+    const long long blocks = std::min<long long>((kept + 255) / 256, 148ll * 16);
+    reduce_axes_kernel<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(src, dst, d, kept, red);
+    return cudaGetLastError();
+}
 
 // Internal (hidden) hook for the other translation units of the library.
 void ptg_set_last_status(int code) { set_status(code); }
@@ -1059,6 +1166,30 @@ PT_API int cuda_f64_matmul_nd_launcher(double *a, double *b, double *c, int *sha
 {
     return nd_entry(DT_F64, a, b, c, shape_a, stride_a, nd_a, shape_b, stride_b, nd_b, shape_c,
                     stride_c, nd_c, nullptr, ACT_NONE, stream);
+}
+
+PT_API int cuda_mixed_matmul_nd_launcher(const void *a, dtype_t a_dtype, const void *b,
+                                         dtype_t b_dtype, float *c, int *shape_a,
+                                         size_t *stride_a, int nd_a, int *shape_b,
+                                         size_t *stride_b, int nd_b, int *shape_c,
+                                         size_t *stride_c, int nd_c, cudaStream_t stream)
+{
+    const int da = dtype_code(a_dtype), db = dtype_code(b_dtype);
+    if (da < 0 || db < 0 || da == DT_F64 || db == DT_F64)
+        return 0;
+    // at most one 16-bit type: float16 and bfloat16 do not meet in one product
+    if (da != DT_F32 && db != DT_F32 && da != db)
+        return 0;
+    Problem P;
+    const int v = build_problem(DT_F32, a, b, c, shape_a, stride_a, nd_a, shape_b, stride_b,
+                                nd_b, shape_c, stride_c, nd_c, &P);
+    if (v == 0)
+        return 0;
+    if (v == 2)
+        return 1;
+    P.a_dt = da;
+    P.b_dt = db;
+    return run(P, stream);
 }
 
 PT_API int cuda_matmul_epilogue_nd_launcher(void *a, void *b, void *c, dtype_t dtype,

@@ -12,8 +12,12 @@
 //                activation, convert, stage 32x(128 B) boxes in swizzled shared
 //                memory and write them with TMA stores.  Double-buffered TMEM
 //                lets the epilogue of tile i overlap the mainloop of tile i+1.
-//   warps 6..13  (SPLIT3 only) split each FP32 tile into TF32 hi/lo parts so
-//                the MMA warp can issue hi*hi + hi*lo + lo*hi (3xTF32).
+//   warps 6..13  (split kinds only) F32X3: split each FP32 tile into TF32
+//                hi/lo parts so the MMA warp can issue hi*hi + hi*lo + lo*hi
+//                (3xTF32).  MIX_A / MIX_B (one operand float32, the other
+//                bfloat16): split the float32 tile into three bfloat16 parts
+//                hi + mid + lo (24+ significant bits) so the MMA warp can
+//                issue three exact bf16 x bf16 products per k16.
 // Tiles (batch, m-block, n-block) are distributed round-robin over a grid of
 // at most one CTA per SM.  Split-K (p.ksplit = G > 1, for problems with too
 // few tiles to fill the GPU): a cluster of G CTAs shares one tile, CTA rank r
@@ -35,7 +39,7 @@
 
 namespace ptg {
 
-enum InKind : int { IN_F16 = 0, IN_BF16 = 1, IN_TF32 = 2, IN_F32X3 = 3 };
+enum InKind : int { IN_F16 = 0, IN_BF16 = 1, IN_TF32 = 2, IN_F32X3 = 3, IN_MIX_A = 4, IN_MIX_B = 5 };
 enum OutKind : int { OUT_F32 = 0, OUT_F16 = 1, OUT_BF16 = 2 };
 enum Activation : int { ACT_NONE = 0, ACT_TANH = 1, ACT_RELU = 2, ACT_SIGMOID = 3 };
 
@@ -203,7 +207,10 @@ template <int IN_KIND, int BN_, int OUT>
 struct TcConfig {
     static constexpr int BM = 128;
     static constexpr int BN = BN_;
-    static constexpr bool kSplit3 = IN_KIND == IN_F32X3;
+    static constexpr bool kMix = IN_KIND == IN_MIX_A || IN_KIND == IN_MIX_B;
+    static constexpr bool kMixA = IN_KIND == IN_MIX_A;   // the float32 operand is A
+    // split warps, chunked accumulation and the TMEM running total
+    static constexpr bool kSplit3 = IN_KIND == IN_F32X3 || kMix;
     static constexpr bool kTf32 = IN_KIND == IN_TF32 || IN_KIND == IN_F32X3;
     static constexpr int kInBytes = kTf32 ? 4 : 2;
     static constexpr int BK = 128 / kInBytes;            // one 128-byte swizzle row of K
@@ -218,8 +225,16 @@ struct TcConfig {
     static constexpr uint32_t kMnSbo = kTf32 ? 512 : 1024;
     static constexpr int kATile = BM * BK * kInBytes;     // 16 KB
     static constexpr int kBTile = BN * BK * kInBytes;     // 16 or 32 KB
-    static constexpr int kLoadBytes = kATile + kBTile;    // bytes TMA lands per stage
-    static constexpr int kStageBytes = kLoadBytes * (kSplit3 ? 2 : 1);
+    // MIX: the float32 operand lands raw ([128][BK] floats, 32 KB, no swizzle)
+    // at the stage start; the split rewrites it in place as the bf16 hi and
+    // mid tiles and writes lo after it; the bf16 operand tile follows.
+    static constexpr int kMixRawBytes = 128 * BK * 4;
+    static constexpr int kMixLoOffset = kMixRawBytes;
+    static constexpr int kMixOtherOffset = kMixRawBytes + 128 * BK * 2;
+    static constexpr int kLoadBytes =
+        kMix ? kMixRawBytes + 128 * BK * 2 : kATile + kBTile;   // bytes TMA lands per stage
+    static constexpr int kStageBytes =
+        kMix ? kMixOtherOffset + 128 * BK * 2 : kLoadBytes * (kSplit3 ? 2 : 1);
     static constexpr int kStages = (196608 / kStageBytes) > 8 ? 8 : (196608 / kStageBytes);
     static constexpr int kOutBytes = OutTraits<OUT>::kBytes;
     static constexpr int kEpiCols = 128 / kOutBytes;      // columns per staged box
@@ -253,7 +268,48 @@ struct TcConfig {
     static_assert(BN % kEpiCols == 0, "epilogue box must divide BN");
     static_assert(kSmemBytes <= 232448, "shared memory budget exceeded");
     static_assert(kTmemUsed <= 512, "TMEM holds 512 columns");
+    static_assert(!kMix || (BN == 128 && !kTf32), "mixed kinds use 128x128 bf16 tiles");
 };
+
+// x = hi + mid + lo in bfloat16 (round-to-nearest at each step; both
+// differences are exact in float), so 24+ significant bits survive.  A
+// non-finite hi carries the value alone.
+__device__ __forceinline__ void split3_bf16(float x, __nv_bfloat16 &h, __nv_bfloat16 &m,
+                                            __nv_bfloat16 &l)
+{
+    h = __float2bfloat16_rn(x);
+    const float hf = __bfloat162float(h);
+    if (!isfinite(hf)) {
+        m = l = __float2bfloat16_rn(0.0f);
+        return;
+    }
+    const float r = x - hf;
+    m = __float2bfloat16_rn(r);
+    l = __float2bfloat16_rn(r - __bfloat162float(m));
+}
+
+// Splits four consecutive floats into the hi/mid/lo bf16 tiles (8 bytes each
+// at byte offset `off` of the three tiles, `part` bytes apart).
+__device__ __forceinline__ void split3_store(const float4 &x, uint8_t *base, uint32_t off, int part)
+{
+    __nv_bfloat16 h[4], m[4], l[4];
+    split3_bf16(x.x, h[0], m[0], l[0]);
+    split3_bf16(x.y, h[1], m[1], l[1]);
+    split3_bf16(x.z, h[2], m[2], l[2]);
+    split3_bf16(x.w, h[3], m[3], l[3]);
+    auto pack = [](const __nv_bfloat16 (&v)[4]) {
+        uint2 u;
+        __nv_bfloat162 lo2, hi2;
+        lo2.x = v[0]; lo2.y = v[1];
+        hi2.x = v[2]; hi2.y = v[3];
+        u.x = *reinterpret_cast<uint32_t *>(&lo2);
+        u.y = *reinterpret_cast<uint32_t *>(&hi2);
+        return u;
+    };
+    *reinterpret_cast<uint2 *>(base + off) = pack(h);
+    *reinterpret_cast<uint2 *>(base + part + off) = pack(m);
+    *reinterpret_cast<uint2 *>(base + 2 * part + off) = pack(l);
+}
 
 __device__ __forceinline__ void decode_batch(long long b, const TcParams &p, int (&c)[3])
 {
@@ -370,9 +426,22 @@ __global__ void __launch_bounds__(TcConfig<IN_KIND, BN, OUT>::kThreads, 1)
                     }
                     uint8_t *sa = smem + stage * Cfg::kStageBytes;
                     uint8_t *sb = sa + Cfg::kATile;
+                    if constexpr (Cfg::kMix) {
+                        // the float32 operand lands raw at the stage start
+                        // (one unswizzled box), the bf16 one after lo
+                        if constexpr (Cfg::kMixA)
+                            sb = sa + Cfg::kMixOtherOffset;
+                        else
+                            sa = sa + Cfg::kMixOtherOffset, sb = smem + stage * Cfg::kStageBytes;
+                    }
                     mbar_arrive_expect_tx(&full[stage], Cfg::kLoadBytes);
                     const int k0 = kb * Cfg::BK;
-                    if (!p.a_mn_major) {
+                    if (Cfg::kMixA) {
+                        if (!p.a_mn_major)
+                            tma_load_5d(sa, &tma_a, &full[stage], k0, m0, ca[0], ca[1], ca[2]);
+                        else
+                            tma_load_5d(sa, &tma_a, &full[stage], m0, k0, ca[0], ca[1], ca[2]);
+                    } else if (!p.a_mn_major) {
                         tma_load_5d(sa, &tma_a, &full[stage], k0, m0, ca[0], ca[1], ca[2]);
                     } else {
 #pragma unroll
@@ -380,7 +449,12 @@ __global__ void __launch_bounds__(TcConfig<IN_KIND, BN, OUT>::kThreads, 1)
                             tma_load_5d(sa + j * Cfg::kChunkBytes, &tma_a, &full[stage],
                                         m0 + j * Cfg::kChunk, k0, ca[0], ca[1], ca[2]);
                     }
-                    if (!p.b_mn_major) {
+                    if (Cfg::kMix && !Cfg::kMixA) {
+                        if (!p.b_mn_major)
+                            tma_load_5d(sb, &tma_b, &full[stage], k0, n0, cb[0], cb[1], cb[2]);
+                        else
+                            tma_load_5d(sb, &tma_b, &full[stage], n0, k0, cb[0], cb[1], cb[2]);
+                    } else if (!p.b_mn_major) {
                         tma_load_5d(sb, &tma_b, &full[stage], k0, n0, cb[0], cb[1], cb[2]);
                     } else {
 #pragma unroll
@@ -438,8 +512,14 @@ __global__ void __launch_bounds__(TcConfig<IN_KIND, BN, OUT>::kThreads, 1)
                         break;
                     }
                     tc_fence_after();
-                    const uint32_t sa = smem_base + stage * Cfg::kStageBytes;
-                    const uint32_t sb = sa + Cfg::kATile;
+                    const uint32_t stage_base = smem_base + stage * Cfg::kStageBytes;
+                    // MIX: the float32 operand's hi, mid, lo bf16 tiles sit at
+                    // 0, kATile, 2 * kATile of the stage, the other operand after
+                    const uint32_t sa = Cfg::kMix && !Cfg::kMixA ? stage_base + Cfg::kMixOtherOffset
+                                                                 : stage_base;
+                    const uint32_t sb = Cfg::kMix ? (Cfg::kMixA ? stage_base + Cfg::kMixOtherOffset
+                                                                : stage_base)
+                                                  : stage_base + Cfg::kATile;
 #pragma unroll
                     for (int k = 0; k < Cfg::kKSteps; k++) {
                         // one MMA consumes 32 bytes of K: a 32-byte column step
@@ -464,6 +544,21 @@ __global__ void __launch_bounds__(TcConfig<IN_KIND, BN, OUT>::kThreads, 1)
                                     smem_desc(sb + Cfg::kLoadBytes + b_off, b_lbo, b_sbo, b_lay);
                                 umma_tf32(d_tmem, ad, bd_lo, p.idesc, 1);
                                 umma_tf32(d_tmem, ad_lo, bd, p.idesc, 1);
+                            }
+                        } else if constexpr (Cfg::kMix) {
+                            // hi, mid and lo of the float32 operand against the
+                            // bf16 operand: three exact products per k16
+                            umma_f16(d_tmem, ad, bd, p.idesc, accumulate);
+#pragma unroll
+                            for (int part = 1; part < 3; part++) {
+                                const uint32_t po = static_cast<uint32_t>(part * Cfg::kATile);
+                                if constexpr (Cfg::kMixA)
+                                    umma_f16(d_tmem, smem_desc(sa + po + a_off, a_lbo, a_sbo, a_lay),
+                                             bd, p.idesc, 1);
+                                else
+                                    umma_f16(d_tmem, ad,
+                                             smem_desc(sb + po + b_off, b_lbo, b_sbo, b_lay),
+                                             p.idesc, 1);
                             }
                         } else {
                             umma_f16(d_tmem, ad, bd, p.idesc, accumulate);
@@ -697,8 +792,55 @@ __global__ void __launch_bounds__(TcConfig<IN_KIND, BN, OUT>::kThreads, 1)
             bulk_wait_group<0>();
         __syncwarp();
     } else {
-        // ------------------------------------------------------------ 3xTF32 split
-        if constexpr (Cfg::kSplit3) {
+        // ------------------------------------------------------------ split warps
+        if constexpr (Cfg::kMix) {
+            // float32 operand -> bf16 hi/mid/lo tiles in the 128-byte-swizzled
+            // layout a bf16 TMA load of the same operand would produce.  The
+            // raw tile is read whole into registers, then (named barrier)
+            // overwritten.  A failed wait sets the abort flag, after which
+            // every wait returns at once; the loop still runs to the end so
+            // that all 256 threads meet at every barrier.
+            const int st = threadIdx.x - 32 * (2 + Cfg::kEpiWarps);   // 0..255
+            const bool f_mn = Cfg::kMixA ? p.a_mn_major : p.b_mn_major;
+            int stage = 0;
+            uint32_t phase = 0;
+            for (long long t = t_first; t < p.tiles; t += t_step) {
+                for (int kb = kb_begin; kb < kb_end; kb++) {
+                    if (!mbar_wait(&full[stage], phase, abort))
+                        record_failure(abort, p.status, DEV_TIMEOUT_SPLIT);
+                    uint8_t *base = smem + stage * Cfg::kStageBytes;
+                    const float4 *raw = reinterpret_cast<const float4 *>(base);
+                    constexpr int kPer = Cfg::kMixRawBytes / 16 / (Cfg::kSplitWarps * 32);   // 8
+                    float4 x[kPer];
+#pragma unroll
+                    for (int j = 0; j < kPer; j++)
+                        x[j] = raw[st + j * Cfg::kSplitWarps * 32];
+                    named_barrier_sync(1, Cfg::kSplitWarps * 32);
+#pragma unroll
+                    for (int j = 0; j < kPer; j++) {
+                        const int e = st + j * Cfg::kSplitWarps * 32;
+                        uint32_t off;
+                        if (!f_mn) {
+                            // raw [128 rows][64 k]: row e/16, k 4*(e%16)
+                            const int r = e >> 4, k4 = e & 15;
+                            off = r * 128 + ((((k4 >> 1) ^ (r & 7))) << 4) + ((k4 & 1) << 3);
+                        } else {
+                            // raw [64 k][128 rows]: k e/32, rows 4*(e%32)
+                            const int k = e >> 5, r4 = e & 31;
+                            off = (r4 >> 4) * Cfg::kChunkBytes + k * 128 +
+                                  ((((r4 & 15) >> 1) ^ (k & 7)) << 4) + ((r4 & 1) << 3);
+                        }
+                        split3_store(x[j], base, off, Cfg::kATile);
+                    }
+                    fence_proxy_async_smem();
+                    mbar_arrive(&ready[stage]);
+                    if (++stage == S) {
+                        stage = 0;
+                        phase ^= 1;
+                    }
+                }
+            }
+        } else if constexpr (Cfg::kSplit3) {
             const int st = threadIdx.x - 32 * (2 + Cfg::kEpiWarps);   // 0..127
             int stage = 0;
             uint32_t phase = 0;

@@ -26,3 +26,17 @@ struct F64PeerOut {
 cudaError_t ptg_launch_f64_peer(const double *a, size_t a_s0, size_t a_s1, const double *b,
                                 size_t b_s0, size_t b_s1, int M, int nb, int K,
                                 const ptg::F64PeerOut &po, cudaStream_t stream);
+
+// Shape of a gradient's un-broadcast reduction: src is a contiguous float32
+// tensor of extents ext[0..n); axes with keep[d] == 0 are summed (in
+// row-major order of their coordinates, so the result is deterministic) and
+// the sum lands at dst + sum over kept axes of coord * dst_stride[d].
+struct PtgReduceDims {
+    int n;
+    int ext[10];
+    int keep[10];
+    long long dst_stride[10];
+};
+
+cudaError_t ptg_reduce_axes(const float *src, float *dst, const PtgReduceDims &d,
+                            cudaStream_t stream);

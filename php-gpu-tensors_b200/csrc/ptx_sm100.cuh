@@ -269,6 +269,12 @@ __device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t lbo_bytes
 
 namespace ptg {
 
+// Barrier `id` (1..15) among `threads` threads (a multiple of 32) of the CTA.
+__device__ __forceinline__ void named_barrier_sync(int id, int threads)
+{
+    asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
 // ---------------------------------------------------------------- launch overlap
 // Programmatic dependent launch: wait until the grids this launch depends on
 // (the previous kernel in the stream) have completed and their writes are

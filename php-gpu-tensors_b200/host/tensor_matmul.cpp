@@ -4,6 +4,8 @@
 // src/autograd.c:1539-1585) and calls the launcher ABI of gemm_sm100.h.
 #include "pt_tensor.h"
 
+#include "internal.h"
+
 #include <cstdio>
 #include <cstring>
 
@@ -211,24 +213,163 @@ PT_API void pt_tensor_release(pt_tensor *t, cudaStream_t stream)
     }
 }
 
+namespace {
+
+// out (float32) = x . y where x and y are float32 or one 16-bit type each:
+// float32 pairs take the reference's launchers, anything else the mixed
+// launcher, which reads the 16-bit operands as they are.
+int launch_product(const pt_tensor *x, const pt_tensor *y, const pt_tensor *out,
+                   cudaStream_t stream)
+{
+    if (x->dtype == DTYPE_FLOAT32 && y->dtype == DTYPE_FLOAT32)
+        return dispatch(x, y, out, stream);
+    pt_tensor cx = *x, cy = *y, co = *out;
+    const int st = cuda_mixed_matmul_nd_launcher(x->data, x->dtype, y->data, y->dtype,
+                                                 static_cast<float *>(out->data), cx.shape,
+                                                 cx.strides, x->ndims, cy.shape, cy.strides,
+                                                 y->ndims, co.shape, co.strides, out->ndims,
+                                                 stream);
+    return st ? ok() : submission_failed();
+}
+
+// Whether the batch axes of t (aligned to the product's nb batch axes, all at
+// full extent) chain onto its axis `inner` so that (batch..., inner) is one
+// strided axis; returns its extent through *total.
+bool folds_into(const pt_tensor *t, const int *full, int nb, int inner, long long *total)
+{
+    if (t->ndims - 2 != nb)
+        return false;
+    long long extent = t->shape[inner];
+    long long stride = static_cast<long long>(t->strides[inner]);
+    for (int d = nb - 1; d >= 0; d--) {
+        if (t->shape[d] != full[d])
+            return false;
+        if (t->shape[d] == 1)
+            continue;
+        if (static_cast<long long>(t->strides[d]) != extent * stride)
+            return false;
+        extent *= t->shape[d];
+    }
+    *total = extent;
+    return extent <= 0x7fffffffll;
+}
+
+// out = x . y, or -- when out has the shape of an operand that the product
+// broadcast (extent 1 or no axis where the product has a batch axis) -- that
+// product summed over the broadcast axes, the un-broadcast step of
+// src/autograd.c:714-760 fused with the GEMM:
+//   * every batch axis summed and both operands' batch axes chaining onto the
+//     product's inner axis (contiguous tensors): one GEMM whose inner axis is
+//     (batch..., K);
+//   * otherwise: the batched product into a float32 scratch tensor, then a
+//     fixed-order reduction kernel.
+int gradient_product(const pt_tensor *x, const pt_tensor *y, const pt_tensor *out,
+                     cudaStream_t stream)
+{
+    int full[MAX_DIMS], nf = 0;
+    if (!matmul_shape(x, y, full, &nf) || out->ndims < 2 || out->ndims > nf ||
+        out->shape[out->ndims - 2] != full[nf - 2] || out->shape[out->ndims - 1] != full[nf - 1])
+        return fail(PT_INVALID_ARGUMENT, "Matrix multiplication failed - incompatible dimensions");
+    if (out->dtype != DTYPE_FLOAT32)
+        return fail(PT_INVALID_ARGUMENT, "matmul gradients are float32 tensors");
+    const int nb = nf - 2;
+    bool same = out->ndims == nf, all_reduced = true;
+    int keep[MAX_DIMS];
+    for (int d = 0; d < nb; d++) {
+        const int io = d - (nf - out->ndims);
+        const int eo = io >= 0 ? out->shape[io] : 1;
+        if (eo != full[d] && eo != 1)
+            return fail(PT_INVALID_ARGUMENT,
+                        "Gradient shape cannot be reduced to its operand shape at axis %d", io);
+        same = same && eo == full[d];
+        keep[d] = eo == full[d] ? 1 : 0;
+        all_reduced = all_reduced && (full[d] == 1 || !keep[d]);
+    }
+    if (same)
+        return launch_product(x, y, out, stream);
+
+    long long fx = 0, fy = 0;
+    if (all_reduced && folds_into(x, full, nb, x->ndims - 1, &fx) &&
+        folds_into(y, full, nb, y->ndims - 2, &fy) && fx == fy) {
+        pt_tensor x2 = *x, y2 = *y, o2 = *out;
+        x2.ndims = y2.ndims = o2.ndims = 2;
+        x2.shape[0] = x->shape[x->ndims - 2];
+        x2.shape[1] = static_cast<int>(fx);
+        x2.strides[0] = x->strides[x->ndims - 2];
+        x2.strides[1] = x->strides[x->ndims - 1];
+        y2.shape[0] = static_cast<int>(fy);
+        y2.shape[1] = y->shape[y->ndims - 1];
+        y2.strides[0] = y->strides[y->ndims - 2];
+        y2.strides[1] = y->strides[y->ndims - 1];
+        o2.shape[0] = out->shape[out->ndims - 2];
+        o2.shape[1] = out->shape[out->ndims - 1];
+        o2.strides[0] = out->strides[out->ndims - 2];
+        o2.strides[1] = out->strides[out->ndims - 1];
+        return launch_product(&x2, &y2, &o2, stream);
+    }
+
+    // scratch product of the full broadcast shape, then the reduction
+    pt_tensor t;
+    std::memset(&t, 0, sizeof(t));
+    t.dtype = DTYPE_FLOAT32;
+    t.ndims = nf;
+    std::memcpy(t.shape, full, sizeof(int) * static_cast<size_t>(nf));
+    contiguous_strides(full, nf, t.strides);
+    size_t total = 1;
+    for (int d = 0; d < nf; d++)
+        total *= static_cast<size_t>(full[d]);
+    if (total == 0)
+        return ok();
+    cudaError_t err = cudaMallocAsync(&t.data, total * sizeof(float), stream);
+    if (err != cudaSuccess)
+        return fail(PT_RUNTIME, "Failed to allocate the gradient scratch (CUDA error %d)",
+                    static_cast<int>(err));
+    int st = launch_product(x, y, &t, stream);
+    if (st == PT_OK) {
+        PtgReduceDims rd;
+        std::memset(&rd, 0, sizeof(rd));
+        rd.n = nf;
+        for (int d = 0; d < nf; d++) {
+            rd.ext[d] = full[d];
+            rd.keep[d] = d < nb ? keep[d] : 1;
+            const int io = d - (nf - out->ndims);
+            rd.dst_stride[d] = rd.keep[d] && io >= 0 ? static_cast<long long>(out->strides[io]) : 0;
+        }
+        err = ptg_reduce_axes(static_cast<const float *>(t.data), static_cast<float *>(out->data),
+                              rd, stream);
+        if (err != cudaSuccess)
+            st = fail(PT_RUNTIME, "Gradient reduction failed (CUDA error %d)",
+                      static_cast<int>(err));
+    }
+    cudaFreeAsync(t.data, stream);
+    return st;
+}
+
+} // namespace
+
 PT_API int pt_tensor_matmul_backward(const pt_tensor *a, const pt_tensor *b,
                                      const pt_tensor *grad_c, const pt_tensor *grad_a,
                                      const pt_tensor *grad_b, cudaStream_t stream)
 {
-    if (!a || !b || !grad_c || a->dtype != DTYPE_FLOAT32 || b->dtype != DTYPE_FLOAT32 ||
-        grad_c->dtype != DTYPE_FLOAT32)
-        return fail(PT_INVALID_ARGUMENT, "matmul backward requires float32 tensors");
+    // src/autograd.c:1547-1551: float16/bfloat16 operands have float32
+    // gradients; the upstream gradient is float32 or the operands' type
+    if (!a || !b || !grad_c || a->dtype != b->dtype ||
+        (a->dtype != DTYPE_FLOAT32 && a->dtype != DTYPE_FLOAT16 && a->dtype != DTYPE_BFLOAT16) ||
+        (grad_c->dtype != DTYPE_FLOAT32 && grad_c->dtype != a->dtype))
+        return fail(PT_INVALID_ARGUMENT,
+                    "matmul backward requires float32, float16 or bfloat16 operands with a "
+                    "float32 or same-typed upstream gradient");
     if (a->ndims < 2 || b->ndims < 2)
-        return fail(PT_INVALID_ARGUMENT, "Matrix multiplication failed - incompatible dimensions");
+        return fail(PT_INVALID_ARGUMENT, "Autograd matmul requires operands with rank at least 2");
     if (grad_a) {
         const pt_tensor bt = transposed_view(b);
-        const int s = pt_tensor_matmul_into(grad_c, &bt, grad_a, 0, stream);
+        const int s = gradient_product(grad_c, &bt, grad_a, stream);
         if (s != PT_OK)
             return s;
     }
     if (grad_b) {
         const pt_tensor at = transposed_view(a);
-        const int s = pt_tensor_matmul_into(&at, grad_c, grad_b, 0, stream);
+        const int s = gradient_product(&at, grad_c, grad_b, stream);
         if (s != PT_OK)
             return s;
     }

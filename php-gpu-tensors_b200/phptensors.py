@@ -101,6 +101,11 @@ _SIGNATURES = {
         ctypes.c_int, [ctypes.c_void_p] * 3 + [ctypes.c_int] +
         [ctypes.POINTER(ctypes.c_int), ctypes.POINTER(ctypes.c_size_t), ctypes.c_int] * 3 +
         [ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p]),
+    "cuda_mixed_matmul_nd_launcher": (
+        ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p, ctypes.c_int,
+                       ctypes.c_void_p] +
+        [ctypes.POINTER(ctypes.c_int), ctypes.POINTER(ctypes.c_size_t), ctypes.c_int] * 3 +
+        [ctypes.c_void_p]),
     "gemm_sm100_last_kernel": (ctypes.c_char_p, []),
     "gemm_sm100_set_path": (ctypes.c_int, [ctypes.c_int]),
     "gemm_sm100_last_launch": (None, [ctypes.POINTER(ctypes.c_int)] * 3),

@@ -505,6 +505,134 @@ def test_config3_fp16_transposed_bias_tanh():
         check_close(c[row * N:(row + 1) * N], ref, "float16", row)
 
 
+# ------------------------------------------------------------------ gradients
+def as_f32_op(op, dtype):
+    """The same view over an exact float32 copy of the storage (what the
+    reference's gradient_cast produces, src/autograd.c:683-712)."""
+    storage, shape, strides, offset = op
+    return (O.to_float32(storage, dtype).astype(np.float32), shape, strides, offset)
+
+
+def mixed_product(a_op, a_dt, b_op, b_dt):
+    """C (float32) = A . B through cuda_mixed_matmul_nd_launcher."""
+    import ctypes
+    ad, bd = to_device(a_op, a_dt), to_device(b_op, b_dt)
+    M, N = a_op[1][-2], b_op[1][-1]
+    batch = []
+    for x, y in zip([1] * (max(len(a_op[1]), len(b_op[1])) - len(a_op[1])) + list(a_op[1][:-2]),
+                    [1] * (max(len(a_op[1]), len(b_op[1])) - len(b_op[1])) + list(b_op[1][:-2])):
+        batch.append(max(x, y))
+    c = P.CudaArray.zeros(batch + [M, N])
+    pa, pb, pc = ad._pt(), bd._pt(), c._pt()
+    ok = P.library().cuda_mixed_matmul_nd_launcher(
+        pa.data, P.DTYPE_CODES[a_dt], pb.data, P.DTYPE_CODES[b_dt], pc.data,
+        pa.shape, pa.strides, pa.ndims, pb.shape, pb.strides, pb.ndims,
+        pc.shape, pc.strides, pc.ndims, P.current_stream())
+    assert ok, P.cuda_get_backend_info()
+    return c
+
+
+MIXED_CASES = [
+    # (name, a_shape, b_shape, a_transposed, b_transposed, a dtype, b dtype, tensor-core kernel)
+    ("f32_bf16_kk", [300, 520], [520, 264], False, True, "float32", "bfloat16", "tc-f32xbf16"),
+    ("f32_bf16_mn", [300, 520], [520, 264], True, False, "float32", "bfloat16", "tc-f32xbf16"),
+    ("f32_bf16_km", [257, 1000], [1000, 136], False, False, "float32", "bfloat16", "tc-f32xbf16"),
+    ("bf16_f32_mm", [264, 704], [704, 392], True, False, "bfloat16", "float32", "tc-bf16xf32"),
+    ("bf16_f32_kk", [264, 704], [704, 392], False, True, "bfloat16", "float32", "tc-bf16xf32"),
+    ("bf16_f32_batched", [3, 200, 136], [136, 264], True, False, "bfloat16", "float32", "tc-bf16xf32"),
+    ("bf16_bf16", [256, 512], [512, 384], False, False, "bfloat16", "bfloat16", "tc-bf16-f32out"),
+    ("f16_f16", [256, 512], [512, 384], False, True, "float16", "float16", "tc-f16-f32out"),
+    ("f32_f16_simt", [130, 300], [300, 70], False, False, "float32", "float16", "simt-"),
+    ("f32_bf16_short_k", [200, 8], [8, 136], False, True, "float32", "bfloat16", "simt-"),
+]
+
+
+@pytest.mark.parametrize("case", MIXED_CASES, ids=[c[0] for c in MIXED_CASES])
+def test_mixed_precision_products(case):
+    """float32 result from a float32 and a 16-bit operand (or two 16-bit
+    operands) without a float32 copy: within the float32 bound of the oracle
+    run on the exact float32 upcast."""
+    name, ashape, bshape, at, bt, adt, bdt, kernel = case
+    seed = sum(map(ord, name))
+    a = padded(O.seeded(ashape, seed, "normal"), ashape, 0, adt, at)
+    b = padded(O.seeded(bshape, seed + 1, "normal"), bshape, 0, bdt, bt)
+    c = mixed_product(a, adt, b, bdt)
+    got = P.cuda_get_backend_info()["kernel"]
+    assert got.startswith(kernel), (name, got)
+    check_fp32(c.to_numpy(), as_f32_op(a, adt), as_f32_op(b, bdt), (name, got))
+    assert P.device_status() == 0
+
+
+def _backward(a, b, gc, ga, gb):
+    import ctypes
+    rc = P.library().pt_tensor_matmul_backward(
+        ctypes.byref(a._pt()), ctypes.byref(b._pt()), ctypes.byref(gc._pt()),
+        ctypes.byref(ga._pt()) if ga is not None else None,
+        ctypes.byref(gb._pt()) if gb is not None else None, P.current_stream())
+    assert rc == P.PT_OK, P.library().pt_last_error()
+
+
+@pytest.mark.parametrize("dt,gdt", [("bfloat16", "float32"), ("bfloat16", "bfloat16"),
+                                    ("float16", "float32")])
+def test_backward_low_precision_operands(dt, gdt):
+    """src/autograd.c:1547-1577 for 16-bit operands: float32 gradients of the
+    float32-cast operands, here computed without the casts."""
+    M, K, N = 384, 520, 264
+    a = O.dense(O.to_storage(O.seeded([M, K], 51, "normal"), dt), [M, K])
+    b = O.dense(O.to_storage(O.seeded([K, N], 52, "normal"), dt), [K, N])
+    gc = O.dense(O.to_storage(O.seeded([M, N], 53, "normal"), gdt), [M, N])
+    ga, gb = P.CudaArray.zeros([M, K]), P.CudaArray.zeros([K, N])
+    _backward(to_device(a, dt), to_device(b, dt), to_device(gc, gdt), ga, gb)
+    af, bf, gf = as_f32_op(a, dt), as_f32_op(b, dt), as_f32_op(gc, gdt)
+    bt = (bf[0], [N, K], [1, N], 0)
+    at = (af[0], [K, M], [1, K], 0)
+    check_fp32(ga.to_numpy(), gf, bt, ("dA", dt, gdt))
+    check_fp32(gb.to_numpy(), at, gf, ("dB", dt, gdt))
+
+
+@pytest.mark.parametrize("dt", ["float32", "bfloat16"])
+def test_backward_broadcast_reduction_fused(dt):
+    """A shared weight (rank 2) under a batched input: its gradient, requested
+    in the weight's own shape, is the product summed over the batch
+    (src/autograd.c:714-760).  dB folds the batch into one GEMM's inner axis;
+    dA of a broadcast A goes through the scratch product and the fixed-order
+    reduction."""
+    Bt, M, K, N = 3, 200, 136, 264
+    # dB fused by folding: A [Bt, M, K] contiguous, B [K, N] broadcast
+    a = O.dense(O.to_storage(O.seeded([Bt, M, K], 61, "normal"), dt), [Bt, M, K])
+    b = O.dense(O.to_storage(O.seeded([K, N], 62, "normal"), dt), [K, N])
+    gc = O.dense(O.seeded([Bt, M, N], 63, "normal"), [Bt, M, N])
+    gb = P.CudaArray.zeros([K, N])
+    ga = P.CudaArray.zeros([Bt, M, K])
+    _backward(to_device(a, dt), to_device(b, dt), to_device(gc, "float32"), ga, gb)
+    af, bf = as_f32_op(a, dt), as_f32_op(b, dt)
+    # reference dB: the same sum as one product over the folded (batch, M) axis
+    a_fold_t = (af[0], [K, Bt * M], [1, K], 0)
+    gc_fold = (gc[0], [Bt * M, N], [N, 1], 0)
+    check_fp32(gb.to_numpy(), a_fold_t, gc_fold, ("dB folded", dt))
+    check_fp32(ga.to_numpy(), gc, (bf[0], [N, K], [1, N], 0), ("dA batched", dt))
+
+    # dA of a broadcast A: A [M, K], B [Bt, K, N]
+    a2 = O.dense(O.to_storage(O.seeded([M, K], 64, "normal"), dt), [M, K])
+    b2 = O.dense(O.to_storage(O.seeded([Bt, K, N], 65, "normal"), dt), [Bt, K, N])
+    ga2 = P.CudaArray.zeros([M, K])
+    _backward(to_device(a2, dt), to_device(b2, dt), to_device(gc, "float32"), ga2, None)
+    b2f = as_f32_op(b2, dt)
+    th = O.oracle().orc_host_threads()
+    ref = np.zeros(M * K)
+    absp = np.zeros(M * K)
+    for i in range(Bt):
+        gci = (gc[0][i * M * N:(i + 1) * M * N].copy(), [M, N], [N, 1], 0)
+        bti = (b2f[0][i * K * N:(i + 1) * K * N].copy(), [N, K], [1, N], 0)
+        ref += O.host_matmul_f64(gci, bti, "float32", th).reshape(-1)
+        absp += O.host_matmul_f64(O.absolute(gci, "float32"), O.absolute(bti, "float32"),
+                                  "float32", th).reshape(-1)
+    got = ga2.to_numpy().reshape(-1).astype(np.float64)
+    assert np.all(np.abs(got - ref) <= Bt * N * 2.0 ** -24 * absp + 1e-30)
+    assert np.max(np.abs(got - ref)) / max(1.0, np.max(np.abs(ref))) <= 1e-5
+    assert P.device_status() == 0
+
+
 def test_config4_mlp_forward_backward_fp32():
     """float32 MLP 784->1024->1024->10, batch 4096: forward GEMMs and the
     backward pair dA = dC.B^T, dB = A^T.dC of every layer (transposed views),
