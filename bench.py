@@ -2,7 +2,7 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
                     [--workload config2|config3|config4|config5a|config5b]
-                    [--precision fp32-strict|tf32]
+                    [--precision fp32-strict|tf32] [--operand-dtype float32|bfloat16]
 
 One step = one pass of the workload through the library's launchers:
   config2  (default) BASELINE config 2: bf16 A[64,1024,1024] x B[64,1024,1024],
@@ -81,6 +81,9 @@ def parse():
                    help="config5b exchange: fused peer stores, or NCCL all-gather + permute")
     p.add_argument("--precision", default="fp32-strict", choices=["fp32-strict", "tf32"],
                    help="float32 precision mode for config4 (cuda_blas_set_precision)")
+    p.add_argument("--operand-dtype", default="float32", choices=["float32", "bfloat16"],
+                   help="config4: weights and activations in bfloat16 (forward in bf16, "
+                        "float32 gradients from pt_tensor_matmul_backward without cast copies)")
     p.add_argument("--cpu-seconds", type=float, default=8.0,
                    help="target duration of the bounded CPU baseline sample")
     return p.parse_args()
@@ -423,6 +426,76 @@ def setup_config3(w, rank, torch, P, lib, stream):
     }
 
 
+def setup_config4_bf16(w, rank, torch, P, lib, stream):
+    """config4 with bfloat16 weights and activations: forward products in
+    bf16 (cuda_low_precision_matmul_nd_launcher), and per layer one
+    pt_tensor_matmul_backward call giving float32 dA and dW from the bf16
+    operands and a float32 upstream gradient, without cast copies."""
+    dims = w["mlp"]
+    batch = w["M"]
+    gen = torch.Generator(device="cuda").manual_seed(4100 + rank)
+    x = torch.rand(batch, dims[0], device="cuda", generator=gen).bfloat16()
+    Ws = [(torch.randn(dims[i], dims[i + 1], device="cuda", generator=gen) / dims[i] ** 0.5)
+          .bfloat16() for i in range(3)]
+    dCs = [torch.randn(batch, dims[i + 1], device="cuda", generator=gen) for i in range(3)]
+    hs = [x] + [torch.empty(batch, dims[i + 1], device="cuda", dtype=torch.bfloat16)
+                for i in range(3)]
+    dAs = [torch.empty(batch, dims[i], device="cuda") for i in range(3)]
+    dWs = [torch.empty(dims[i], dims[i + 1], device="cuda") for i in range(3)]
+    bf16 = P.DTYPE_CODES["bfloat16"]
+    sptr = ctypes.c_void_p(stream.cuda_stream)
+    fwd = []
+    for l in range(3):
+        fi, fo = dims[l], dims[l + 1]
+        fwd.append((hs[l], Ws[l], hs[l + 1], (ctypes.c_int * 10)(batch, fi),
+                    (ctypes.c_size_t * 10)(fi, 1), (ctypes.c_int * 10)(fi, fo),
+                    (ctypes.c_size_t * 10)(fo, 1), (ctypes.c_int * 10)(batch, fo),
+                    (ctypes.c_size_t * 10)(fo, 1)))
+    wrap = [P.CudaArray.from_torch(t) for t in hs + Ws + dCs + dAs + dWs]
+    pts = [t._pt() for t in wrap]
+    H, W, DC, DA, DW = pts[0:4], pts[4:7], pts[7:10], pts[10:13], pts[13:16]
+    flop = sum(6.0 * batch * dims[l] * dims[l + 1] for l in range(3))
+
+    def step():
+        for (a, b, c, sa, ta, sb, tb, sc, tc) in fwd:
+            if not lib.cuda_low_precision_matmul_nd_launcher(
+                    a.data_ptr(), b.data_ptr(), c.data_ptr(), bf16, sa, ta, 2, sb, tb, 2, sc, tc,
+                    2, sptr):
+                raise RuntimeError("launcher failed: %s" % P.cuda_get_backend_info())
+        for l in range(3):
+            rc = lib.pt_tensor_matmul_backward(ctypes.byref(H[l]), ctypes.byref(W[l]),
+                                               ctypes.byref(DC[l]), ctypes.byref(DA[l]),
+                                               ctypes.byref(DW[l]), sptr)
+            if rc != P.PT_OK:
+                raise RuntimeError(lib.pt_last_error())
+
+    inputs = [x] + Ws + dCs
+    outputs = dWs + [hs[3]]
+    h_in = [t.cpu().pin_memory() for t in inputs]
+    h_out = [torch.empty(t.shape, dtype=t.dtype).pin_memory() for t in outputs]
+
+    def e2e_step():
+        for d, h in zip(inputs, h_in):
+            d.copy_(h, non_blocking=True)
+        step()
+        for h, d in zip(h_out, outputs):
+            h.copy_(d, non_blocking=True)
+
+    return {
+        "step": step, "e2e_step": e2e_step, "flop": flop, "launches": 9,
+        "dtype": "bf16 (float32 gradients)", "flush": True, "peak_div": 1.0,
+        "data": "synthetic x U[0,1), W N(0,1/fan_in) in bf16, dC N(0,1) float32 on device",
+        "config": {"batch": batch, "layers": "784->1024->1024->10", "gemms_per_step": 9,
+                   "operands": "bfloat16 (forward bf16; dA, dW float32 via "
+                               "pt_tensor_matmul_backward, no cast copies)",
+                   "l2": "L2 flushed before every step (256 MB write, outside the timing)"},
+        "h2d": sum(t.numel() * t.element_size() for t in inputs),
+        "d2h": sum(t.numel() * t.element_size() for t in outputs),
+        "api": "cuda_low_precision_matmul_nd_launcher x3 + pt_tensor_matmul_backward x3 "
+               "with pinned-host copies on the stream",
+    }
+
+
 def setup_config4(w, rank, torch, P, lib, stream):
     """config4: the float32 MLP GEMM set (forward, dA, dW per layer)."""
     dims = w["mlp"]
@@ -493,6 +566,8 @@ def run_ours(args, w):
     stream = torch.cuda.current_stream()
     if args.workload == "config3":
         wl = setup_config3(w, rank, torch, P, lib, stream)
+    elif args.workload == "config4" and args.operand_dtype == "bfloat16":
+        wl = setup_config4_bf16(w, rank, torch, P, lib, stream)
     elif args.workload == "config4":
         P.cuda_set_matmul_precision(args.precision)
         wl = setup_config4(w, rank, torch, P, lib, stream)

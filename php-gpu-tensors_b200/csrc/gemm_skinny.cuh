@@ -99,7 +99,8 @@ __device__ __forceinline__ void skinny_store_out(const SimtParams &p, long long 
     E::store(p.c, oc + static_cast<long long>(m) * p.c_sm + static_cast<long long>(n) * p.c_sn, v);
 }
 
-template <typename T, int NB>
+// TA / TB: operand element types (widened to float on load), T the result's.
+template <typename T, int NB, typename TA = T, typename TB = T>
 __global__ void __launch_bounds__(kSkinnyThreads) skinny_gemm_kernel(const SimtParams p,
                                                                       const SkinnyArgs sa)
 {
@@ -143,8 +144,8 @@ __global__ void __launch_bounds__(kSkinnyThreads) skinny_gemm_kernel(const SimtP
                 const int kk = sa.a_k_major ? e % kSkinnyKC : e / kSkinnyBM;
                 const int m = m0 + row, k = k0 + kk;
                 ra[i] = (m < p.M && k < p.K)
-                            ? Acc(E::load(p.a, oa + static_cast<long long>(m) * p.a_sm +
-                                                   static_cast<long long>(k) * p.a_sk))
+                            ? Acc(Elem<TA>::load(p.a, oa + static_cast<long long>(m) * p.a_sm +
+                                                          static_cast<long long>(k) * p.a_sk))
                             : Acc(0);
             }
 #pragma unroll
@@ -154,8 +155,8 @@ __global__ void __launch_bounds__(kSkinnyThreads) skinny_gemm_kernel(const SimtP
                 const int kk = sa.b_n_major ? e / NB : e % kSkinnyKC;
                 const int k = k0 + kk;
                 rb[i] = (e < S::kBElems && n < p.N && k < p.K)
-                            ? Acc(E::load(p.b, ob + static_cast<long long>(k) * p.b_sk +
-                                                   static_cast<long long>(n) * p.b_sn))
+                            ? Acc(Elem<TB>::load(p.b, ob + static_cast<long long>(k) * p.b_sk +
+                                                          static_cast<long long>(n) * p.b_sn))
                             : Acc(0);
             }
         };

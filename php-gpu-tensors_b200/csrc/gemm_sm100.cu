@@ -24,6 +24,7 @@
 #include <cudaTypedefs.h>
 
 #include <algorithm>
+#include <type_traits>
 #include <cmath>
 #include <cstdint>
 #include <cstring>
@@ -761,7 +762,7 @@ cudaError_t launch_simt(const Problem &P, cudaStream_t stream)
 // Few-column products (N <= 32) on the split-K CUDA-core kernel.  The
 // cluster size C (1, 2, 4 or 8 CTAs splitting K) is the smallest that puts
 // about four CTAs on every SM while each CTA keeps at least four chunks.
-template <typename T, int NB>
+template <typename T, int NB, typename TA = T, typename TB = T>
 cudaError_t launch_skinny_nb(const Problem &P, DeviceState *ds, cudaStream_t stream)
 {
     const SimtParams s = simt_params(P);
@@ -790,7 +791,7 @@ cudaError_t launch_skinny_nb(const Problem &P, DeviceState *ds, cudaStream_t str
     cfg.attrs = attr;
     cfg.numAttrs = C > 1 ? 1 : 0;
     cudaError_t err;
-    if constexpr (sizeof(T) >= 4) {
+    if constexpr (sizeof(T) >= 4 && std::is_same<T, TA>::value && std::is_same<T, TB>::value) {
         // float32 / float64: the cp.async ring variant
         constexpr int smem = skinny_async_smem_bytes<T, NB>();
         const int base = KID_SKINNY_ASYNC + (sizeof(T) == 8 ? 12 : 0) + 2 * (NB <= 16 ? NB / 4 - 1 : NB == 24 ? 4 : 5);
@@ -805,12 +806,23 @@ cudaError_t launch_skinny_nb(const Problem &P, DeviceState *ds, cudaStream_t str
             err = cudaLaunchKernelEx(&cfg, skinny_async_kernel<T, NB, false>, s, sa);
         }
     } else {
-        err = cudaLaunchKernelEx(&cfg, skinny_gemm_kernel<T, NB>, s, sa);
+        err = cudaLaunchKernelEx(&cfg, skinny_gemm_kernel<T, NB, TA, TB>, s, sa);
     }
     t_last_grid = static_cast<int>(xc * C);
     t_last_block = kSkinnyThreads;
     t_last_cluster = C;
     return err != cudaSuccess ? err : cudaGetLastError();
+}
+
+// Mixed operand types (float32 result): the register-staged kernel, whose
+// warp layout needs a power-of-two NB.
+template <typename TA, typename TB>
+cudaError_t launch_skinny_mixed(const Problem &P, DeviceState *ds, cudaStream_t stream)
+{
+    if (P.N <= 4) return launch_skinny_nb<float, 4, TA, TB>(P, ds, stream);
+    if (P.N <= 8) return launch_skinny_nb<float, 8, TA, TB>(P, ds, stream);
+    if (P.N <= 16) return launch_skinny_nb<float, 16, TA, TB>(P, ds, stream);
+    return launch_skinny_nb<float, 32, TA, TB>(P, ds, stream);
 }
 
 // Column padding NB: 4, 8, 12, 16, 24 or 32 for float32/float64; the 16-bit
@@ -868,7 +880,18 @@ const char *skinny_name(int dt)
 int run_skinny(const Problem &P, DeviceState *ds, cudaStream_t stream)
 {
     cudaError_t err;
-    switch (P.dt) {
+    if (P.a_dt != P.dt || P.b_dt != P.dt) {
+        auto code = [](int dt) { return dt == DT_F32 ? 0 : (dt == DT_BF16 ? 1 : 2); };
+        switch (code(P.a_dt) * 3 + code(P.b_dt)) {
+        case 1: err = launch_skinny_mixed<float, __nv_bfloat16>(P, ds, stream); break;
+        case 2: err = launch_skinny_mixed<float, __half>(P, ds, stream); break;
+        case 3: err = launch_skinny_mixed<__nv_bfloat16, float>(P, ds, stream); break;
+        case 4: err = launch_skinny_mixed<__nv_bfloat16, __nv_bfloat16>(P, ds, stream); break;
+        case 6: err = launch_skinny_mixed<__half, float>(P, ds, stream); break;
+        case 8: err = launch_skinny_mixed<__half, __half>(P, ds, stream); break;
+        default: err = cudaErrorInvalidValue; break;
+        }
+    } else switch (P.dt) {
     case DT_F32: err = launch_skinny<float>(P, ds, stream); break;
     case DT_F64: err = launch_skinny<double>(P, ds, stream); break;
     case DT_F16: err = launch_skinny<__half>(P, ds, stream); break;
@@ -898,8 +921,9 @@ int run(Problem &P, cudaStream_t stream)
     const double work = static_cast<double>(P.M) * P.N * P.K * static_cast<double>(P.batches);
     const bool want_tc = P.K > 0 && t_path != 2 && (t_path == 1 || t_path == 3 || work >= kTcMinWork);
     const bool wide_out = P.a_dt != P.dt || P.b_dt != P.dt;   // float32 result, 16-bit operand(s)
-    const bool skinny_fit = !wide_out && P.N > 0 && P.N <= kSkinnyMaxN && P.M > 0 &&
-                            P.batches > 0 && P.K >= kSkinnyMinK;
+    const bool skinny_fit = P.N > 0 && P.N <= kSkinnyMaxN && P.M > 0 && P.batches > 0 &&
+                            P.K >= kSkinnyMinK;
+    // float32 / float64 results, mixed-type gradient products included
     const bool wide_acc = P.dt == DT_F32 || P.dt == DT_F64;
     if (skinny_fit && (t_path == 4 || (t_path == 0 && wide_acc)))
         return run_skinny(P, ds, stream);

@@ -544,6 +544,8 @@ MIXED_CASES = [
     ("f16_f16", [256, 512], [512, 384], False, True, "float16", "float16", "tc-f16-f32out"),
     ("f32_f16_simt", [130, 300], [300, 70], False, False, "float32", "float16", "simt-"),
     ("f32_bf16_short_k", [200, 8], [8, 136], False, True, "float32", "bfloat16", "simt-"),
+    ("bf16_f32_few_cols", [1024, 4096], [4096, 10], True, False, "bfloat16", "float32", "skinny-"),
+    ("f32_f16_few_cols", [300, 1000], [1000, 6], False, False, "float32", "float16", "skinny-"),
 ]
 
 
