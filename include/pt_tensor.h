@@ -109,7 +109,21 @@ int pt_tensor_matmul_backward(const pt_tensor *a, const pt_tensor *b, const pt_t
 int pt_host_matmul(const void *a, const void *b, void *c, dtype_t dtype, int batches, int M,
                    int N, int K, int b_shared, int chunks, int flags);
 
-/* Frees this thread's pt_host_matmul streams and staging (synchronises them). */
+/* pt_host_matmul over several devices of this process: the batch axis is cut
+ * into ndev contiguous shards (sizes differing by at most one, shard g on
+ * devices[g]), each streamed in `chunks` pieces through that device's own
+ * pipeline as above, with chunk i enqueued on every device before chunk i+1
+ * so that every device's PCIe link copies at the same time -- the
+ * host-staged form of the batch-sharded product (toGpu / fromBuffer
+ * transfers feeding the sharded path, src/cuda_array/tensor_transfer.c).  A
+ * shared B is copied to every device.  Devices must be distinct; the
+ * caller's current device is restored.  Blocks until C is on the host. */
+int pt_host_matmul_sharded(const void *a, const void *b, void *c, dtype_t dtype, int batches,
+                           int M, int N, int K, int b_shared, const int *devices, int ndev,
+                           int chunks, int flags);
+
+/* Frees this thread's pt_host_matmul streams and staging on every device
+ * (synchronises them). */
 void pt_host_release(void);
 
 #ifdef __cplusplus

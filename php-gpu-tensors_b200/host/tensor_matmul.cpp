@@ -389,8 +389,10 @@ struct HostPipeline {
     size_t stage_bytes = 0;
 };
 
-thread_local HostPipeline t_pipe;
+constexpr int kMaxPipeDevices = 64;
+thread_local HostPipeline t_pipes[kMaxPipeDevices];
 
+// Frees one device's pipeline (switches to that device and back).
 void release_pipeline(HostPipeline &p)
 {
     if (p.device < 0)
@@ -415,17 +417,15 @@ void release_pipeline(HostPipeline &p)
     p = HostPipeline();
 }
 
-// Makes the pipeline ready on the current device with at least `bytes` of
-// staging.  Returns a cudaError_t.
-cudaError_t prepare_pipeline(size_t bytes)
+// Makes device `dev`'s pipeline ready with at least `bytes` of staging; `dev`
+// must be the current device.  Returns a cudaError_t.
+cudaError_t prepare_pipeline(int dev, size_t bytes)
 {
-    int dev = -1;
-    cudaError_t e = cudaGetDevice(&dev);
-    if (e != cudaSuccess)
-        return e;
-    HostPipeline &p = t_pipe;
+    if (dev < 0 || dev >= kMaxPipeDevices)
+        return cudaErrorInvalidDevice;
+    cudaError_t e;
+    HostPipeline &p = t_pipes[dev];
     if (p.device != dev) {
-        release_pipeline(p);
         p.device = dev;
         if ((e = cudaStreamCreateWithFlags(&p.s_in, cudaStreamNonBlocking)) != cudaSuccess ||
             (e = cudaStreamCreateWithFlags(&p.s_comp, cudaStreamNonBlocking)) != cudaSuccess ||
@@ -456,15 +456,104 @@ cudaError_t prepare_pipeline(size_t bytes)
 
 size_t round256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
 
-} // namespace
+// One device's share of a host-buffer product: batches [first, first +
+// count) cut into chunks of `per`, double-buffered through two staging slots.
+struct HostShard {
+    int device;
+    int first, count, per, chunks;
+    HostPipeline *p;
+};
 
-PT_API void pt_host_release(void)
+struct HostJob {
+    const void *a, *b;
+    void *c;
+    dtype_t dtype;
+    int M, N, K, b_shared, flags;
+    size_t a_b, b_b, c_b;   // bytes per batch
+};
+
+size_t slot_bytes_for(const HostJob &j, int per, size_t *sa, size_t *sb)
 {
-    release_pipeline(t_pipe);
+    *sa = round256(j.a_b * per);
+    *sb = j.b_shared ? 0 : round256(j.b_b * per);
+    return *sa + *sb + round256(j.c_b * per);
 }
 
-PT_API int pt_host_matmul(const void *a, const void *b, void *c, dtype_t dtype, int batches, int M,
-                          int N, int K, int b_shared, int chunks, int flags)
+// Enqueues chunk i of a shard (its device is current): H2D of A (and B) on
+// s_in, the product on s_comp, D2H of C on s_out, slots recycled through
+// events only -- the host never waits here.  Returns PT_OK or an error.
+int enqueue_chunk(const HostJob &j, const HostShard &sh, int i)
+{
+    HostPipeline &p = *sh.p;
+    const int b0 = sh.first + i * sh.per;
+    const int nb = (i + 1) * sh.per <= sh.count ? sh.per : sh.count - i * sh.per;
+    if (nb <= 0)
+        return PT_OK;
+    size_t sa, sb;
+    const size_t slot = slot_bytes_for(j, sh.per, &sa, &sb);
+    const int k = i & 1;
+    char *a_s = static_cast<char *>(p.stage) + k * slot, *b_s = a_s + sa, *c_s = b_s + sb;
+    char *b_dev = static_cast<char *>(p.stage) + 2 * slot;
+    auto err = [](cudaError_t e) {
+        return fail(PT_RUNTIME, "Host matmul failed (CUDA error %d)", static_cast<int>(e));
+    };
+    cudaError_t e;
+    if (i >= 2) {
+        // slot reuse: the product of chunk i-2 has read its inputs and its
+        // result has been copied out
+        if ((e = cudaStreamWaitEvent(p.s_in, p.compute_done[k], 0)) != cudaSuccess ||
+            (e = cudaStreamWaitEvent(p.s_comp, p.out_done[k], 0)) != cudaSuccess)
+            return err(e);
+    }
+    if ((e = cudaMemcpyAsync(a_s, static_cast<const char *>(j.a) + j.a_b * b0, j.a_b * nb,
+                             cudaMemcpyHostToDevice, p.s_in)) != cudaSuccess)
+        return err(e);
+    if (!j.b_shared &&
+        (e = cudaMemcpyAsync(b_s, static_cast<const char *>(j.b) + j.b_b * b0, j.b_b * nb,
+                             cudaMemcpyHostToDevice, p.s_in)) != cudaSuccess)
+        return err(e);
+    if ((e = cudaEventRecord(p.in_done[k], p.s_in)) != cudaSuccess ||
+        (e = cudaStreamWaitEvent(p.s_comp, p.in_done[k], 0)) != cudaSuccess)
+        return err(e);
+    pt_tensor ta, tb, tc;
+    std::memset(&ta, 0, sizeof(ta));
+    ta.data = a_s;
+    ta.dtype = j.dtype;
+    ta.ndims = 3;
+    ta.shape[0] = nb; ta.shape[1] = j.M; ta.shape[2] = j.K;
+    contiguous_strides(ta.shape, 3, ta.strides);
+    tb = ta;
+    if (j.b_shared) {
+        tb.data = b_dev;
+        tb.ndims = 2;
+        tb.shape[0] = j.K; tb.shape[1] = j.N;
+        contiguous_strides(tb.shape, 2, tb.strides);
+    } else {
+        tb.data = b_s;
+        tb.shape[1] = j.K; tb.shape[2] = j.N;
+        contiguous_strides(tb.shape, 3, tb.strides);
+    }
+    tc = ta;
+    tc.data = c_s;
+    tc.shape[1] = j.M; tc.shape[2] = j.N;
+    contiguous_strides(tc.shape, 3, tc.strides);
+    const int st = pt_tensor_matmul_into(&ta, &tb, &tc, j.flags, p.s_comp);
+    if (st != PT_OK)
+        return st;
+    if ((e = cudaEventRecord(p.compute_done[k], p.s_comp)) != cudaSuccess ||
+        (e = cudaStreamWaitEvent(p.s_out, p.compute_done[k], 0)) != cudaSuccess ||
+        (e = cudaMemcpyAsync(static_cast<char *>(j.c) + j.c_b * b0, c_s, j.c_b * nb,
+                             cudaMemcpyDeviceToHost, p.s_out)) != cudaSuccess ||
+        (e = cudaEventRecord(p.out_done[k], p.s_out)) != cudaSuccess)
+        return err(e);
+    return PT_OK;
+}
+
+// Shards the batch over `ndev` devices and runs their pipelines side by side
+// from this thread; restores the caller's current device.
+int host_matmul_devices(const void *a, const void *b, void *c, dtype_t dtype, int batches, int M,
+                        int N, int K, int b_shared, const int *devices, int ndev, int chunks,
+                        int flags)
 {
     if (!supported_dtype(dtype, flags))
         return fail(PT_INVALID_ARGUMENT,
@@ -473,105 +562,106 @@ PT_API int pt_host_matmul(const void *a, const void *b, void *c, dtype_t dtype, 
         (!a && static_cast<long long>(M) * K != 0) || (!b && static_cast<long long>(K) * N != 0) ||
         (!c && static_cast<long long>(M) * N != 0))
         return fail(PT_INVALID_ARGUMENT, "Matrix multiplication failed - incompatible dimensions");
+    if (ndev < 1 || ndev > kMaxPipeDevices || !devices)
+        return fail(PT_INVALID_ARGUMENT, "host matmul needs between 1 and 64 devices");
+    for (int g = 0; g < ndev; g++)
+        for (int h = 0; h < g; h++)
+            if (devices[g] == devices[h] || devices[g] < 0 || devices[g] >= kMaxPipeDevices)
+                return fail(PT_INVALID_ARGUMENT, "host matmul devices must be distinct, got %d",
+                            devices[g]);
     if (batches == 0 || M == 0 || N == 0)
         return ok();
+    HostJob j;
+    j.a = a; j.b = b; j.c = c; j.dtype = dtype;
+    j.M = M; j.N = N; j.K = K; j.b_shared = b_shared; j.flags = flags;
     const size_t es = element_size(dtype);
+    j.a_b = static_cast<size_t>(M) * K * es;
+    j.b_b = static_cast<size_t>(K) * N * es;
+    j.c_b = static_cast<size_t>(M) * N * es;
     if (chunks < 1)
         chunks = 1;
-    if (chunks > batches)
-        chunks = batches;
-    const int per = (batches + chunks - 1) / chunks;   // batches per chunk (last may be shorter)
-    const size_t a_b = static_cast<size_t>(M) * K * es;   // bytes per batch
-    const size_t b_b = static_cast<size_t>(K) * N * es;
-    const size_t c_b = static_cast<size_t>(M) * N * es;
-    const size_t sa = round256(a_b * per), sb = b_shared ? 0 : round256(b_b * per);
-    const size_t sc = round256(c_b * per), slot_bytes = sa + sb + sc;
-    const size_t shared_b = b_shared ? round256(b_b) : 0;
 
-    cudaError_t e = prepare_pipeline(2 * slot_bytes + shared_b);
+    int prev = -1;
+    cudaGetDevice(&prev);
+    HostShard shards[kMaxPipeDevices];
+    int nsh = 0, status = PT_OK, max_chunks = 0;
+    const int base = batches / ndev, extra = batches % ndev;
+    for (int g = 0, first = 0; g < ndev && status == PT_OK; g++) {
+        HostShard &sh = shards[nsh];
+        sh.device = devices[g];
+        sh.first = first;
+        sh.count = base + (g < extra ? 1 : 0);
+        first += sh.count;
+        if (sh.count == 0)
+            continue;
+        sh.chunks = chunks < sh.count ? chunks : sh.count;
+        sh.per = (sh.count + sh.chunks - 1) / sh.chunks;
+        size_t sa, sb;
+        const size_t slot = slot_bytes_for(j, sh.per, &sa, &sb);
+        cudaError_t e = cudaSetDevice(sh.device);
+        if (e == cudaSuccess)
+            e = prepare_pipeline(sh.device, 2 * slot + (b_shared ? round256(j.b_b) : 0));
+        if (e == cudaSuccess && b_shared)
+            e = cudaMemcpyAsync(static_cast<char *>(t_pipes[sh.device].stage) + 2 * slot, b, j.b_b,
+                                cudaMemcpyHostToDevice, t_pipes[sh.device].s_comp);
+        if (e != cudaSuccess) {
+            status = fail(PT_RUNTIME, "Host matmul staging set-up failed (CUDA error %d)",
+                          static_cast<int>(e));
+            break;
+        }
+        sh.p = &t_pipes[sh.device];
+        max_chunks = sh.chunks > max_chunks ? sh.chunks : max_chunks;
+        nsh++;
+    }
+    // chunk i on every device before chunk i + 1, so all links copy at once
+    for (int i = 0; i < max_chunks && status == PT_OK; i++)
+        for (int g = 0; g < nsh && status == PT_OK; g++) {
+            if (i >= shards[g].chunks)
+                continue;
+            const cudaError_t e = cudaSetDevice(shards[g].device);
+            status = e == cudaSuccess ? enqueue_chunk(j, shards[g], i)
+                                      : fail(PT_RUNTIME, "Host matmul failed (CUDA error %d)",
+                                             static_cast<int>(e));
+        }
+    // drain every device's streams (also on the error path) before returning
+    for (int g = 0; g < nsh; g++) {
+        cudaSetDevice(shards[g].device);
+        const cudaError_t e1 = cudaStreamSynchronize(shards[g].p->s_in);
+        const cudaError_t e2 = cudaStreamSynchronize(shards[g].p->s_comp);
+        const cudaError_t e3 = cudaStreamSynchronize(shards[g].p->s_out);
+        const cudaError_t e = e1 != cudaSuccess ? e1 : (e2 != cudaSuccess ? e2 : e3);
+        if (e != cudaSuccess && status == PT_OK)
+            status = fail(PT_RUNTIME, "Host matmul failed (CUDA error %d)", static_cast<int>(e));
+    }
+    if (prev >= 0)
+        cudaSetDevice(prev);
+    return status == PT_OK ? ok() : status;
+}
+
+} // namespace
+
+PT_API void pt_host_release(void)
+{
+    for (int d = 0; d < kMaxPipeDevices; d++)
+        release_pipeline(t_pipes[d]);
+}
+
+PT_API int pt_host_matmul(const void *a, const void *b, void *c, dtype_t dtype, int batches, int M,
+                          int N, int K, int b_shared, int chunks, int flags)
+{
+    int dev = -1;
+    const cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess)
         return fail(PT_RUNTIME, "Host matmul staging set-up failed (CUDA error %d)",
                     static_cast<int>(e));
-    HostPipeline &p = t_pipe;
-    char *stage = static_cast<char *>(p.stage);
-    char *b_dev = stage + 2 * slot_bytes;
-    int status = PT_OK;
-    auto cuda_ok = [&](cudaError_t err) {
-        if (err == cudaSuccess)
-            return true;
-        if (status == PT_OK)
-            status = fail(PT_RUNTIME, "Host matmul failed (CUDA error %d)", static_cast<int>(err));
-        return false;
-    };
-    // the previous call on this thread is complete (it synchronised), so the
-    // staging is free; start with the shared B
-    bool good = !b_shared ||
-                cuda_ok(cudaMemcpyAsync(b_dev, b, b_b, cudaMemcpyHostToDevice, p.s_comp));
+    return host_matmul_devices(a, b, c, dtype, batches, M, N, K, b_shared, &dev, 1, chunks,
+                               flags);
+}
 
-    for (int i = 0; good && i < chunks; i++) {
-        const int b0 = i * per;
-        const int nb = (b0 + per <= batches) ? per : batches - b0;
-        if (nb <= 0)
-            break;
-        const int k = i & 1;
-        char *a_s = stage + k * slot_bytes, *b_s = a_s + sa, *c_s = b_s + sb;
-        if (i >= 2) {
-            // slot reuse: the product of chunk i-2 has read its inputs and its
-            // result has been copied out
-            good = cuda_ok(cudaStreamWaitEvent(p.s_in, p.compute_done[k], 0)) &&
-                   cuda_ok(cudaStreamWaitEvent(p.s_comp, p.out_done[k], 0));
-        }
-        good = good &&
-               cuda_ok(cudaMemcpyAsync(a_s, static_cast<const char *>(a) + a_b * b0, a_b * nb,
-                                       cudaMemcpyHostToDevice, p.s_in)) &&
-               (b_shared ||
-                cuda_ok(cudaMemcpyAsync(b_s, static_cast<const char *>(b) + b_b * b0, b_b * nb,
-                                        cudaMemcpyHostToDevice, p.s_in))) &&
-               cuda_ok(cudaEventRecord(p.in_done[k], p.s_in)) &&
-               cuda_ok(cudaStreamWaitEvent(p.s_comp, p.in_done[k], 0));
-        if (!good)
-            break;
-        pt_tensor ta, tb, tc;
-        std::memset(&ta, 0, sizeof(ta));
-        ta.data = a_s;
-        ta.dtype = dtype;
-        ta.ndims = 3;
-        ta.shape[0] = nb; ta.shape[1] = M; ta.shape[2] = K;
-        contiguous_strides(ta.shape, 3, ta.strides);
-        tb = ta;
-        if (b_shared) {
-            tb.data = b_dev;
-            tb.ndims = 2;
-            tb.shape[0] = K; tb.shape[1] = N;
-            contiguous_strides(tb.shape, 2, tb.strides);
-        } else {
-            tb.data = b_s;
-            tb.shape[1] = K; tb.shape[2] = N;
-            contiguous_strides(tb.shape, 3, tb.strides);
-        }
-        tc = ta;
-        tc.data = c_s;
-        tc.shape[1] = M; tc.shape[2] = N;
-        contiguous_strides(tc.shape, 3, tc.strides);
-        const int st = pt_tensor_matmul_into(&ta, &tb, &tc, flags, p.s_comp);
-        if (st != PT_OK) {
-            status = st;
-            good = false;
-            break;
-        }
-        good = cuda_ok(cudaEventRecord(p.compute_done[k], p.s_comp)) &&
-               cuda_ok(cudaStreamWaitEvent(p.s_out, p.compute_done[k], 0)) &&
-               cuda_ok(cudaMemcpyAsync(static_cast<char *>(c) + c_b * b0, c_s, c_b * nb,
-                                       cudaMemcpyDeviceToHost, p.s_out)) &&
-               cuda_ok(cudaEventRecord(p.out_done[k], p.s_out));
-    }
-    // drain all three streams (also on the error path) before returning
-    const cudaError_t e1 = cudaStreamSynchronize(p.s_in);
-    const cudaError_t e2 = cudaStreamSynchronize(p.s_comp);
-    const cudaError_t e3 = cudaStreamSynchronize(p.s_out);
-    if (good)
-        good = cuda_ok(e1) && cuda_ok(e2) && cuda_ok(e3);
-    if (good && status == PT_OK)
-        return ok();
-    return status;
+PT_API int pt_host_matmul_sharded(const void *a, const void *b, void *c, dtype_t dtype,
+                                  int batches, int M, int N, int K, int b_shared,
+                                  const int *devices, int ndev, int chunks, int flags)
+{
+    return host_matmul_devices(a, b, c, dtype, batches, M, N, K, b_shared, devices, ndev, chunks,
+                               flags);
 }

@@ -141,6 +141,8 @@ _SIGNATURES = {
                                                      ctypes.c_int, ctypes.c_int, ctypes.c_int,
                                                      ctypes.c_void_p]),
     "pt_host_matmul": (ctypes.c_int, [ctypes.c_void_p] * 3 + [ctypes.c_int] * 8),
+    "pt_host_matmul_sharded": (ctypes.c_int, [ctypes.c_void_p] * 3 + [ctypes.c_int] * 6 +
+                               [ctypes.POINTER(ctypes.c_int)] + [ctypes.c_int] * 3),
     "pt_host_release": (None, []),
     "pt_last_error": (ctypes.c_char_p, []),
     "pt_matmul_result_shape": (ctypes.c_int, [ctypes.POINTER(PtTensor)] * 2 +
@@ -387,10 +389,12 @@ class CudaArray:
         return t.numpy()
 
 
-def host_matmul(a, b, c, chunks=8, allow_float64=False):
+def host_matmul(a, b, c, chunks=8, allow_float64=False, devices=None):
     """Batched product between HOST torch tensors (pinned for overlap):
     a [batches, M, K], b [batches, K, N] or [K, N] (shared), c [batches, M, N]
-    are filled through pt_host_matmul, whose copies and products overlap."""
+    are filled through pt_host_matmul, whose copies and products overlap.
+    devices=[d0, d1, ...] shards the batch over those GPUs of this process
+    (pt_host_matmul_sharded), `chunks` pieces per device."""
     torch = _torch()
     rev = {torch.float32: "float32", torch.float64: "float64", torch.float16: "float16",
            torch.bfloat16: "bfloat16"}
@@ -403,9 +407,16 @@ def host_matmul(a, b, c, chunks=8, allow_float64=False):
     if (b.shape[-2] != K or list(c.shape) != [batches, M, N]
             or (not shared and b.shape[0] != batches)):
         raise InvalidArgumentException("Matrix multiplication failed - incompatible dimensions")
-    _raise_for(library().pt_host_matmul(
-        a.data_ptr(), b.data_ptr(), c.data_ptr(), DTYPE_CODES[dt], batches, M, N, K,
-        1 if shared else 0, chunks, PT_MATMUL_ALLOW_FLOAT64 if allow_float64 else 0))
+    flags = PT_MATMUL_ALLOW_FLOAT64 if allow_float64 else 0
+    if devices is None:
+        _raise_for(library().pt_host_matmul(
+            a.data_ptr(), b.data_ptr(), c.data_ptr(), DTYPE_CODES[dt], batches, M, N, K,
+            1 if shared else 0, chunks, flags))
+    else:
+        devs = (ctypes.c_int * len(devices))(*devices)
+        _raise_for(library().pt_host_matmul_sharded(
+            a.data_ptr(), b.data_ptr(), c.data_ptr(), DTYPE_CODES[dt], batches, M, N, K,
+            1 if shared else 0, devs, len(devices), chunks, flags))
     return c
 
 

@@ -163,3 +163,34 @@ def test_tensor_layer_errors_without_gpu(golden):
     a, b, r = _pt([0, 3], "float32"), _pt([3, 4], "float32"), _pt([0, 4], "float32")
     assert lib.pt_tensor_matmul_into(ctypes.byref(a), ctypes.byref(b), ctypes.byref(r), 0,
                                      s) == P.PT_OK
+
+
+def test_gradient_and_host_staging_errors_without_gpu():
+    """Argument errors of pt_tensor_matmul_backward and pt_host_matmul_sharded
+    are reported before any CUDA call."""
+    lib = P.library()
+    s = ctypes.c_void_p(0)
+    # operands of different types
+    a, b, g = _pt([3, 4], "float32"), _pt([4, 5], "bfloat16"), _pt([3, 5], "float32")
+    ga = _pt([3, 4], "float32")
+    assert lib.pt_tensor_matmul_backward(ctypes.byref(a), ctypes.byref(b), ctypes.byref(g),
+                                         ctypes.byref(ga), None, s) == P.PT_INVALID_ARGUMENT
+    assert b"matmul backward requires" in lib.pt_last_error()
+    # a gradient of a 16-bit operand must be float32
+    a, b = _pt([3, 4], "bfloat16"), _pt([4, 5], "bfloat16")
+    ga = _pt([3, 4], "bfloat16")
+    assert lib.pt_tensor_matmul_backward(ctypes.byref(a), ctypes.byref(b), ctypes.byref(g),
+                                         ctypes.byref(ga), None, s) == P.PT_INVALID_ARGUMENT
+    assert lib.pt_last_error() == b"matmul gradients are float32 tensors"
+    # a gradient shape that is not a reduction of the product's batch shape
+    a, b, g = _pt([2, 3, 4], "float32"), _pt([4, 5], "float32"), _pt([2, 3, 5], "float32")
+    gb = _pt([3, 4, 5], "float32")
+    assert lib.pt_tensor_matmul_backward(ctypes.byref(a), ctypes.byref(b), ctypes.byref(g),
+                                         None, ctypes.byref(gb), s) == P.PT_INVALID_ARGUMENT
+    assert lib.pt_last_error().startswith(b"Gradient shape cannot be reduced")
+    # sharded host staging: the device list is checked first
+    devs = (ctypes.c_int * 2)(0, 0)
+    assert lib.pt_host_matmul_sharded(16, 16, 16, P.DTYPE_CODES["float32"], 4, 2, 2, 2, 0, devs,
+                                      2, 2, 0) == P.PT_INVALID_ARGUMENT
+    assert lib.pt_host_matmul_sharded(16, 16, 16, P.DTYPE_CODES["float32"], 4, 2, 2, 2, 0, devs,
+                                      0, 2, 0) == P.PT_INVALID_ARGUMENT

@@ -699,3 +699,25 @@ def test_host_matmul_streams_equal_device_product(dtype, shared):
     assert torch.equal(c, ref.cpu())
     with pytest.raises(P.InvalidArgumentException):
         P.host_matmul(a, b, torch.empty(batches, M, N + 1, dtype=tdt))
+
+
+@pytest.mark.parametrize("dtype", ["bfloat16", "float32"])
+def test_host_matmul_sharded_over_devices(dtype):
+    """pt_host_matmul_sharded: the batch cut over every GPU of this process
+    (one on a single-GPU box), chunks pipelined per device, equals the device
+    product; a shared B reaches every device."""
+    tdt = TORCH_DT[dtype]
+    devices = list(range(torch.cuda.device_count()))
+    g = torch.Generator().manual_seed(12)
+    batches, M, N, K = 9, 256, 264, 320
+    a = torch.randn(batches, M, K, generator=g).to(tdt).pin_memory()
+    for shared in (False, True):
+        b = (torch.randn(K, N, generator=g) if shared
+             else torch.randn(batches, K, N, generator=g)).to(tdt).pin_memory()
+        c = torch.full((batches, M, N), float("nan"), dtype=tdt).pin_memory()
+        P.host_matmul(a, b, c, chunks=2, devices=devices)
+        torch.cuda.set_device(0)
+        ref = torch.matmul(a.cuda().double(), b.cuda().double()).cpu()
+        err = (c.double() - ref).abs().max() / ref.abs().max()
+        assert err <= (1e-2 if dtype == "bfloat16" else 1e-5), (shared, float(err))
+        assert torch.cuda.current_device() == 0
