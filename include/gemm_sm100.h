@@ -240,9 +240,17 @@ int gemm_sm100_set_path(int path);
 
 /* Reads (and with clear != 0 resets) the device status word of `device`:
  * 0 = no kernel has reported a problem; 1..4 = a tensor-core kernel gave up a
- * bounded wait (producer, MMA, epilogue, split stage) and returned early.
+ * bounded wait (producer, MMA, epilogue, split stage) and returned early;
+ * 5 = gemm_sm100_selftest_wait_timeout ran.
  * Synchronises the device.  Returns -1 if the device cannot be queried. */
 int gemm_sm100_device_status(int device, int clear);
+
+/* Failure-detection self-test (no counterpart in the reference): launches on
+ * `stream` one warp that waits, with the same bounded mbarrier wait every
+ * tensor-core kernel uses, on a barrier nothing completes.  The wait gives up
+ * after its 2 s limit, the kernel records status 5 in the device status word
+ * and returns; the context stays usable.  Returns 1 if the launch was made. */
+int gemm_sm100_selftest_wait_timeout(cudaStream_t stream);
 
 /* Human-readable name of a tuning algorithm_id. */
 const char *gemm_sm100_algorithm_name(int algorithm_id);

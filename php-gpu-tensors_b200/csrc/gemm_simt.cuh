@@ -6,7 +6,9 @@
 // and more than three non-mergeable batch axes.  It also carries FP64.
 // Each output is accumulated with fma in k order starting from zero, the same
 // sequence as the reference's host loop (src/contiguous_array_ce.c:1327-1333),
-// so float32 and float64 results here are bit-identical to that loop.
+// so float32 and float64 results here are bit-identical to that loop.  Folded
+// batch axes (a gradient summed over the axes its operand was broadcast
+// along) are walked outside the k loop, in row-major order.
 #pragma once
 
 #include <cuda_bf16.h>
@@ -32,6 +34,13 @@ struct SimtParams {
     long long a_sm, a_sk, b_sk, b_sn, c_sm, c_sn;
     const void *bias;
     int act;
+    // batch axes summed into the product (gradient of a broadcast operand):
+    // each output accumulates A[f] . B[f] over every fold coordinate f
+    int nfd;
+    int fshape[kSimtMaxBatchDims];
+    long long a_fs[kSimtMaxBatchDims];
+    long long b_fs[kSimtMaxBatchDims];
+    long long folds;   // product of fshape (1 without folding)
 };
 
 template <typename T>
@@ -127,6 +136,17 @@ __global__ void __launch_bounds__(256) simt_gemm_kernel(const SimtParams p)
             for (int j = 0; j < 4; j++)
                 acc[i][j] = Acc(0);
 
+        const long long oa0 = oa, ob0 = ob;
+        for (long long f = 0; f < p.folds; f++) {
+        oa = oa0;
+        ob = ob0;
+        long long frem = f;
+        for (int d = p.nfd - 1; d >= 0; d--) {
+            const long long coord = frem % p.fshape[d];
+            frem /= p.fshape[d];
+            oa += coord * p.a_fs[d];
+            ob += coord * p.b_fs[d];
+        }
         for (int k0 = 0; k0 < p.K; k0 += kSimtBK) {
 #pragma unroll
             for (int r = 0; r < 4; r++) {
@@ -156,6 +176,7 @@ __global__ void __launch_bounds__(256) simt_gemm_kernel(const SimtParams p)
             }
             __syncthreads();
         }
+        }   // folds
 #pragma unroll
         for (int i = 0; i < 4; i++) {
             const int m = m0 + ty + 16 * i;

@@ -67,6 +67,11 @@ struct Problem {
     int forced_bn;                 // 0 = heuristic / tuned plan
     int a_dt, b_dt;                // operand dtypes (dt is the result's; they differ only
                                    // for the float32-result gradient products)
+    int nfd;                       // batch axes summed into the product (0 = none)
+    int fshape[kMaxBatchDims];
+    long long a_fs[kMaxBatchDims]; // element strides along the summed axes, 0 = broadcast
+    long long b_fs[kMaxBatchDims];
+    long long folds;               // product of fshape
 };
 
 // ------------------------------------------------------------ thread state
@@ -171,6 +176,7 @@ int build_problem(int dt, const void *a, const void *b, void *c, const int *sa, 
     P->dt = dt;
     P->a_dt = dt;
     P->b_dt = dt;
+    P->folds = 1;
     P->a = a;
     P->b = b;
     P->c = c;
@@ -213,6 +219,94 @@ int build_problem(int dt, const void *a, const void *b, void *c, const int *sa, 
         return 2;
     if (!c || (inner > 0 && (!a || !b)))
         return 0;
+    return 1;
+}
+
+// As build_problem, but C's batch axes may be a reduction of the broadcast
+// batch shape of A and B: an axis where C has extent 1 (or no axis) while the
+// product has extent > 1 is summed into the product (fshape, a_fs, b_fs).
+int build_fold_problem(int dt, const void *a, const void *b, void *c, const int *sa,
+                       const size_t *ta, int na, const int *sb, const size_t *tb, int nb,
+                       const int *sc, const size_t *tc, int nc, Problem *P)
+{
+    if (na < 2 || nb < 2 || nc < 2 || na > MAX_DIMS || nb > MAX_DIMS || nc > MAX_DIMS)
+        return 0;
+    if (!sa || !sb || !sc || !ta || !tb || !tc)
+        return 0;
+    const int rows = sa[na - 2], inner = sa[na - 1], cols = sb[nb - 1];
+    if (inner != sb[nb - 2] || rows < 0 || inner < 0 || cols < 0 || sc[nc - 2] != rows ||
+        sc[nc - 1] != cols)
+        return 0;
+    const int nba = na - 2, nbb = nb - 2, nbc = nc - 2;
+    const int nfull = nba > nbb ? nba : nbb;
+    if (nbc > nfull)
+        return 0;
+    std::memset(P, 0, sizeof(*P));
+    P->dt = P->a_dt = P->b_dt = dt;
+    P->a = a;
+    P->b = b;
+    P->c = c;
+    P->M = rows;
+    P->N = cols;
+    P->K = inner;
+    bool empty = rows == 0 || cols == 0, fold_empty = false;
+    long long batches = 1, folds = 1;
+    for (int d = 0; d < nfull; d++) {
+        const int ia = d - (nfull - nba), ib = d - (nfull - nbb), ic = d - (nfull - nbc);
+        const int ea = ia >= 0 ? sa[ia] : 1, eb = ib >= 0 ? sb[ib] : 1;
+        if (ea < 0 || eb < 0 || (ea != 1 && eb != 1 && ea != eb))
+            return 0;
+        const int ext = ea == 1 ? eb : ea;
+        const int ec = ic >= 0 ? sc[ic] : 1;
+        if (ec != ext && ec != 1)
+            return 0;
+        if (ext == 0) {
+            if (ec == 0)
+                empty = true;        // C itself is empty
+            else
+                fold_empty = true;   // a sum over nothing: C = 0
+            continue;
+        }
+        if (ext == 1)
+            continue;
+        const long long as = ea != 1 ? static_cast<long long>(ta[ia]) : 0;
+        const long long bs = eb != 1 ? static_cast<long long>(tb[ib]) : 0;
+        if (ec == ext) {
+            if (batches > (1ll << 40) / ext)
+                return 0;
+            batches *= ext;
+            const int k = P->nbd++;
+            P->bshape[k] = ext;
+            P->a_bs[k] = as;
+            P->b_bs[k] = bs;
+            P->c_bs[k] = static_cast<long long>(tc[ic]);
+        } else {
+            if (folds > (1ll << 40) / ext)
+                return 0;
+            folds *= ext;
+            const int k = P->nfd++;
+            P->fshape[k] = ext;
+            P->a_fs[k] = as;
+            P->b_fs[k] = bs;
+        }
+    }
+    P->batches = batches;
+    P->folds = folds;
+    P->a_sm = static_cast<long long>(ta[na - 2]);
+    P->a_sk = static_cast<long long>(ta[na - 1]);
+    P->b_sk = static_cast<long long>(tb[nb - 2]);
+    P->b_sn = static_cast<long long>(tb[nb - 1]);
+    P->c_sm = static_cast<long long>(tc[nc - 2]);
+    P->c_sn = static_cast<long long>(tc[nc - 1]);
+    if (empty)
+        return 2;
+    if (!c || (!fold_empty && inner > 0 && (!a || !b)))
+        return 0;
+    // a sum over an empty axis leaves C = 0: the CUDA-core kernel writes it
+    if (fold_empty) {
+        P->folds = 0;
+        P->nfd = 0;
+    }
     return 1;
 }
 
@@ -324,6 +418,64 @@ bool merge_batches(const Problem &P, TcBatch *out)
 }
 
 // Appends an operand's present batch axes to its map and records their slots.
+// Merged summed (fold) axes of a tensor-core launch: as merge_batches, for A
+// and B only.
+struct TcFold {
+    int nfd;
+    int fshape[3];
+    long long a[3], b[3];
+};
+
+bool merge_folds(const Problem &P, TcFold *out)
+{
+    int n = P.nfd;
+    long long ext[kMaxBatchDims], sa[kMaxBatchDims], sb[kMaxBatchDims];
+    for (int d = 0; d < n; d++) {
+        ext[d] = P.fshape[d];
+        sa[d] = P.a_fs[d];
+        sb[d] = P.b_fs[d];
+    }
+    auto composable = [](long long outer, long long inner, long long inner_ext) {
+        return (outer == 0 && inner == 0) || (outer != 0 && inner != 0 && outer == inner * inner_ext);
+    };
+    for (int d = n - 1; d > 0; d--) {
+        if (composable(sa[d - 1], sa[d], ext[d]) && composable(sb[d - 1], sb[d], ext[d]) &&
+            ext[d - 1] * ext[d] < (1ll << 31)) {
+            ext[d - 1] *= ext[d];
+            sa[d - 1] = sa[d];
+            sb[d - 1] = sb[d];
+            for (int e = d; e < n - 1; e++) {
+                ext[e] = ext[e + 1];
+                sa[e] = sa[e + 1];
+                sb[e] = sb[e + 1];
+            }
+            n--;
+        }
+    }
+    if (n > 3)
+        return false;
+    out->nfd = n;
+    for (int d = 0; d < 3; d++) {
+        out->fshape[d] = d < n ? static_cast<int>(ext[d]) : 1;
+        out->a[d] = d < n ? sa[d] : 0;
+        out->b[d] = d < n ? sb[d] : 0;
+    }
+    return true;
+}
+
+void add_fold_dims(MapDims &m, const TcFold &tf, const long long (&fs)[3], int (&slot)[3])
+{
+    for (int d = 0; d < 3; d++) {
+        slot[d] = -1;
+        if (d < tf.nfd && fs[d] != 0) {
+            slot[d] = m.rank;
+            m.ext[m.rank] = static_cast<uint64_t>(tf.fshape[d]);
+            m.stride[m.rank] = fs[d];
+            m.rank++;
+        }
+    }
+}
+
 void add_batch_dims(MapDims &m, const TcBatch &tb, const long long (&bs)[3], int (&slot)[3])
 {
     for (int d = 0; d < 3; d++) {
@@ -498,7 +650,7 @@ cudaError_t launch_tc2_kernel(DeviceState *ds, int kid, int slot, const CUtensor
 
 const TunedPlan *find_plan(const Problem &P)
 {
-    if (P.nbd != 0 || P.dt != DT_F32)
+    if (P.nbd != 0 || P.nfd != 0 || P.dt != DT_F32 || P.a_dt != DT_F32 || P.b_dt != DT_F32)
         return nullptr;
     for (const TunedPlan &t : t_plans)
         if (t.rows == P.M && t.inner == P.K && t.cols == P.N &&
@@ -527,6 +679,11 @@ int try_tc(const Problem &P, DeviceState *ds, cudaStream_t stream, int *kid_out)
     TcBatch tb;
     if (!merge_batches(P, &tb))
         return 0;
+    TcFold tf;
+    tf.nfd = 0;
+    if (P.nfd > 0 && (!merge_folds(P, &tf) || tb.nbd + tf.nfd > 3))
+        return 0;
+    const bool folded = P.nfd > 0;
 
     // A: K-major when K is contiguous, M-major for a transposed view.
     int a_mn;
@@ -575,8 +732,8 @@ int try_tc(const Problem &P, DeviceState *ds, cudaStream_t stream, int *kid_out)
         const long long tiles_pair = P.batches * ((P.M + 255) / 256) * ((P.N + 255) / 256);
         pair = t_path == 3 || (t_path != 1 && tiles_pair >= ds->sms / 2);
     }
-    if (wide_out)
-        bn = 128, pair = false;
+    if (wide_out || folded)
+        bn = wide_out ? 128 : bn, pair = false;
     if (pair)
         bn = 256;
     if (wide_out)
@@ -627,6 +784,8 @@ int try_tc(const Problem &P, DeviceState *ds, cudaStream_t stream, int *kid_out)
     add_batch_dims(ma, tb, tb.a, p.a_slot);
     add_batch_dims(mb, tb, tb.b, p.b_slot);
     add_batch_dims(mc, tb, tb.c, c_slot);
+    add_fold_dims(ma, tf, tf.a, p.a_fslot);
+    add_fold_dims(mb, tf, tf.b, p.b_fslot);
 
     // TF32 operands stored MN-major need the 32-byte-atom 128-byte swizzle
     CUtensorMapSwizzle sw_a = (fp32 && a_mn) ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B
@@ -653,7 +812,13 @@ int try_tc(const Problem &P, DeviceState *ds, cudaStream_t stream, int *kid_out)
     p.K = P.K;
     p.m_blocks = static_cast<int>(pair ? (P.M + 255) / 256 : m_blocks);
     p.n_blocks = (P.N + bn - 1) / bn;
-    p.k_blocks = (P.K + bk - 1) / bk;
+    p.k_per_fold = (P.K + bk - 1) / bk;
+    if (static_cast<double>(p.k_per_fold) * P.folds > 2e9)
+        return 0;
+    p.k_blocks = static_cast<int>(p.k_per_fold * P.folds);
+    p.nfd = tf.nfd;
+    for (int d = 0; d < 3; d++)
+        p.fshape[d] = tf.fshape[d];
     p.tiles = P.batches * p.m_blocks * p.n_blocks;
     p.nbd = tb.nbd;
     for (int d = 0; d < 3; d++)
@@ -743,6 +908,13 @@ SimtParams simt_params(const Problem &P)
     s.c_sn = P.c_sn;
     s.bias = P.bias;
     s.act = P.act;
+    s.nfd = P.nfd;
+    s.folds = P.folds;
+    for (int d = 0; d < P.nfd; d++) {
+        s.fshape[d] = P.fshape[d];
+        s.a_fs[d] = P.a_fs[d];
+        s.b_fs[d] = P.b_fs[d];
+    }
     return s;
 }
 
@@ -918,16 +1090,19 @@ int run(Problem &P, cudaStream_t stream)
     if (P.nbd > kMaxBatchDims) {
         return 0;
     }
-    const double work = static_cast<double>(P.M) * P.N * P.K * static_cast<double>(P.batches);
-    const bool want_tc = P.K > 0 && t_path != 2 && (t_path == 1 || t_path == 3 || work >= kTcMinWork);
+    const double work =
+        static_cast<double>(P.M) * P.N * P.K * static_cast<double>(P.batches) * P.folds;
+    const bool want_tc = P.K > 0 && P.folds > 0 && t_path != 2 &&
+                         (t_path == 1 || t_path == 3 || work >= kTcMinWork);
     const bool wide_out = P.a_dt != P.dt || P.b_dt != P.dt;   // float32 result, 16-bit operand(s)
-    const bool skinny_fit = P.N > 0 && P.N <= kSkinnyMaxN && P.M > 0 && P.batches > 0 &&
-                            P.K >= kSkinnyMinK;
+    const bool folded = P.nfd > 0 || P.folds != 1;             // summed batch axes
+    const bool skinny_fit = !folded && P.N > 0 && P.N <= kSkinnyMaxN && P.M > 0 &&
+                            P.batches > 0 && P.K >= kSkinnyMinK;
     // float32 / float64 results, mixed-type gradient products included
     const bool wide_acc = P.dt == DT_F32 || P.dt == DT_F64;
     if (skinny_fit && (t_path == 4 || (t_path == 0 && wide_acc)))
         return run_skinny(P, ds, stream);
-    if (want_tc && P.dt == DT_F64 && ds->cc_major == 10) {
+    if (want_tc && !folded && P.dt == DT_F64 && ds->cc_major == 10) {
         const cudaError_t err = launch_f64_dmma(P, ds, stream);
         if (err != cudaSuccess) {
             set_status(static_cast<int>(err));
@@ -1015,58 +1190,25 @@ int nd_entry(int dt, const void *a, const void *b, void *c, int *shape_a, size_t
 
 namespace {
 
-// One thread per kept element; the reduced coordinates are walked in
-// row-major order.
-__global__ void reduce_axes_kernel(const float *__restrict__ src, float *__restrict__ dst,
-                                   const PtgReduceDims d, long long kept_total,
-                                   long long red_total)
+// Failure-detection self-test: one warp waits, with the kernels' bounded
+// mbar_wait, on a barrier that nothing ever completes; the wait gives up
+// after its time limit and the kernel records DEV_TIMEOUT_SELFTEST.
+__global__ void wait_selftest_kernel(int *status)
 {
-    long long src_stride[10];
-    long long s = 1;
-    for (int i = d.n - 1; i >= 0; i--) {
-        src_stride[i] = s;
-        s *= d.ext[i];
+    __shared__ uint64_t bar;
+    __shared__ int abort_flag;
+    if (threadIdx.x == 0) {
+        mbar_init(&bar, 1);
+        abort_flag = 0;
+        fence_barrier_init();
     }
-    for (long long j = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x;
-         j < kept_total; j += static_cast<long long>(gridDim.x) * blockDim.x) {
-        long long rem = j, src_off = 0, dst_off = 0;
-        for (int i = d.n - 1; i >= 0; i--) {
-            if (!d.keep[i])
-                continue;
-            const long long c = rem % d.ext[i];
-            rem /= d.ext[i];
-            src_off += c * src_stride[i];
-            dst_off += c * d.dst_stride[i];
-        }
-        float acc = 0.0f;
-        for (long long r = 0; r < red_total; r++) {
-            long long rr = r, off = 0;
-            for (int i = d.n - 1; i >= 0; i--) {
-                if (d.keep[i])
-                    continue;
-                off += (rr % d.ext[i]) * src_stride[i];
-                rr /= d.ext[i];
-            }
-            acc += src[src_off + off];
-        }
-        dst[dst_off] = acc;
-    }
+    __syncwarp();
+    const bool got = __all_sync(0xffffffffu, mbar_wait(&bar, 0, &abort_flag));
+    if (!got && threadIdx.x == 0)
+        record_failure(&abort_flag, status, DEV_TIMEOUT_SELFTEST);
 }
 
 } // namespace
-
-cudaError_t ptg_reduce_axes(const float *src, float *dst, const PtgReduceDims &d,
-                            cudaStream_t stream)
-{
-    long long kept = 1, red = 1;
-    for (int i = 0; i < d.n; i++)
-        (d.keep[i] ? kept : red) *= d.ext[i];
-    if (kept == 0)
-        return cudaSuccess;
-    const long long blocks = std::min<long long>((kept + 255) / 256, 148ll * 16);
-    reduce_axes_kernel<<<static_cast<unsigned>(blocks), 256, 0, stream>>>(src, dst, d, kept, red);
-    return cudaGetLastError();
-}
 
 // Internal (hidden) hook for the other translation units of the library.
 void ptg_set_last_status(int code) { set_status(code); }
@@ -1190,6 +1332,30 @@ PT_API int cuda_f64_matmul_nd_launcher(double *a, double *b, double *c, int *sha
 {
     return nd_entry(DT_F64, a, b, c, shape_a, stride_a, nd_a, shape_b, stride_b, nd_b, shape_c,
                     stride_c, nd_c, nullptr, ACT_NONE, stream);
+}
+
+// Internal (hidden, declared in internal.h): float32 C = the sum over C's
+// reduced batch axes of A . B (see build_fold_problem), operand types as for
+// cuda_mixed_matmul_nd_launcher.
+int ptg_reduced_matmul(const void *a, int a_dtype, const void *b, int b_dtype, float *c,
+                       int *shape_a, size_t *stride_a, int nd_a, int *shape_b, size_t *stride_b,
+                       int nd_b, int *shape_c, size_t *stride_c, int nd_c, cudaStream_t stream)
+{
+    const int da = dtype_code(static_cast<dtype_t>(a_dtype));
+    const int db = dtype_code(static_cast<dtype_t>(b_dtype));
+    if (da < 0 || db < 0 || da == DT_F64 || db == DT_F64 ||
+        (da != DT_F32 && db != DT_F32 && da != db))
+        return 0;
+    Problem P;
+    const int v = build_fold_problem(DT_F32, a, b, c, shape_a, stride_a, nd_a, shape_b, stride_b,
+                                     nd_b, shape_c, stride_c, nd_c, &P);
+    if (v == 0)
+        return 0;
+    if (v == 2)
+        return 1;
+    P.a_dt = da;
+    P.b_dt = db;
+    return run(P, stream);
 }
 
 PT_API int cuda_mixed_matmul_nd_launcher(const void *a, dtype_t a_dtype, const void *b,
@@ -1370,6 +1536,15 @@ PT_API int gemm_sm100_device_status(int device, int clear)
     if (device != prev)
         cudaSetDevice(prev);
     return value;
+}
+
+PT_API int gemm_sm100_selftest_wait_timeout(cudaStream_t stream)
+{
+    DeviceState *ds = device_state();
+    if (!ds)
+        return 0;
+    wait_selftest_kernel<<<1, 32, 0, stream>>>(ds->status);
+    return cudaGetLastError() == cudaSuccess ? 1 : 0;
 }
 
 PT_API const char *gemm_sm100_algorithm_name(int algorithm_id)

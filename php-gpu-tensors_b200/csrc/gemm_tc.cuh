@@ -50,6 +50,7 @@ enum DeviceStatus : int {
     DEV_TIMEOUT_MMA = 2,
     DEV_TIMEOUT_EPILOGUE = 3,
     DEV_TIMEOUT_SPLIT = 4,
+    DEV_TIMEOUT_SELFTEST = 5,   // gemm_sm100_selftest_wait_timeout
 };
 
 struct TcParams {
@@ -67,6 +68,14 @@ struct TcParams {
     int act;
     int *status;      // device status word
     int ksplit;       // CTAs per tile splitting K (cluster size), 1 = none
+    // Batch axes summed into the product: k_blocks counts (fold, k-block)
+    // pairs, k_per_fold k-blocks per fold coordinate; a_fslot / b_fslot give
+    // the tensor-map slot (2..4) of each merged fold axis, -1 = broadcast.
+    int nfd;
+    int fshape[3];
+    int a_fslot[3];
+    int b_fslot[3];
+    int k_per_fold;
 };
 
 __device__ __forceinline__ float apply_activation(float v, int act)
@@ -418,7 +427,22 @@ __global__ void __launch_bounds__(TcConfig<IN_KIND, BN, OUT>::kThreads, 1)
                 operand_coords(c, p.a_slot, p.nbd, ca);
                 operand_coords(c, p.b_slot, p.nbd, cb);
                 const int m0 = mb * Cfg::BM, n0 = nb * BN;
-                for (int kb = kb_begin; kb < kb_end; kb++) {
+                for (int kbf = kb_begin; kbf < kb_end; kbf++) {
+                    // (fold, k-block) of this step; the fold coordinates
+                    // fill the operands' summed-axis map slots
+                    int kb = kbf;
+                    if (p.nfd > 0) {
+                        int f = kbf / p.k_per_fold;
+                        kb = kbf - f * p.k_per_fold;
+                        for (int d = p.nfd - 1; d >= 0; d--) {
+                            const int coord = f % p.fshape[d];
+                            f /= p.fshape[d];
+                            if (p.a_fslot[d] >= 2)
+                                ca[p.a_fslot[d] - 2] = coord;
+                            if (p.b_fslot[d] >= 2)
+                                cb[p.b_fslot[d] - 2] = coord;
+                        }
+                    }
                     if (!mbar_wait(&empty[stage], phase ^ 1, abort)) {
                         record_failure(abort, p.status, DEV_TIMEOUT_PRODUCER);
                         ok = false;

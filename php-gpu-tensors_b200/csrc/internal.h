@@ -27,16 +27,12 @@ cudaError_t ptg_launch_f64_peer(const double *a, size_t a_s0, size_t a_s1, const
                                 size_t b_s0, size_t b_s1, int M, int nb, int K,
                                 const ptg::F64PeerOut &po, cudaStream_t stream);
 
-// Shape of a gradient's un-broadcast reduction: src is a contiguous float32
-// tensor of extents ext[0..n); axes with keep[d] == 0 are summed (in
-// row-major order of their coordinates, so the result is deterministic) and
-// the sum lands at dst + sum over kept axes of coord * dst_stride[d].
-struct PtgReduceDims {
-    int n;
-    int ext[10];
-    int keep[10];
-    long long dst_stride[10];
-};
-
-cudaError_t ptg_reduce_axes(const float *src, float *dst, const PtgReduceDims &d,
-                            cudaStream_t stream);
+// float32 C = the sum over C's reduced batch axes of A . B: an axis where the
+// broadcast batch shape of A and B has extent > 1 and C has extent 1 (or no
+// axis) is summed inside the product kernel (the k loop runs over it), so the
+// un-broadcast step of a gradient needs no scratch tensor and no second
+// kernel.  Operand dtypes are dtype_t values: float32, float16, bfloat16 (not
+// float16 with bfloat16).  Returns 1 / 0 like the launchers.
+int ptg_reduced_matmul(const void *a, int a_dtype, const void *b, int b_dtype, float *c,
+                       int *shape_a, size_t *stride_a, int nd_a, int *shape_b, size_t *stride_b,
+                       int nd_b, int *shape_c, size_t *stride_c, int nd_c, cudaStream_t stream);

@@ -261,8 +261,8 @@ bool folds_into(const pt_tensor *t, const int *full, int nb, int inner, long lon
 //   * every batch axis summed and both operands' batch axes chaining onto the
 //     product's inner axis (contiguous tensors): one GEMM whose inner axis is
 //     (batch..., K);
-//   * otherwise: the batched product into a float32 scratch tensor, then a
-//     fixed-order reduction kernel.
+//   * otherwise: the product kernel itself walks the summed axes in its k
+//     loop (ptg_reduced_matmul), writing the reduced gradient directly.
 int gradient_product(const pt_tensor *x, const pt_tensor *y, const pt_tensor *out,
                      cudaStream_t stream)
 {
@@ -274,7 +274,6 @@ int gradient_product(const pt_tensor *x, const pt_tensor *y, const pt_tensor *ou
         return fail(PT_INVALID_ARGUMENT, "matmul gradients are float32 tensors");
     const int nb = nf - 2;
     bool same = out->ndims == nf, all_reduced = true;
-    int keep[MAX_DIMS];
     for (int d = 0; d < nb; d++) {
         const int io = d - (nf - out->ndims);
         const int eo = io >= 0 ? out->shape[io] : 1;
@@ -282,8 +281,7 @@ int gradient_product(const pt_tensor *x, const pt_tensor *y, const pt_tensor *ou
             return fail(PT_INVALID_ARGUMENT,
                         "Gradient shape cannot be reduced to its operand shape at axis %d", io);
         same = same && eo == full[d];
-        keep[d] = eo == full[d] ? 1 : 0;
-        all_reduced = all_reduced && (full[d] == 1 || !keep[d]);
+        all_reduced = all_reduced && (full[d] == 1 || eo != full[d]);
     }
     if (same)
         return launch_product(x, y, out, stream);
@@ -308,41 +306,13 @@ int gradient_product(const pt_tensor *x, const pt_tensor *y, const pt_tensor *ou
         return launch_product(&x2, &y2, &o2, stream);
     }
 
-    // scratch product of the full broadcast shape, then the reduction
-    pt_tensor t;
-    std::memset(&t, 0, sizeof(t));
-    t.dtype = DTYPE_FLOAT32;
-    t.ndims = nf;
-    std::memcpy(t.shape, full, sizeof(int) * static_cast<size_t>(nf));
-    contiguous_strides(full, nf, t.strides);
-    size_t total = 1;
-    for (int d = 0; d < nf; d++)
-        total *= static_cast<size_t>(full[d]);
-    if (total == 0)
-        return ok();
-    cudaError_t err = cudaMallocAsync(&t.data, total * sizeof(float), stream);
-    if (err != cudaSuccess)
-        return fail(PT_RUNTIME, "Failed to allocate the gradient scratch (CUDA error %d)",
-                    static_cast<int>(err));
-    int st = launch_product(x, y, &t, stream);
-    if (st == PT_OK) {
-        PtgReduceDims rd;
-        std::memset(&rd, 0, sizeof(rd));
-        rd.n = nf;
-        for (int d = 0; d < nf; d++) {
-            rd.ext[d] = full[d];
-            rd.keep[d] = d < nb ? keep[d] : 1;
-            const int io = d - (nf - out->ndims);
-            rd.dst_stride[d] = rd.keep[d] && io >= 0 ? static_cast<long long>(out->strides[io]) : 0;
-        }
-        err = ptg_reduce_axes(static_cast<const float *>(t.data), static_cast<float *>(out->data),
-                              rd, stream);
-        if (err != cudaSuccess)
-            st = fail(PT_RUNTIME, "Gradient reduction failed (CUDA error %d)",
-                      static_cast<int>(err));
-    }
-    cudaFreeAsync(t.data, stream);
-    return st;
+    // every other reduction: the summed axes run inside the product kernel
+    pt_tensor cx = *x, cy = *y, co = *out;
+    const int st = ptg_reduced_matmul(x->data, x->dtype, y->data, y->dtype,
+                                      static_cast<float *>(out->data), cx.shape, cx.strides,
+                                      x->ndims, cy.shape, cy.strides, y->ndims, co.shape,
+                                      co.strides, out->ndims, stream);
+    return st ? ok() : submission_failed();
 }
 
 } // namespace

@@ -107,6 +107,7 @@ _SIGNATURES = {
         [ctypes.POINTER(ctypes.c_int), ctypes.POINTER(ctypes.c_size_t), ctypes.c_int] * 3 +
         [ctypes.c_void_p]),
     "gemm_sm100_last_kernel": (ctypes.c_char_p, []),
+    "gemm_sm100_selftest_wait_timeout": (ctypes.c_int, [ctypes.c_void_p]),
     "gemm_sm100_set_path": (ctypes.c_int, [ctypes.c_int]),
     "gemm_sm100_last_launch": (None, [ctypes.POINTER(ctypes.c_int)] * 3),
     "gemm_sm100_device_status": (ctypes.c_int, [ctypes.c_int, ctypes.c_int]),
