@@ -46,7 +46,7 @@ enum DType : int { DT_F32 = 0, DT_F16 = 1, DT_BF16 = 2, DT_F64 = 3 };
 constexpr int kMaxBatchDims = kSimtMaxBatchDims;
 constexpr double kTcMinWork = 4194304.0;   // M*N*K*batches below this: CUDA-core kernel
 constexpr int kSkinnyMinK = 128;           // shortest K for the few-column kernel
-constexpr int kStrictMinK = 16;            // shortest K for 3xTF32 (strict float32)
+constexpr int kStrictMinK = 64;            // shortest K for 3xTF32 (strict float32)
 constexpr int kSplitMinKBlocks = 8;        // k-blocks per split-K rank, at least
 constexpr double kTuneMinWork = 10000000.0; // matmul_kernels.cu:24 (MATMUL_LT_MIN_WORK)
 
@@ -707,9 +707,10 @@ int try_tc(const Problem &P, DeviceState *ds, cudaStream_t stream, int *kid_out)
     // kernel selection
     int kid;
     const bool fp32 = P.dt == DT_F32 && !wide_out;
-    // 3xTF32 drops lo*lo and rounds lo to TF32: up to about 12 float32 ulps
-    // per product, inside the K-ulp float32 dot-product bound only from K = 12
-    // on.  Shorter inner axes run the exact-fma CUDA-core kernel.
+    // 3xTF32 (hi = the tensor core's truncation, lo rounded to TF32, lo*lo
+    // dropped) errs by up to about 32 float32 ulps per product, inside the
+    // K-ulp float32 dot-product bound with room to spare only for longer inner
+    // axes; shorter ones run the exact-fma CUDA-core kernel.
     if (fp32 && t_precision == CUDA_MATMUL_PRECISION_FP32_STRICT && P.K < kStrictMinK)
         return 0;
     const long long m_blocks = (P.M + 127) / 128;

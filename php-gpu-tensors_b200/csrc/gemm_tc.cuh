@@ -12,9 +12,10 @@
 //                activation, convert, stage 32x(128 B) boxes in swizzled shared
 //                memory and write them with TMA stores.  Double-buffered TMEM
 //                lets the epilogue of tile i overlap the mainloop of tile i+1.
-//   warps 6..13  (split kinds only) F32X3: split each FP32 tile into TF32
-//                hi/lo parts so the MMA warp can issue hi*hi + hi*lo + lo*hi
-//                (3xTF32).  MIX_A / MIX_B (one operand float32, the other
+//   warps 6..13  (split kinds only) F32X3: write lo = tf32(x - trunc(x)) of
+//                each FP32 tile (the tensor core reads the tile itself as
+//                hi = trunc(x)) so the MMA warp can issue hi*hi + hi*lo +
+//                lo*hi (3xTF32).  MIX_A / MIX_B (one operand float32, the other
 //                bfloat16): split the float32 tile into three bfloat16 parts
 //                hi + mid + lo (24+ significant bits) so the MMA warp can
 //                issue three exact bf16 x bf16 products per k16.
@@ -210,6 +211,14 @@ __device__ __forceinline__ float round_tf32(float x)
     uint32_t r;
     asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
     return __uint_as_float(r);
+}
+
+// The TF32 value tcgen05.mma kind::tf32 takes from a float32 operand: the
+// low 13 mantissa bits dropped (measured on B200: 1 + 2^-11 + 2^-12 and the
+// exact half-ulp case both enter the product as 1).
+__device__ __forceinline__ float trunc_tf32(float x)
+{
+    return __uint_as_float(__float_as_uint(x) & 0xffffe000u);
 }
 
 template <int IN_KIND, int BN_, int OUT>
@@ -876,22 +885,21 @@ __global__ void __launch_bounds__(TcConfig<IN_KIND, BN, OUT>::kThreads, 1)
                         ok = false;
                         break;
                     }
-                    float4 *raw = reinterpret_cast<float4 *>(smem + stage * Cfg::kStageBytes);
+                    // hi is the landed tile itself (the tensor core truncates
+                    // it to TF32); only lo = tf32(x - trunc(x)) is written
+                    const float4 *raw =
+                        reinterpret_cast<const float4 *>(smem + stage * Cfg::kStageBytes);
                     float4 *lo = reinterpret_cast<float4 *>(smem + stage * Cfg::kStageBytes +
                                                             Cfg::kLoadBytes);
                     constexpr int kVecs = Cfg::kLoadBytes / 16;
 #pragma unroll 4
                     for (int i = st; i < kVecs; i += Cfg::kSplitWarps * 32) {
-                        float4 x = raw[i], h, l;
-                        h.x = round_tf32(x.x);
-                        h.y = round_tf32(x.y);
-                        h.z = round_tf32(x.z);
-                        h.w = round_tf32(x.w);
-                        l.x = isfinite(h.x) ? round_tf32(x.x - h.x) : 0.0f;
-                        l.y = isfinite(h.y) ? round_tf32(x.y - h.y) : 0.0f;
-                        l.z = isfinite(h.z) ? round_tf32(x.z - h.z) : 0.0f;
-                        l.w = isfinite(h.w) ? round_tf32(x.w - h.w) : 0.0f;
-                        raw[i] = h;
+                        const float4 x = raw[i];
+                        float4 l;
+                        l.x = isfinite(x.x) ? round_tf32(x.x - trunc_tf32(x.x)) : 0.0f;
+                        l.y = isfinite(x.y) ? round_tf32(x.y - trunc_tf32(x.y)) : 0.0f;
+                        l.z = isfinite(x.z) ? round_tf32(x.z - trunc_tf32(x.z)) : 0.0f;
+                        l.w = isfinite(x.w) ? round_tf32(x.w - trunc_tf32(x.w)) : 0.0f;
                         lo[i] = l;
                     }
                     fence_proxy_async_smem();
