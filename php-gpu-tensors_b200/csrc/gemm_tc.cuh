@@ -251,9 +251,15 @@ struct TcConfig {
     static constexpr int kMixOtherOffset = kMixRawBytes + 128 * BK * 2;
     static constexpr int kLoadBytes =
         kMix ? kMixRawBytes + 128 * BK * 2 : kATile + kBTile;   // bytes TMA lands per stage
+    // F32X3: lo = tf32(x - trunc(x)) lives in its own 2-slot ring, needed only
+    // from the split to the MMA, so the TMA ring of raw tiles gets 4 stages.
+    static constexpr bool kLoRing = IN_KIND == IN_F32X3;
+    static constexpr int kLoStages = kLoRing ? 2 : 0;
     static constexpr int kStageBytes =
-        kMix ? kMixOtherOffset + 128 * BK * 2 : kLoadBytes * (kSplit3 ? 2 : 1);
-    static constexpr int kStages = (196608 / kStageBytes) > 8 ? 8 : (196608 / kStageBytes);
+        kMix ? kMixOtherOffset + 128 * BK * 2 : kLoadBytes * ((kSplit3 && !kLoRing) ? 2 : 1);
+    static constexpr int kRawBudget = 196608 - kLoStages * kLoadBytes;
+    static constexpr int kStages = (kRawBudget / kStageBytes) > 8 ? 8 : (kRawBudget / kStageBytes);
+    static constexpr int kLoOffset = kStages * kStageBytes;
     static constexpr int kOutBytes = OutTraits<OUT>::kBytes;
     static constexpr int kEpiCols = 128 / kOutBytes;      // columns per staged box
     static constexpr int kEpiChunks = BN / kEpiCols;
@@ -272,11 +278,11 @@ struct TcConfig {
     static constexpr int kTotalCol = 2 * kAccCols;
     static constexpr int kTmemUsed = (kSplit3 ? 3 : 2) * kAccCols;
     static constexpr int kTmemCols = kTmemUsed <= 256 ? 256 : 512;   // power of two
-    static constexpr int kRingBytes = kStages * kStageBytes;
+    static constexpr int kRingBytes = kStages * kStageBytes + kLoStages * kLoadBytes;
     static constexpr int kEpiOffset = kRingBytes;
     static constexpr int kBarOffset = kEpiOffset + kEpiWarps * 2 * kEpiBufBytes;
     // full, empty, ready per stage; tmem full/empty x2; drain
-    static constexpr int kNumBars = 3 * kStages + 4 + 1;
+    static constexpr int kNumBars = 3 * kStages + 4 + 1 + kLoStages;
     static constexpr int kSmemBytes = kBarOffset + kNumBars * 8 + 16 + 1024;
     // split-K partial tile [BM][BN + 4] floats at the start of the ring (the
     // 4-float pad keeps 16-byte row accesses of 8 lanes on distinct banks)
@@ -372,6 +378,7 @@ __global__ void __launch_bounds__(TcConfig<IN_KIND, BN, OUT>::kThreads, 1)
     uint64_t *tfull = bars + 3 * S;
     uint64_t *tempty = bars + 3 * S + 2;
     uint64_t *drain = bars + 3 * S + 4;
+    uint64_t *lo_free = bars + 3 * S + 5;   // F32X3 lo ring: slot read by the MMAs
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + Cfg::kNumBars);
     volatile int *abort = reinterpret_cast<volatile int *>(tmem_slot + 1);
 
@@ -392,6 +399,8 @@ __global__ void __launch_bounds__(TcConfig<IN_KIND, BN, OUT>::kThreads, 1)
             mbar_init(&tempty[i], Cfg::kEpiWarps);
         }
         mbar_init(drain, 1);
+        for (int i = 0; i < Cfg::kLoStages; i++)
+            mbar_init(&lo_free[i], 1);
         *abort = 0;
         fence_barrier_init();
     }
@@ -521,6 +530,7 @@ __global__ void __launch_bounds__(TcConfig<IN_KIND, BN, OUT>::kThreads, 1)
             uint32_t phase = 0;
             long long iter = 0;   // accumulator slot uses
             int acc = 0;
+            int lo_slot = 0;      // F32X3 lo ring slot of the current k-block
             uint32_t d_tmem = 0;
             bool ok = true;
             const uint32_t smem_base = smem_addr(smem);
@@ -571,10 +581,12 @@ __global__ void __launch_bounds__(TcConfig<IN_KIND, BN, OUT>::kThreads, 1)
                         if constexpr (Cfg::kTf32) {
                             umma_tf32(d_tmem, ad, bd, p.idesc, accumulate);
                             if constexpr (Cfg::kSplit3) {
-                                const uint64_t ad_lo =
-                                    smem_desc(sa + Cfg::kLoadBytes + a_off, a_lbo, a_sbo, a_lay);
-                                const uint64_t bd_lo =
-                                    smem_desc(sb + Cfg::kLoadBytes + b_off, b_lbo, b_sbo, b_lay);
+                                // lo tiles: slot lo_slot of the lo ring, A then B
+                                const uint32_t la = smem_base + Cfg::kLoOffset +
+                                                    static_cast<uint32_t>(lo_slot * Cfg::kLoadBytes);
+                                const uint32_t lb = la + Cfg::kATile;
+                                const uint64_t ad_lo = smem_desc(la + a_off, a_lbo, a_sbo, a_lay);
+                                const uint64_t bd_lo = smem_desc(lb + b_off, b_lbo, b_sbo, b_lay);
                                 umma_tf32(d_tmem, ad, bd_lo, p.idesc, 1);
                                 umma_tf32(d_tmem, ad_lo, bd, p.idesc, 1);
                             }
@@ -598,6 +610,11 @@ __global__ void __launch_bounds__(TcConfig<IN_KIND, BN, OUT>::kThreads, 1)
                         }
                     }
                     umma_commit(&empty[stage]);
+                    if constexpr (Cfg::kLoRing) {
+                        umma_commit(&lo_free[lo_slot]);
+                        if (++lo_slot == Cfg::kLoStages)
+                            lo_slot = 0;
+                    }
                     if (++stage == S) {
                         stage = 0;
                         phase ^= 1;
@@ -874,23 +891,25 @@ __global__ void __launch_bounds__(TcConfig<IN_KIND, BN, OUT>::kThreads, 1)
                 }
             }
         } else if constexpr (Cfg::kSplit3) {
-            const int st = threadIdx.x - 32 * (2 + Cfg::kEpiWarps);   // 0..127
-            int stage = 0;
-            uint32_t phase = 0;
+            const int st = threadIdx.x - 32 * (2 + Cfg::kEpiWarps);   // 0..255
+            int stage = 0, lo_slot = 0;
+            uint32_t phase = 0, lo_phase = 0;
             bool ok = true;
             for (long long t = t_first; ok && t < p.tiles; t += t_step) {
                 for (int kb = kb_begin; kb < kb_end; kb++) {
-                    if (!mbar_wait(&full[stage], phase, abort)) {
+                    if (!mbar_wait(&full[stage], phase, abort) ||
+                        !mbar_wait(&lo_free[lo_slot], lo_phase ^ 1, abort)) {
                         record_failure(abort, p.status, DEV_TIMEOUT_SPLIT);
                         ok = false;
                         break;
                     }
                     // hi is the landed tile itself (the tensor core truncates
-                    // it to TF32); only lo = tf32(x - trunc(x)) is written
+                    // it to TF32); only lo = tf32(x - trunc(x)) is written, into
+                    // the lo ring's slot
                     const float4 *raw =
                         reinterpret_cast<const float4 *>(smem + stage * Cfg::kStageBytes);
-                    float4 *lo = reinterpret_cast<float4 *>(smem + stage * Cfg::kStageBytes +
-                                                            Cfg::kLoadBytes);
+                    float4 *lo = reinterpret_cast<float4 *>(smem + Cfg::kLoOffset +
+                                                            lo_slot * Cfg::kLoadBytes);
                     constexpr int kVecs = Cfg::kLoadBytes / 16;
 #pragma unroll 4
                     for (int i = st; i < kVecs; i += Cfg::kSplitWarps * 32) {
@@ -907,6 +926,10 @@ __global__ void __launch_bounds__(TcConfig<IN_KIND, BN, OUT>::kThreads, 1)
                     if (++stage == S) {
                         stage = 0;
                         phase ^= 1;
+                    }
+                    if (++lo_slot == Cfg::kLoStages) {
+                        lo_slot = 0;
+                        lo_phase ^= 1;
                     }
                 }
             }
