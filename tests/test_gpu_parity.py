@@ -793,3 +793,74 @@ def test_bounded_wait_reports_timeout_and_context_survives():
     c = np.frombuffer(a.matmul(a).toBuffer(), np.float32)
     assert c[0] == 256.0 and c[-1] == 256.0
     assert P.device_status() == 0
+
+
+# ------------------------------------------------------------------ randomized sweep
+def _random_case(rng):
+    """Random operand shapes with NumPy broadcasting, transposes and padding."""
+    M, N, K = (int(rng.integers(1, 300)) for _ in range(3))
+    nb = int(rng.integers(0, 3))
+    batch = [int(rng.integers(1, 4)) for _ in range(nb)]
+    a_batch = [d if rng.random() < 0.7 else 1 for d in batch]
+    b_batch = [d if rng.random() < 0.7 else 1 for d in batch]
+    if rng.random() < 0.3 and nb:
+        b_batch = b_batch[int(rng.integers(0, nb + 1)):]   # B with fewer batch axes
+    return (a_batch + [M, K], b_batch + [K, N], bool(rng.random() < 0.4),
+            bool(rng.random() < 0.4), int(rng.choice([0, 0, 3, 8])))
+
+
+@pytest.mark.parametrize("dtype", ["bfloat16", "float16", "float32"])
+@pytest.mark.parametrize("path", ["auto", "tensor-core", "skinny"])
+def test_randomized_products(dtype, path):
+    """40 seeded random products per dtype and kernel path against the oracle."""
+    rng = np.random.default_rng(sum(map(ord, dtype + path)))
+    P.set_kernel_path(path)
+    for i in range(40):
+        ashape, bshape, at, bt, pad = _random_case(rng)
+        a = padded(O.seeded(ashape, 1000 + i, "normal"), ashape, pad, dtype, at)
+        b = padded(O.seeded(bshape, 2000 + i, "normal"), bshape, pad, dtype, bt)
+        c = to_device(a, dtype).matmul(to_device(b, dtype))
+        what = (dtype, path, i, ashape, bshape, at, bt, pad, P.cuda_get_backend_info()["kernel"])
+        if dtype == "float32":
+            check_fp32(c.to_numpy(), a, b, what)
+        else:
+            ref = O.host_matmul(a, b, dtype, threads=O.oracle().orc_host_threads())
+            check_close(c.to_numpy(), ref, dtype, what)
+    assert P.device_status() == 0
+
+
+def test_randomized_gradients():
+    """Seeded random backward nodes (float32 / bfloat16 operands, float32 or
+    same-typed upstream, broadcast operands whose gradients are reduced)
+    against exact float64 sums."""
+    rng = np.random.default_rng(77)
+    for i in range(30):
+        dt = "bfloat16" if rng.random() < 0.5 else "float32"
+        gdt = dt if rng.random() < 0.3 else "float32"
+        ashape, bshape, _, _, _ = _random_case(rng)
+        a = O.dense(O.to_storage(O.seeded(ashape, 3000 + i, "normal"), dt), ashape)
+        b = O.dense(O.to_storage(O.seeded(bshape, 4000 + i, "normal"), dt), bshape)
+        nb = max(len(ashape), len(bshape)) - 2
+        full = [max(x, y) for x, y in zip([1] * (nb - len(ashape) + 2) + ashape[:-2],
+                                          [1] * (nb - len(bshape) + 2) + bshape[:-2])]
+        M, K, N = ashape[-2], ashape[-1], bshape[-1]
+        gshape = full + [M, N]
+        gc = O.dense(O.to_storage(O.seeded(gshape, 5000 + i, "normal"), gdt), gshape)
+        ga, gb = P.CudaArray.zeros(ashape), P.CudaArray.zeros(bshape)
+        _backward(to_device(a, dt), to_device(b, dt), to_device(gc, gdt), ga, gb)
+        A = torch.from_numpy(O.to_float32(a[0], dt).astype(np.float64)).reshape(ashape)
+        B = torch.from_numpy(O.to_float32(b[0], dt).astype(np.float64)).reshape(bshape)
+        G = torch.from_numpy(O.to_float32(gc[0], gdt).astype(np.float64)).reshape(gshape)
+        for got, prod, absp, target, inner in (
+                (ga, G @ B.transpose(-1, -2), G.abs() @ B.abs().transpose(-1, -2), ashape, N),
+                (gb, A.transpose(-1, -2) @ G, A.abs().transpose(-1, -2) @ G.abs(), bshape, M)):
+            lead = len(gshape) - len(target)
+            dims = tuple(range(lead)) + tuple(lead + j for j, e in enumerate(target[:-2])
+                                              if e == 1 and gshape[lead + j] != 1)
+            ref = (prod.sum(dim=dims) if dims else prod).reshape(target)
+            refabs = (absp.sum(dim=dims) if dims else absp).reshape(target)
+            folds = int(np.prod(gshape[:-2])) // max(1, int(np.prod(target[:-2])))
+            g = got.to_torch().double().cpu()
+            what = (i, dt, gdt, ashape, bshape, P.cuda_get_backend_info()["kernel"])
+            assert torch.all((g - ref).abs() <= folds * inner * 2.0 ** -24 * refabs + 1e-30), what
+    assert P.device_status() == 0
