@@ -48,6 +48,18 @@ constexpr double kTcMinWork = 4194304.0;   // M*N*K*batches below this: CUDA-cor
 constexpr int kSkinnyMinK = 128;           // shortest K for the few-column kernel
 constexpr int kStrictMinK = 64;            // shortest K for 3xTF32 (strict float32)
 constexpr int kSplitMinKBlocks = 8;        // k-blocks per split-K rank, at least
+#ifndef PTG_PAIR_CHUNK_KB
+#define PTG_PAIR_CHUNK_KB 4
+#endif
+// 2-CTA 3xTF32: k-blocks (32 K each) per accumulator chunk, 128 K as in the
+// single-CTA kernel
+constexpr int kPairChunkKB = PTG_PAIR_CHUNK_KB;
+// Time of one 256 x 256 tile of the 2-CTA 3xTF32 kernel in 128 x 128 tiles of
+// the single-CTA one (B200, 4096 x 1024 x 1024: 64.0 us for one round of 64
+// cluster tiles against 71.6 us for two waves of 256 tiles).  With it the
+// choice matches the faster kernel on every measured shape (8192^3 pair,
+// 4096^3 single-CTA, the config-4 layer products pair, their dW single-CTA).
+constexpr double kPairTileCost = 1.79;
 constexpr double kTuneMinWork = 10000000.0; // matmul_kernels.cu:24 (MATMUL_LT_MIN_WORK)
 
 struct Problem {
@@ -512,6 +524,7 @@ enum KernelId : int {
     KID_F16_PAIR,
     KID_F64_DMMA,
     KID_F64_DMMA_PEER,
+    KID_F32X3_PAIR,          // strict float32 on the 2-CTA 3xTF32 kernel
     KID_SKINNY_ASYNC = 16,   // 24 ids: (float64 ? 12 : 0) + 2 * index of NB in {4,8,12,16,24,32} + A k-major
     KID_MIX_A = 40,          // float32 A (split into 3 bf16) x bf16 B -> float32
     KID_MIX_B,               // bf16 A x float32 B -> float32
@@ -532,6 +545,7 @@ const char *kernel_name(int kid)
     case KID_BF16_PAIR: return "tc2-bf16-256x256";
     case KID_F16_PAIR: return "tc2-f16-256x256";
     case KID_F64_DMMA: return "dmma-f64-128x128";
+    case KID_F32X3_PAIR: return "tc2-3xtf32-256x256";
     case KID_MIX_A: return "tc-f32xbf16-bf16x3-128x128";
     case KID_MIX_B: return "tc-bf16xf32-bf16x3-128x128";
     case KID_BF16_F32: return "tc-bf16-f32out-128x128";
@@ -602,13 +616,11 @@ cudaError_t launch_tc_kernel(DeviceState *ds, int kid, const CUtensorMap &ma,
 
 // Cluster launch of the 2-CTA kernel: at most as many clusters as can be
 // co-resident (one CTA per SM), two CTAs each.
-template <int IN, int OUT>
-cudaError_t launch_tc2_kernel(DeviceState *ds, int kid, int slot, const CUtensorMap &ma,
-                              const CUtensorMap &mb, const CUtensorMap &mc, TcParams &p,
-                              cudaStream_t stream)
+template <typename Cfg, typename Kernel>
+cudaError_t launch_pair_kernel(DeviceState *ds, int kid, int slot, Kernel kernel,
+                               const CUtensorMap &ma, const CUtensorMap &mb,
+                               const CUtensorMap &mc, TcParams &p, cudaStream_t stream)
 {
-    using Cfg = Tc2Config<IN, OUT>;
-    auto kernel = tc2_gemm_kernel<IN, OUT>;
     if (!ensure_smem_attr(ds, kid, kernel, Cfg::kSmemBytes))
         return cudaErrorInvalidConfiguration;
     cudaLaunchAttribute attr[2];
@@ -646,6 +658,15 @@ cudaError_t launch_tc2_kernel(DeviceState *ds, int kid, int slot, const CUtensor
     if (err != cudaSuccess)
         return err;
     return cudaGetLastError();
+}
+
+template <int IN, int OUT>
+cudaError_t launch_tc2_kernel(DeviceState *ds, int kid, int slot, const CUtensorMap &ma,
+                              const CUtensorMap &mb, const CUtensorMap &mc, TcParams &p,
+                              cudaStream_t stream)
+{
+    return launch_pair_kernel<Tc2Config<IN, OUT>>(ds, kid, slot, tc2_gemm_kernel<IN, OUT>, ma, mb,
+                                                  mc, p, stream);
 }
 
 const TunedPlan *find_plan(const Problem &P)
@@ -729,20 +750,44 @@ int try_tc(const Problem &P, DeviceState *ds, cudaStream_t stream, int *kid_out)
     // 16-bit products with enough 256x256 tiles to fill the co-resident
     // clusters run on the 2-CTA kernel (or whenever path 3 asks for it).
     bool pair = false;
-    if (!fp32 && P.forced_bn == 0) {
-        const long long tiles_pair = P.batches * ((P.M + 255) / 256) * ((P.N + 255) / 256);
+    const bool strict = fp32 && t_precision == CUDA_MATMUL_PRECISION_FP32_STRICT;
+    const long long tiles_pair = P.batches * ((P.M + 255) / 256) * ((P.N + 255) / 256);
+    if (!fp32 && P.forced_bn == 0)
         pair = t_path == 3 || (t_path != 1 && tiles_pair >= ds->sms / 2);
-    }
     if (wide_out || folded)
         bn = wide_out ? 128 : bn, pair = false;
+    // Strict float32: the 2-CTA 3xTF32 kernel runs a 256 x 256 tile in
+    // kPairTileCost single-CTA 128 x 128 tile times (measured on B200), so it
+    // is chosen when its rounds of co-resident clusters take less time than
+    // the single-CTA kernel's waves (or its split-K launch).
+    if (strict && P.forced_bn == 0) {
+        if (t_path == 3) {
+            pair = true;
+        } else if (t_path == 0) {
+            const long long tiles1 = P.batches * m_blocks * ((P.N + 127) / 128);
+            const long long kb1 = static_cast<long long>((P.K + 31) / 32) * P.folds;
+            double t1 = std::ceil(static_cast<double>(tiles1) / ds->sms);
+            if (tiles1 < ds->sms / 2) {
+                for (int g : {4, 2}) {
+                    if (tiles1 * g <= ds->sms && kb1 >= kSplitMinKBlocks * g) {
+                        t1 = 1.0 / g;
+                        break;
+                    }
+                }
+            }
+            const double t2 =
+                std::ceil(static_cast<double>(tiles_pair) / (ds->sms / 2)) * kPairTileCost;
+            pair = t2 < t1;
+        }
+    }
     if (pair)
         bn = 256;
     if (wide_out)
         kid = mix_side == 0 ? KID_MIX_A
                             : mix_side == 1 ? KID_MIX_B : (op_dt == DT_BF16 ? KID_BF16_F32 : KID_F16_F32);
     else if (fp32)
-        kid = t_precision == CUDA_MATMUL_PRECISION_FP32_STRICT ? KID_F32X3_128
-                                                                : (bn == 256 ? KID_TF32_256 : KID_TF32_128);
+        kid = strict ? (pair ? KID_F32X3_PAIR : KID_F32X3_128)
+                     : (bn == 256 ? KID_TF32_256 : KID_TF32_128);
     else if (P.dt == DT_BF16)
         kid = pair ? KID_BF16_PAIR : (bn == 256 ? KID_BF16_256 : KID_BF16_128);
     else
@@ -841,6 +886,10 @@ int try_tc(const Problem &P, DeviceState *ds, cudaStream_t stream, int *kid_out)
     case KID_TF32_256: err = launch_tc_kernel<IN_TF32, 256, OUT_F32>(ds, kid, tma_a, tma_b, tma_c, p, stream); break;
     case KID_BF16_PAIR: err = launch_tc2_kernel<IN_BF16, OUT_BF16>(ds, kid, 0, tma_a, tma_b, tma_c, p, stream); break;
     case KID_F16_PAIR: err = launch_tc2_kernel<IN_F16, OUT_F16>(ds, kid, 1, tma_a, tma_b, tma_c, p, stream); break;
+    case KID_F32X3_PAIR:
+        err = launch_pair_kernel<Tc2x3Config<kPairChunkKB>>(ds, kid, 2, tc2x3_gemm_kernel<kPairChunkKB>,
+                                                            tma_a, tma_b, tma_c, p, stream);
+        break;
     case KID_MIX_A: err = launch_tc_kernel<IN_MIX_A, 128, OUT_F32>(ds, kid, tma_a, tma_b, tma_c, p, stream); break;
     case KID_MIX_B: err = launch_tc_kernel<IN_MIX_B, 128, OUT_F32>(ds, kid, tma_a, tma_b, tma_c, p, stream); break;
     case KID_BF16_F32: err = launch_tc_kernel<IN_BF16, 128, OUT_F32>(ds, kid, tma_a, tma_b, tma_c, p, stream); break;

@@ -895,32 +895,40 @@ __global__ void __launch_bounds__(TcConfig<IN_KIND, BN, OUT>::kThreads, 1)
             int stage = 0, lo_slot = 0;
             uint32_t phase = 0, lo_phase = 0;
             bool ok = true;
+            constexpr int kVecs = Cfg::kLoadBytes / 16;
+            constexpr int kPer = kVecs / (Cfg::kSplitWarps * 32);
+            static_assert(kVecs % (Cfg::kSplitWarps * 32) == 0, "split covers the tile evenly");
+            auto lo_of = [](float x) { return isfinite(x) ? round_tf32(x - trunc_tf32(x)) : 0.0f; };
             for (long long t = t_first; ok && t < p.tiles; t += t_step) {
                 for (int kb = kb_begin; kb < kb_end; kb++) {
-                    if (!mbar_wait(&full[stage], phase, abort) ||
-                        !mbar_wait(&lo_free[lo_slot], lo_phase ^ 1, abort)) {
+                    // hi is the landed tile itself (the tensor core truncates
+                    // it to TF32); only lo = tf32(x - trunc(x)) is written, into
+                    // the lo ring's slot.  lo is computed into registers as soon
+                    // as the tile lands and stored once the slot is free, which
+                    // keeps the loads and arithmetic off the slot-release chain.
+                    if (!mbar_wait(&full[stage], phase, abort)) {
                         record_failure(abort, p.status, DEV_TIMEOUT_SPLIT);
                         ok = false;
                         break;
                     }
-                    // hi is the landed tile itself (the tensor core truncates
-                    // it to TF32); only lo = tf32(x - trunc(x)) is written, into
-                    // the lo ring's slot
                     const float4 *raw =
                         reinterpret_cast<const float4 *>(smem + stage * Cfg::kStageBytes);
+                    float4 l[kPer];
+#pragma unroll
+                    for (int j = 0; j < kPer; j++) {
+                        const float4 x = raw[st + j * Cfg::kSplitWarps * 32];
+                        l[j] = make_float4(lo_of(x.x), lo_of(x.y), lo_of(x.z), lo_of(x.w));
+                    }
+                    if (!mbar_wait(&lo_free[lo_slot], lo_phase ^ 1, abort)) {
+                        record_failure(abort, p.status, DEV_TIMEOUT_SPLIT);
+                        ok = false;
+                        break;
+                    }
                     float4 *lo = reinterpret_cast<float4 *>(smem + Cfg::kLoOffset +
                                                             lo_slot * Cfg::kLoadBytes);
-                    constexpr int kVecs = Cfg::kLoadBytes / 16;
-#pragma unroll 4
-                    for (int i = st; i < kVecs; i += Cfg::kSplitWarps * 32) {
-                        const float4 x = raw[i];
-                        float4 l;
-                        l.x = isfinite(x.x) ? round_tf32(x.x - trunc_tf32(x.x)) : 0.0f;
-                        l.y = isfinite(x.y) ? round_tf32(x.y - trunc_tf32(x.y)) : 0.0f;
-                        l.z = isfinite(x.z) ? round_tf32(x.z - trunc_tf32(x.z)) : 0.0f;
-                        l.w = isfinite(x.w) ? round_tf32(x.w - trunc_tf32(x.w)) : 0.0f;
-                        lo[i] = l;
-                    }
+#pragma unroll
+                    for (int j = 0; j < kPer; j++)
+                        lo[st + j * Cfg::kSplitWarps * 32] = l[j];
                     fence_proxy_async_smem();
                     mbar_arrive(&ready[stage]);
                     if (++stage == S) {

@@ -329,4 +329,464 @@ __global__ void __launch_bounds__(Tc2Config<IN_KIND, OUT>::kThreads, 1)
     }
 }
 
+// ---------------------------------------------------------------------------
+// 2-CTA strict float32 (3xTF32) GEMM.
+//
+// A CTA pair computes a 256 x 256 tile with M = 256, N = 256
+// tcgen05.mma.cta_group::2 instructions: CTA r holds rows [128 r, 128 r + 128)
+// of the A tile and columns [128 r, 128 r + 128) of the B tile and computes a
+// 128 x 256 output block, so per FLOP each SM streams and splits half the
+// bytes of the single-CTA 128 x 128 kernel.
+//
+// Per CTA: a 4-stage ring of raw float32 tiles (A 16 KB + B 16 KB), a 2-slot
+// lo ring, 6 split warps writing lo = tf32(x - trunc(x)) of the CTA's own
+// tiles and 8 epilogue warps (16 warps: 128 registers per thread).  The lo of k-block kb can be stored only when
+// the MMAs of k-block kb - 2 have released its slot, and must be in place
+// before the tensor core runs out of k-block kb - 1's work, a chain of
+// barrier round trips that measured on B200 held the kernel to 188 of the
+// 215 TFLOP/s it reached with the wait removed (8192^3, split skipped in both
+// timing builds).  So each split thread loads its raw elements and computes
+// lo into registers as soon as the tile lands, and only stores them once the
+// slot is free.  (Stages of 16 K in the 64-byte swizzle, twice as many slots
+// in the same bytes, ran slower: 130 against 154 TFLOP/s.)
+// TMEM: the accumulator (columns [0, 256)) and the running total of the
+// finished K chunks ([256, 512)); the accumulator is single-buffered, so the
+// MMA thread waits for each chunk's drain, which two epilogue warps per TMEM
+// lane quadrant share by columns (8192^3 on B200: 4 epilogue + 8 split warps
+// 163 TFLOP/s, 8 + 6 169.5).
+//
+// Barriers (no TMA multicast anywhere):
+//   full[s]      per CTA: its own TMA loads of stage s landed.
+//   ready[s]     CTA 0, 2 x 8 arrivals: every split warp of both CTAs wrote lo
+//                for stage s (remote arrive, release.cluster).
+//   empty[s], lo_free[l], tfull
+//                per CTA, committed by CTA 0's MMA thread to both CTAs.
+//   tempty       CTA 0, 2 x 4 arrivals: the epilogue warps of both CTAs
+//                drained the accumulator.
+template <int CHUNK_KB>
+struct Tc2x3Config {
+    static constexpr int BM = 256, BN = 256;            // per CTA pair
+    static constexpr int kRowsCta = 128, kColsCta = 128;
+    static constexpr int BK = 32;                        // 128 bytes of float32 K
+    static constexpr int kMmaK = 8;
+    static constexpr int kKSteps = BK / kMmaK;
+    static constexpr int kChunk = 32;                    // MN elements per 128-byte row
+    static constexpr int kChunkBytes = 128 * BK;         // one MN-major box (4 KB)
+    static constexpr uint32_t kMnLayout = kLayoutSw128Base32B;
+    static constexpr uint32_t kMnSbo = 512;
+    static constexpr uint32_t kKLayout = kLayoutSw128;
+    static constexpr uint32_t kKSbo = 1024;
+    static constexpr int kATile = kRowsCta * BK * 4;     // 16 KB
+    static constexpr int kBTile = kColsCta * BK * 4;     // 16 KB
+    static constexpr int kLoadBytes = kATile + kBTile;   // per CTA and stage
+#ifndef PTG_PAIR3_STAGES
+#define PTG_PAIR3_STAGES 4
+#endif
+    static constexpr int kStages = PTG_PAIR3_STAGES;
+    static constexpr int kLoStages = 6 - kStages;
+    static constexpr int kLoOffset = kStages * kLoadBytes;
+    static constexpr int kRingBytes = kLoOffset + kLoStages * kLoadBytes;
+    static constexpr int kEpiCols = 32;                  // 128 bytes of float32 output
+    static constexpr int kEpiBufBytes = 32 * 128;
+#ifndef PTG_PAIR3_EPI
+#define PTG_PAIR3_EPI 8
+#endif
+    // epilogue warps: 4, or 8 (two per TMEM lane quadrant, each draining half
+    // of the columns, with one staging buffer each)
+    static constexpr int kEpiWarps = PTG_PAIR3_EPI;
+    static constexpr int kEpiParts = kEpiWarps / 4;
+    static constexpr int kEpiBufs = kEpiWarps == 4 ? 2 : 1;
+#ifndef PTG_PAIR3_SPLIT
+#define PTG_PAIR3_SPLIT 6
+#endif
+    static constexpr int kSplitWarps = PTG_PAIR3_SPLIT;
+    static constexpr int kThreads = 32 * (2 + kEpiWarps + kSplitWarps);
+    static constexpr int kEpiOffset = kRingBytes;
+    static constexpr int kBarOffset = kEpiOffset + kEpiWarps * kEpiBufs * kEpiBufBytes;
+    // full, empty, ready per stage; lo_free per lo slot; tfull, tempty, drain
+    static constexpr int kNumBars = 3 * kStages + kLoStages + 3;
+    static constexpr int kSmemBytes = kBarOffset + kNumBars * 8 + 16 + 1024;
+    static constexpr int kChunkKB = CHUNK_KB;            // k-blocks per accumulator chunk
+    static constexpr int kTotalCol = BN;
+    static constexpr int kTmemCols = 512;
+    static_assert(kSmemBytes <= 232448, "shared memory budget exceeded");
+};
+
+template <int CHUNK_KB>
+__global__ void __launch_bounds__(Tc2x3Config<CHUNK_KB>::kThreads, 1)
+    tc2x3_gemm_kernel(const __grid_constant__ CUtensorMap tma_a,
+                      const __grid_constant__ CUtensorMap tma_b,
+                      const __grid_constant__ CUtensorMap tma_c, const TcParams p)
+{
+    using Cfg = Tc2x3Config<CHUNK_KB>;
+    constexpr int S = Cfg::kStages;
+    constexpr int BN = Cfg::BN;
+
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + Cfg::kBarOffset);
+    uint64_t *full = bars;
+    uint64_t *empty = bars + S;
+    uint64_t *ready = bars + 2 * S;
+    uint64_t *lo_free = bars + 3 * S;
+    uint64_t *tfull = bars + 3 * S + Cfg::kLoStages;
+    uint64_t *tempty = tfull + 1;
+    uint64_t *drain = tfull + 2;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + Cfg::kNumBars);
+    volatile int *abort = reinterpret_cast<volatile int *>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const uint32_t rank = cluster_cta_rank();
+    const long long cluster = blockIdx.x >> 1;
+    const long long nclusters = gridDim.x >> 1;
+
+    if (warp == 0 && lane == 0) {
+        prefetch_tensor_map(&tma_a);
+        prefetch_tensor_map(&tma_b);
+        prefetch_tensor_map(&tma_c);
+        for (int s = 0; s < S; s++) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+            mbar_init(&ready[s], 2 * Cfg::kSplitWarps);
+        }
+        for (int i = 0; i < Cfg::kLoStages; i++)
+            mbar_init(&lo_free[i], 1);
+        mbar_init(tfull, 1);
+        mbar_init(tempty, 2 * Cfg::kEpiWarps);
+        mbar_init(drain, 1);
+        *abort = 0;
+        fence_barrier_init();
+    }
+    if (warp == 1) {
+        tmem_alloc_pair(tmem_slot, Cfg::kTmemCols);
+        tmem_relinquish_pair();
+    }
+    tc_fence_before();
+    __syncthreads();
+    cluster_sync();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+    grid_dependency_wait();
+    grid_launch_dependents();
+
+    if (warp == 0) {
+        // ------------------------------------------------------------ producer (both CTAs)
+        if (lane == 0) {
+            int stage = 0;
+            uint32_t phase = 0;
+            uint32_t issued_mask = 0, parity_mask = 0;
+            bool ok = true;
+            for (long long t = cluster; ok && t < p.tiles; t += nclusters) {
+                const int nb = static_cast<int>(t % p.n_blocks);
+                const long long r = t / p.n_blocks;
+                const int mb = static_cast<int>(r % p.m_blocks);
+                const long long batch = r / p.m_blocks;
+                int c[3], ca[3], cb[3];
+                decode_batch(batch, p, c);
+                operand_coords(c, p.a_slot, p.nbd, ca);
+                operand_coords(c, p.b_slot, p.nbd, cb);
+                const int m0 = mb * Cfg::BM + static_cast<int>(rank) * Cfg::kRowsCta;
+                const int n0 = nb * BN + static_cast<int>(rank) * Cfg::kColsCta;
+                for (int kbf = 0; kbf < p.k_blocks; kbf++) {
+                    int kb = kbf;
+                    if (p.nfd > 0) {
+                        int f = kbf / p.k_per_fold;
+                        kb = kbf - f * p.k_per_fold;
+                        for (int d = p.nfd - 1; d >= 0; d--) {
+                            const int coord = f % p.fshape[d];
+                            f /= p.fshape[d];
+                            if (p.a_fslot[d] >= 2)
+                                ca[p.a_fslot[d] - 2] = coord;
+                            if (p.b_fslot[d] >= 2)
+                                cb[p.b_fslot[d] - 2] = coord;
+                        }
+                    }
+                    if (!mbar_wait(&empty[stage], phase ^ 1, abort)) {
+                        record_failure(abort, p.status, DEV_TIMEOUT_PRODUCER);
+                        ok = false;
+                        break;
+                    }
+                    uint8_t *sa = smem + stage * Cfg::kLoadBytes;
+                    uint8_t *sb = sa + Cfg::kATile;
+                    mbar_arrive_expect_tx(&full[stage], Cfg::kLoadBytes);
+                    const int k0 = kb * Cfg::BK;
+                    if (!p.a_mn_major) {
+                        tma_load_5d(sa, &tma_a, &full[stage], k0, m0, ca[0], ca[1], ca[2]);
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < Cfg::kRowsCta / Cfg::kChunk; j++)
+                            tma_load_5d(sa + j * Cfg::kChunkBytes, &tma_a, &full[stage],
+                                        m0 + j * Cfg::kChunk, k0, ca[0], ca[1], ca[2]);
+                    }
+                    if (!p.b_mn_major) {
+                        tma_load_5d(sb, &tma_b, &full[stage], k0, n0, cb[0], cb[1], cb[2]);
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < Cfg::kColsCta / Cfg::kChunk; j++)
+                            tma_load_5d(sb + j * Cfg::kChunkBytes, &tma_b, &full[stage],
+                                        n0 + j * Cfg::kChunk, k0, cb[0], cb[1], cb[2]);
+                    }
+                    issued_mask |= 1u << stage;
+                    parity_mask = (parity_mask & ~(1u << stage)) | (phase << stage);
+                    if (++stage == S) {
+                        stage = 0;
+                        phase ^= 1;
+                    }
+                }
+            }
+            // every copy this thread started lands before shared memory can
+            // be released (bounded, ignores the abort flag)
+            for (int s = 0; s < S; s++) {
+                if (issued_mask & (1u << s)) {
+                    int no_abort = 0;
+                    mbar_wait(&full[s], (parity_mask >> s) & 1u, &no_abort);
+                }
+            }
+        }
+    } else if (warp == 1) {
+        // ------------------------------------------------------------ MMA issuer (CTA 0)
+        if (lane == 0 && rank == 0) {
+            int stage = 0, lo_slot = 0;
+            uint32_t phase = 0;
+            long long uses = 0;   // accumulator chunks issued
+            bool ok = true;
+            const uint32_t smem_base = smem_addr(smem);
+            const uint32_t a_lbo = p.a_mn_major ? Cfg::kChunkBytes : 16;
+            const uint32_t b_lbo = p.b_mn_major ? Cfg::kChunkBytes : 16;
+            const uint32_t a_sbo = p.a_mn_major ? Cfg::kMnSbo : Cfg::kKSbo;
+            const uint32_t b_sbo = p.b_mn_major ? Cfg::kMnSbo : Cfg::kKSbo;
+            const uint32_t a_lay = p.a_mn_major ? Cfg::kMnLayout : Cfg::kKLayout;
+            const uint32_t b_lay = p.b_mn_major ? Cfg::kMnLayout : Cfg::kKLayout;
+            for (long long t = cluster; ok && t < p.tiles; t += nclusters) {
+                for (int kb = 0; kb < p.k_blocks; kb++) {
+                    const int kc = kb % Cfg::kChunkKB;
+                    if (kc == 0) {
+                        if (!mbar_wait_cluster(tempty, static_cast<uint32_t>(uses & 1) ^ 1u, abort)) {
+                            record_failure(abort, p.status, DEV_TIMEOUT_MMA);
+                            ok = false;
+                            break;
+                        }
+                        tc_fence_after();
+                    }
+                    if (!mbar_wait_cluster(&ready[stage], phase, abort)) {
+                        record_failure(abort, p.status, DEV_TIMEOUT_MMA);
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t sa = smem_base + stage * Cfg::kLoadBytes;
+                    const uint32_t sb = sa + Cfg::kATile;
+                    const uint32_t la = smem_base + Cfg::kLoOffset +
+                                        static_cast<uint32_t>(lo_slot * Cfg::kLoadBytes);
+                    const uint32_t lb = la + Cfg::kATile;
+#pragma unroll
+                    for (int k = 0; k < Cfg::kKSteps; k++) {
+                        const uint32_t a_off = p.a_mn_major ? k * Cfg::kMmaK * 128 : k * 32;
+                        const uint32_t b_off = p.b_mn_major ? k * Cfg::kMmaK * 128 : k * 32;
+                        const uint64_t ad = smem_desc(sa + a_off, a_lbo, a_sbo, a_lay);
+                        const uint64_t bd = smem_desc(sb + b_off, b_lbo, b_sbo, b_lay);
+                        const uint64_t ad_lo = smem_desc(la + a_off, a_lbo, a_sbo, a_lay);
+                        const uint64_t bd_lo = smem_desc(lb + b_off, b_lbo, b_sbo, b_lay);
+                        umma_tf32_pair(tmem_base, ad, bd, p.idesc, (kc | k) != 0);
+                        umma_tf32_pair(tmem_base, ad, bd_lo, p.idesc, 1);
+                        umma_tf32_pair(tmem_base, ad_lo, bd, p.idesc, 1);
+                    }
+                    const uint32_t e0 = smem_addr(&empty[stage]);
+                    umma_commit_pair(e0);
+                    umma_commit_pair(map_to_cta(e0, 1));
+                    const uint32_t l0 = smem_addr(&lo_free[lo_slot]);
+                    umma_commit_pair(l0);
+                    umma_commit_pair(map_to_cta(l0, 1));
+                    if (++stage == S) {
+                        stage = 0;
+                        phase ^= 1;
+                    }
+                    if (++lo_slot == Cfg::kLoStages)
+                        lo_slot = 0;
+                    if (kc == Cfg::kChunkKB - 1 || kb == p.k_blocks - 1) {
+                        const uint32_t f0 = smem_addr(tfull);
+                        umma_commit_pair(f0);
+                        umma_commit_pair(map_to_cta(f0, 1));
+                        uses++;
+                    }
+                }
+            }
+            umma_commit_pair(smem_addr(drain));
+            int no_abort = 0;
+            mbar_wait(drain, 0, &no_abort);
+        }
+    } else if (warp < 2 + Cfg::kEpiWarps) {
+        // ------------------------------------------------------------ epilogue (both CTAs)
+        const int ew = warp - 2;
+        const int quad = warp & 3;
+        constexpr int kGroups = BN / 32 / Cfg::kEpiParts;   // 32-column groups per warp
+        const int g0 = (ew >> 2) * kGroups;
+        uint8_t *stage_buf = smem + Cfg::kEpiOffset + ew * Cfg::kEpiBufs * Cfg::kEpiBufBytes;
+        const uint32_t tempty0 = map_to_cta(smem_addr(tempty), 0);
+        int buf = 0;
+        long long uses = 0;
+        bool ok = true;
+        auto emit = [&](float (&v)[Cfg::kEpiCols], int col0, int row0, const int (&c)[3]) {
+            if (p.bias != nullptr || p.act != ACT_NONE)
+                apply_epilogue_compact<OUT_F32, Cfg::kEpiCols>(v, p.bias, p.act, col0, p.N, lane);
+            uint8_t *sbuf = stage_buf + buf * Cfg::kEpiBufBytes;
+            if (lane == 0) {
+                if constexpr (Cfg::kEpiBufs == 2)
+                    bulk_wait_group_read<1>();
+                else
+                    bulk_wait_group_read<0>();
+            }
+            __syncwarp();
+            uint8_t *rowp = sbuf + lane * 128;
+#pragma unroll
+            for (int j = 0; j < 8; j++) {
+                uint4 q;
+                q.x = __float_as_uint(v[4 * j + 0]);
+                q.y = __float_as_uint(v[4 * j + 1]);
+                q.z = __float_as_uint(v[4 * j + 2]);
+                q.w = __float_as_uint(v[4 * j + 3]);
+                *reinterpret_cast<uint4 *>(rowp + ((j ^ (lane & 7)) << 4)) = q;
+            }
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0 && col0 < p.N && row0 < p.M) {
+                tma_store_5d(&tma_c, sbuf, col0, row0, c[0], c[1], c[2]);
+                bulk_commit_group();
+            }
+            buf ^= Cfg::kEpiBufs - 1;
+        };
+        const int nchunks = (p.k_blocks + Cfg::kChunkKB - 1) / Cfg::kChunkKB;
+        const uint32_t lane_base = tmem_base + (static_cast<uint32_t>(quad * 32) << 16);
+        const uint32_t t_total = lane_base + static_cast<uint32_t>(Cfg::kTotalCol);
+        for (long long t = cluster; ok && t < p.tiles; t += nclusters) {
+            const int nb = static_cast<int>(t % p.n_blocks);
+            const long long r = t / p.n_blocks;
+            const int mb = static_cast<int>(r % p.m_blocks);
+            const long long batch = r / p.m_blocks;
+            int c[3];
+            decode_batch(batch, p, c);
+            const int row0 = mb * Cfg::BM + static_cast<int>(rank) * Cfg::kRowsCta + quad * 32;
+            const int n0 = nb * BN;
+            for (int ck = 0; ck < nchunks; ck++, uses++) {
+                const bool got = __all_sync(
+                    0xffffffffu, mbar_wait(tfull, static_cast<uint32_t>(uses & 1), abort));
+                if (!got) {
+                    if (lane == 0)
+                        record_failure(abort, p.status, DEV_TIMEOUT_EPILOGUE);
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const bool last = ck == nchunks - 1;
+#pragma unroll 1
+                for (int h = g0; h < g0 + kGroups; h++) {
+                    uint32_t r32[32], t32[32];
+                    tmem_ld_32x32b_x32(lane_base + h * 32, r32);
+                    if (ck > 0)
+                        tmem_ld_32x32b_x32(t_total + h * 32, t32);
+                    tmem_ld_wait();
+                    float v[32];
+#pragma unroll
+                    for (int i = 0; i < 32; i++)
+                        v[i] = (ck > 0 ? __uint_as_float(t32[i]) : 0.0f) + __uint_as_float(r32[i]);
+                    if (!last) {
+#pragma unroll
+                        for (int i = 0; i < 32; i++)
+                            t32[i] = __float_as_uint(v[i]);
+                        tmem_st_32x32b_x32(t_total + h * 32, t32);
+                    } else {
+                        if (h == g0 + kGroups - 1) {
+                            // accumulator fully read: hand it back to the MMA thread
+                            tc_fence_before();
+                            __syncwarp();
+                            if (lane == 0)
+                                mbar_arrive_cluster(tempty0);
+                        }
+                        emit(v, n0 + h * 32, row0, c);
+                    }
+                }
+                if (!last) {
+                    tmem_st_wait();
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0)
+                        mbar_arrive_cluster(tempty0);
+                }
+            }
+        }
+        if (lane == 0)
+            bulk_wait_group<0>();
+        __syncwarp();
+    } else {
+        // ------------------------------------------------------------ split warps (both CTAs)
+        // lo = tf32(x - trunc(x)) of this CTA's raw tiles into its lo ring;
+        // each warp then arrives on CTA 0's ready barrier.  Waits are made
+        // warp-uniform so a timeout leaves the warp together.
+        const int st = threadIdx.x - 32 * (2 + Cfg::kEpiWarps);   // 0..255
+        int stage = 0, lo_slot = 0;
+        uint32_t phase = 0, lo_phase = 0;
+        bool ok = true;
+        constexpr int kVecs = Cfg::kLoadBytes / 16;
+        constexpr int kPer = (kVecs + Cfg::kSplitWarps * 32 - 1) / (Cfg::kSplitWarps * 32);
+        auto lo_of = [](float x) { return isfinite(x) ? round_tf32(x - trunc_tf32(x)) : 0.0f; };
+        for (long long t = cluster; ok && t < p.tiles; t += nclusters) {
+            for (int kb = 0; kb < p.k_blocks; kb++) {
+                if (!__all_sync(0xffffffffu, mbar_wait(&full[stage], phase, abort))) {
+                    if (lane == 0)
+                        record_failure(abort, p.status, DEV_TIMEOUT_SPLIT);
+                    ok = false;
+                    break;
+                }
+                const float4 *raw = reinterpret_cast<const float4 *>(smem + stage * Cfg::kLoadBytes);
+                float4 l[kPer];
+#pragma unroll
+                for (int j = 0; j < kPer; j++) {
+                    const int i = st + j * Cfg::kSplitWarps * 32;
+                    if (kVecs % (Cfg::kSplitWarps * 32) == 0 || i < kVecs) {
+                        const float4 x = raw[i];
+                        l[j] = make_float4(lo_of(x.x), lo_of(x.y), lo_of(x.z), lo_of(x.w));
+                    }
+                }
+                if (!__all_sync(0xffffffffu, mbar_wait(&lo_free[lo_slot], lo_phase ^ 1, abort))) {
+                    if (lane == 0)
+                        record_failure(abort, p.status, DEV_TIMEOUT_SPLIT);
+                    ok = false;
+                    break;
+                }
+                float4 *lo = reinterpret_cast<float4 *>(smem + Cfg::kLoOffset +
+                                                        lo_slot * Cfg::kLoadBytes);
+#pragma unroll
+                for (int j = 0; j < kPer; j++) {
+                    const int i = st + j * Cfg::kSplitWarps * 32;
+                    if (kVecs % (Cfg::kSplitWarps * 32) == 0 || i < kVecs)
+                        lo[i] = l[j];
+                }
+                fence_proxy_async_smem();
+                __syncwarp();
+                if (lane == 0)
+                    mbar_arrive_cluster(map_to_cta(smem_addr(&ready[stage]), 0));
+                if (++stage == S) {
+                    stage = 0;
+                    phase ^= 1;
+                }
+                if (++lo_slot == Cfg::kLoStages) {
+                    lo_slot = 0;
+                    lo_phase ^= 1;
+                }
+            }
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    cluster_sync();
+    tc_fence_after();
+    if (warp == 1) {
+        __syncwarp();
+        tmem_dealloc_pair(tmem_base, Cfg::kTmemCols);
+    }
+}
+
 } // namespace ptg

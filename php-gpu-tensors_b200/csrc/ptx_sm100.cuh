@@ -377,6 +377,50 @@ __device__ __forceinline__ void umma_f16_pair(uint32_t d_tmem, uint64_t a_desc, 
         : "memory");
 }
 
+// Same with TF32 inputs (3xTF32 pair kernel).
+__device__ __forceinline__ void umma_tf32_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                               uint32_t idesc, uint32_t accumulate)
+{
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t *bar, uint32_t parity)
+{
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(smem_addr(bar)), "r"(parity)
+        : "memory");
+    return done != 0;
+}
+
+// mbar_wait for a barrier that threads of other CTAs of the cluster arrive on
+// (release.cluster): acquires at cluster scope, so their prior shared-memory
+// writes are visible to this thread and to the operations it issues next.
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t *bar, uint32_t parity,
+                                                  volatile int *abort)
+{
+    if (mbar_try_wait_cluster(bar, parity))
+        return true;
+    const uint64_t start = global_timer_ns();
+    for (;;) {
+        if (mbar_try_wait_cluster(bar, parity))
+            return true;
+        if (*abort)
+            return false;
+        if (global_timer_ns() - start > kWaitTimeoutNs)
+            return false;
+    }
+}
+
 // Arrives once on the mbarrier at `cluster_addr` (this CTA or its peer) when
 // all pair MMAs issued so far by this thread have completed.
 __device__ __forceinline__ void umma_commit_pair(uint32_t cluster_addr)

@@ -199,7 +199,7 @@ def test_seeded_parity(case, path, dtype):
     b = padded(bv, bshape, pad, dtype, bt)
     c = to_device(a, dtype).matmul(to_device(b, dtype))
     what = (name, path, P.cuda_get_backend_info()["kernel"])
-    if path == "tensor-core-pair" and dtype != "float32" and what[2].startswith("tc"):
+    if path == "tensor-core-pair" and what[2].startswith("tc"):
         assert what[2].startswith("tc2-"), what
     if path == "skinny" and case in SKINNY_CASES:
         assert what[2].startswith("skinny-"), what
@@ -361,6 +361,39 @@ def test_skinny_split_k_is_deterministic(dtype):
     assert P.device_status() == 0
 
 
+PAIR_3X_CASES = [
+    # (name, a_shape, b_shape, a_transposed, b_transposed): strict float32 on
+    # the 2-CTA 3xTF32 kernel -- more tiles than co-resident clusters, ragged
+    # K chunks, every operand layout, batches with broadcast
+    ("more_tiles_than_clusters", [2048, 256], [256, 2560], False, False),
+    ("ragged_chunks", [600, 520], [520, 700], False, False),
+    ("a_transposed", [520, 1000], [1000, 300], True, False),
+    ("b_transposed", [300, 392], [392, 520], False, True),
+    ("both_transposed", [264, 200], [200, 264], True, True),
+    ("batched_broadcast", [3, 1, 260, 136], [2, 136, 264], False, False),
+]
+
+
+@pytest.mark.parametrize("case", PAIR_3X_CASES, ids=[c[0] for c in PAIR_3X_CASES])
+def test_pair_3xtf32(case):
+    """The 2-CTA 3xTF32 kernel against the oracle's float64 twin (per-element
+    K-ulp bound and normwise 1e-5), bit-identical on repetition."""
+    name, ashape, bshape, at, bt = case
+    P.set_kernel_path("tensor-core-pair")
+    seed = sum(map(ord, name))
+    a = padded(O.seeded(ashape, seed, "normal"), ashape, 0, "float32", at)
+    b = padded(O.seeded(bshape, seed + 1, "normal"), bshape, 0, "float32", bt)
+    ad, bd = to_device(a, "float32"), to_device(b, "float32")
+    c = ad.matmul(bd)
+    assert P.cuda_get_backend_info()["kernel"] == "tc2-3xtf32-256x256", name
+    assert P.last_launch()[2] == 2
+    first = c.to_numpy()
+    check_fp32(first, a, b, name)
+    for _ in range(2):
+        assert np.array_equal(ad.matmul(bd).to_numpy(), first), name
+    assert P.device_status() == 0
+
+
 SPLIT_K_CASES = [
     # (name, a_shape, b_shape, a_transposed, b_transposed, dtype, expected cluster)
     ("splitk_fp32_g4", [256, 4096], [4096, 384], False, False, "float32", 4),
@@ -434,7 +467,7 @@ def test_fused_epilogue_matches_unfused_plan(dtype, act, N):
     a = to_device(O.dense(O.to_storage(av, dtype), [M, K]), dtype)
     x = to_device(O.dense(O.to_storage(xv, dtype), [N, K]), dtype)
     bdev = to_device(O.dense(O.to_storage(bias, dtype), [N]), dtype)
-    for path in ("tensor-core", "simt") + (("skinny",) if N <= 32 else ()):
+    for path in ("tensor-core", "tensor-core-pair", "simt") + (("skinny",) if N <= 32 else ()):
         P.set_kernel_path(path)
         fused = a.matmul_epilogue(x.transpose(), bdev, act).to_torch().float()
         plain = a.matmul(x.transpose()).to_torch().float()
@@ -648,8 +681,9 @@ FOLD_CASES = [
 ]
 
 
+@pytest.mark.parametrize("path", ["auto", "tensor-core-pair"])
 @pytest.mark.parametrize("case", FOLD_CASES, ids=[c[0] for c in FOLD_CASES])
-def test_backward_gradient_folded_into_the_product(case):
+def test_backward_gradient_folded_into_the_product(case, path):
     """A gradient requested in its operand's shape when the product broadcast
     that operand: the summed batch axes run inside the product kernel.
     Checked against the exact float64 sum of the per-batch products, and
@@ -665,6 +699,7 @@ def test_backward_gradient_folded_into_the_product(case):
     gshape = full + [M, N]
     gc = O.dense(O.seeded(gshape, seed + 2, "normal"), gshape)
     target = ashape if which == "a" else bshape
+    P.set_kernel_path(path)
     out = [P.CudaArray.zeros(target) for _ in range(3)]
     ad, bd, gd = to_device(a, dt), to_device(b, dt), to_device(gc, "float32")
     for o in out:
@@ -810,7 +845,7 @@ def _random_case(rng):
 
 
 @pytest.mark.parametrize("dtype", ["bfloat16", "float16", "float32"])
-@pytest.mark.parametrize("path", ["auto", "tensor-core", "skinny"])
+@pytest.mark.parametrize("path", ["auto", "tensor-core", "tensor-core-pair", "skinny"])
 def test_randomized_products(dtype, path):
     """40 seeded random products per dtype and kernel path against the oracle."""
     rng = np.random.default_rng(sum(map(ord, dtype + path)))
