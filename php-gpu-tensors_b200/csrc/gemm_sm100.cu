@@ -525,6 +525,7 @@ enum KernelId : int {
     KID_F64_DMMA,
     KID_F64_DMMA_PEER,
     KID_F32X3_PAIR,          // strict float32 on the 2-CTA 3xTF32 kernel
+    KID_TF32_PAIR,           // tf32 precision mode on the 2-CTA kernel
     KID_SKINNY_ASYNC = 16,   // 24 ids: (float64 ? 12 : 0) + 2 * index of NB in {4,8,12,16,24,32} + A k-major
     KID_MIX_A = 40,          // float32 A (split into 3 bf16) x bf16 B -> float32
     KID_MIX_B,               // bf16 A x float32 B -> float32
@@ -546,6 +547,7 @@ const char *kernel_name(int kid)
     case KID_F16_PAIR: return "tc2-f16-256x256";
     case KID_F64_DMMA: return "dmma-f64-128x128";
     case KID_F32X3_PAIR: return "tc2-3xtf32-256x256";
+    case KID_TF32_PAIR: return "tc2-tf32-256x256";
     case KID_MIX_A: return "tc-f32xbf16-bf16x3-128x128";
     case KID_MIX_B: return "tc-bf16xf32-bf16x3-128x128";
     case KID_BF16_F32: return "tc-bf16-f32out-128x128";
@@ -752,8 +754,13 @@ int try_tc(const Problem &P, DeviceState *ds, cudaStream_t stream, int *kid_out)
     bool pair = false;
     const bool strict = fp32 && t_precision == CUDA_MATMUL_PRECISION_FP32_STRICT;
     const long long tiles_pair = P.batches * ((P.M + 255) / 256) * ((P.N + 255) / 256);
-    if (!fp32 && P.forced_bn == 0)
-        pair = t_path == 3 || (t_path != 1 && tiles_pair >= ds->sms / 2);
+    // 16-bit products and the tf32 precision mode: the 2-CTA kernel once it
+    // has at least sms / 4 tiles of 256 x 256.  From there on it runs as
+    // many CTAs as the single-CTA 128 x 256 kernel, each streaming a third
+    // fewer bytes per FLOP (B200, tf32 4096x1024x1024 with 64 pair tiles:
+    // 21.4 against 23.3 us); below it the 128 x 128 tiles fill more SMs.
+    if ((!fp32 || !strict) && P.forced_bn == 0)
+        pair = t_path == 3 || (t_path != 1 && tiles_pair >= ds->sms / 4);
     if (wide_out || folded)
         bn = wide_out ? 128 : bn, pair = false;
     // Strict float32: the 2-CTA 3xTF32 kernel runs a 256 x 256 tile in
@@ -787,7 +794,7 @@ int try_tc(const Problem &P, DeviceState *ds, cudaStream_t stream, int *kid_out)
                             : mix_side == 1 ? KID_MIX_B : (op_dt == DT_BF16 ? KID_BF16_F32 : KID_F16_F32);
     else if (fp32)
         kid = strict ? (pair ? KID_F32X3_PAIR : KID_F32X3_128)
-                     : (bn == 256 ? KID_TF32_256 : KID_TF32_128);
+                     : (pair ? KID_TF32_PAIR : (bn == 256 ? KID_TF32_256 : KID_TF32_128));
     else if (P.dt == DT_BF16)
         kid = pair ? KID_BF16_PAIR : (bn == 256 ? KID_BF16_256 : KID_BF16_128);
     else
@@ -886,6 +893,7 @@ int try_tc(const Problem &P, DeviceState *ds, cudaStream_t stream, int *kid_out)
     case KID_TF32_256: err = launch_tc_kernel<IN_TF32, 256, OUT_F32>(ds, kid, tma_a, tma_b, tma_c, p, stream); break;
     case KID_BF16_PAIR: err = launch_tc2_kernel<IN_BF16, OUT_BF16>(ds, kid, 0, tma_a, tma_b, tma_c, p, stream); break;
     case KID_F16_PAIR: err = launch_tc2_kernel<IN_F16, OUT_F16>(ds, kid, 1, tma_a, tma_b, tma_c, p, stream); break;
+    case KID_TF32_PAIR: err = launch_tc2_kernel<IN_TF32, OUT_F32>(ds, kid, 3, tma_a, tma_b, tma_c, p, stream); break;
     case KID_F32X3_PAIR:
         err = launch_pair_kernel<Tc2x3Config<kPairChunkKB>>(ds, kid, 2, tc2x3_gemm_kernel<kPairChunkKB>,
                                                             tma_a, tma_b, tma_c, p, stream);

@@ -1,4 +1,6 @@
-// 2-CTA (cta_group::2) tcgen05 GEMM for 16-bit operands on sm_100a.
+// 2-CTA (cta_group::2) tcgen05 GEMMs on sm_100a: 16-bit operands and
+// single-pass TF32 (float32 operands in the tf32 precision mode) in
+// tc2_gemm_kernel, strict float32 (3xTF32) in tc2x3_gemm_kernel below.
 //
 // A cluster of two CTAs on neighbouring SMs computes a 256 x 256 output tile:
 // CTA r (r = 0, 1) loads rows [128 r, 128 r + 128) of the A tile and columns
@@ -28,17 +30,23 @@ template <int IN_KIND, int OUT>
 struct Tc2Config {
     static constexpr int BM = 256, BN = 256;          // per CTA pair
     static constexpr int kRowsCta = 128, kColsCta = 128;
-    static constexpr int BK = 64;                      // 128 bytes of 16-bit K
-    static constexpr int kMmaK = 16;
+    static constexpr bool kTf32 = IN_KIND == IN_TF32;
+    static constexpr int kInBytes = kTf32 ? 4 : 2;
+    static constexpr int BK = 128 / kInBytes;          // one 128-byte swizzle row of K
+    static constexpr int kMmaK = 32 / kInBytes;        // 32 bytes of K per instruction
     static constexpr int kKSteps = BK / kMmaK;
-    static constexpr int kChunk = 64;                  // MN elements per 128-byte row
-    static constexpr int kChunkBytes = 128 * BK;       // one MN-major box (8 KB)
-    static constexpr int kATile = kRowsCta * BK * 2;   // 16 KB
-    static constexpr int kBTile = kColsCta * BK * 2;   // 16 KB
+    static constexpr int kChunk = 128 / kInBytes;      // MN elements per 128-byte row
+    static constexpr int kChunkBytes = 128 * BK;       // one MN-major box (kChunk x BK)
+    // MN-major TF32 tiles use the 32-byte-atom 128-byte swizzle (as in the
+    // single-CTA kernel); everything else the 16-byte-atom one
+    static constexpr uint32_t kMnLayout = kTf32 ? kLayoutSw128Base32B : kLayoutSw128;
+    static constexpr uint32_t kMnSbo = kTf32 ? 512 : 1024;
+    static constexpr int kATile = kRowsCta * BK * kInBytes;   // 16 KB
+    static constexpr int kBTile = kColsCta * BK * kInBytes;   // 16 KB
     static constexpr int kLoadBytes = kATile + kBTile; // per CTA and stage
     static constexpr int kStageBytes = kLoadBytes;
     static constexpr int kStages = 6;
-    static constexpr int kEpiCols = 64;                // 128 bytes of 16-bit output
+    static constexpr int kEpiCols = 128 / OutTraits<OUT>::kBytes;   // 128 bytes of output
     static constexpr int kEpiChunks = BN / kEpiCols;
     static constexpr int kEpiBufBytes = 32 * 128;
     static constexpr int kEpiWarps = 4;
@@ -51,7 +59,10 @@ struct Tc2Config {
     static constexpr int kNumBars = 2 * kStages + 4 + 1;
     static constexpr int kSmemBytes = kBarOffset + kNumBars * 8 + 16 + 1024;
     static_assert(kSmemBytes <= 232448, "shared memory budget exceeded");
-    static_assert(IN_KIND == IN_F16 || IN_KIND == IN_BF16, "16-bit operands only");
+    static_assert(IN_KIND == IN_F16 || IN_KIND == IN_BF16 || IN_KIND == IN_TF32,
+                  "16-bit or single-pass TF32 operands");
+    static_assert(kTf32 == (OUT == OUT_F32), "TF32 products write float32");
+    static_assert(kATile == 16384 && kBTile == 16384, "one 128-byte row of K per tile row");
 };
 
 // Settle time for copies a CTA may still have in flight after it gave up a
@@ -219,11 +230,16 @@ __global__ void __launch_bounds__(Tc2Config<IN_KIND, OUT>::kThreads, 1)
                     for (int k = 0; k < Cfg::kKSteps; k++) {
                         const uint32_t a_off = p.a_mn_major ? k * Cfg::kMmaK * 128 : k * 32;
                         const uint32_t b_off = p.b_mn_major ? k * Cfg::kMmaK * 128 : k * 32;
-                        const uint64_t ad = smem_desc(sa + a_off, p.a_mn_major ? Cfg::kChunkBytes : 16,
-                                                      1024, kLayoutSw128);
-                        const uint64_t bd = smem_desc(sb + b_off, p.b_mn_major ? Cfg::kChunkBytes : 16,
-                                                      1024, kLayoutSw128);
-                        umma_f16_pair(d_tmem, ad, bd, p.idesc, (kb | k) != 0);
+                        const uint64_t ad =
+                            p.a_mn_major ? smem_desc(sa + a_off, Cfg::kChunkBytes, Cfg::kMnSbo, Cfg::kMnLayout)
+                                         : smem_desc(sa + a_off, 16, 1024, kLayoutSw128);
+                        const uint64_t bd =
+                            p.b_mn_major ? smem_desc(sb + b_off, Cfg::kChunkBytes, Cfg::kMnSbo, Cfg::kMnLayout)
+                                         : smem_desc(sb + b_off, 16, 1024, kLayoutSw128);
+                        if constexpr (Cfg::kTf32)
+                            umma_tf32_pair(d_tmem, ad, bd, p.idesc, (kb | k) != 0);
+                        else
+                            umma_f16_pair(d_tmem, ad, bd, p.idesc, (kb | k) != 0);
                     }
                     const uint32_t e0 = smem_addr(&empty[stage]);
                     umma_commit_pair(e0);
@@ -299,10 +315,17 @@ __global__ void __launch_bounds__(Tc2Config<IN_KIND, OUT>::kThreads, 1)
 #pragma unroll
                 for (int j = 0; j < 8; j++) {
                     uint4 q;
-                    q.x = pack2(v[8 * j + 0], v[8 * j + 1], OUT);
-                    q.y = pack2(v[8 * j + 2], v[8 * j + 3], OUT);
-                    q.z = pack2(v[8 * j + 4], v[8 * j + 5], OUT);
-                    q.w = pack2(v[8 * j + 6], v[8 * j + 7], OUT);
+                    if constexpr (OUT == OUT_F32) {
+                        q.x = __float_as_uint(v[4 * j + 0]);
+                        q.y = __float_as_uint(v[4 * j + 1]);
+                        q.z = __float_as_uint(v[4 * j + 2]);
+                        q.w = __float_as_uint(v[4 * j + 3]);
+                    } else {
+                        q.x = pack2(v[8 * j + 0], v[8 * j + 1], OUT);
+                        q.y = pack2(v[8 * j + 2], v[8 * j + 3], OUT);
+                        q.z = pack2(v[8 * j + 4], v[8 * j + 5], OUT);
+                        q.w = pack2(v[8 * j + 6], v[8 * j + 7], OUT);
+                    }
                     *reinterpret_cast<uint4 *>(rowp + ((j ^ (lane & 7)) << 4)) = q;
                 }
                 fence_proxy_async_smem();

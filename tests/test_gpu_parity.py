@@ -394,6 +394,32 @@ def test_pair_3xtf32(case):
     assert P.device_status() == 0
 
 
+@pytest.mark.parametrize("case", PAIR_3X_CASES, ids=[c[0] for c in PAIR_3X_CASES])
+def test_pair_tf32_mode(case):
+    """The tf32 precision mode on the 2-CTA kernel: within the TF32 error
+    bound of the float64 product (operands truncated to 10 mantissa bits,
+    float32 accumulation) and bit-identical on repetition."""
+    name, ashape, bshape, at, bt = case
+    seed = sum(map(ord, name))
+    a = padded(O.seeded(ashape, seed, "normal"), ashape, 0, "float32", at)
+    b = padded(O.seeded(bshape, seed + 1, "normal"), bshape, 0, "float32", bt)
+    ad, bd = to_device(a, "float32"), to_device(b, "float32")
+    P.cuda_set_matmul_precision("tf32")
+    P.set_kernel_path("tensor-core-pair")
+    first = ad.matmul(bd).to_numpy().astype(np.float64).reshape(-1)
+    assert P.cuda_get_backend_info()["kernel"] == "tc2-tf32-256x256", name
+    assert np.array_equal(ad.matmul(bd).to_numpy().astype(np.float64).reshape(-1), first), name
+    P.cuda_set_matmul_precision("fp32-strict")
+    th = O.oracle().orc_host_threads()
+    c64 = O.host_matmul_f64(a, b, "float32", th).reshape(-1)
+    absp = O.host_matmul_f64(O.absolute(a, "float32"), O.absolute(b, "float32"), "float32",
+                             th).reshape(-1)
+    K = a[1][-1]
+    bound = (2.0 ** -9 + K * 2.0 ** -23) * absp
+    assert np.all(np.abs(first - c64) <= bound + 1e-30), name
+    assert P.device_status() == 0
+
+
 SPLIT_K_CASES = [
     # (name, a_shape, b_shape, a_transposed, b_transposed, dtype, expected cluster)
     ("splitk_fp32_g4", [256, 4096], [4096, 384], False, False, "float32", 4),
