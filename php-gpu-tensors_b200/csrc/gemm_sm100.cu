@@ -60,6 +60,9 @@ constexpr int kPairChunkKB = PTG_PAIR_CHUNK_KB;
 // choice matches the faster kernel on every measured shape (8192^3 pair,
 // 4096^3 single-CTA, the config-4 layer products pair, their dW single-CTA).
 constexpr double kPairTileCost = 1.79;
+// mixed kinds on the 2-CTA kernel: k-blocks (64 K each) per accumulator chunk,
+// 256 K as in the single-CTA mixed kernel
+constexpr int kMixPairChunkKB = 4;
 constexpr double kTuneMinWork = 10000000.0; // matmul_kernels.cu:24 (MATMUL_LT_MIN_WORK)
 
 struct Problem {
@@ -110,7 +113,7 @@ struct DeviceState {
     int cc_major, cc_minor;
     int *status;                   // this device's copy of g_device_status
     unsigned long long attr_mask;  // kernels whose shared-memory limit has been raised
-    int pair_clusters[4];          // co-resident 2-CTA clusters per pair kernel (0 = unknown)
+    int pair_clusters[8];          // co-resident 2-CTA clusters per pair kernel (0 = unknown)
 };
 std::mutex g_mutex;
 DeviceState g_devices[kMaxDevices];
@@ -526,6 +529,8 @@ enum KernelId : int {
     KID_F64_DMMA_PEER,
     KID_F32X3_PAIR,          // strict float32 on the 2-CTA 3xTF32 kernel
     KID_TF32_PAIR,           // tf32 precision mode on the 2-CTA kernel
+    KID_MIX_A_PAIR,          // float32 A x bf16 B on the 2-CTA bf16x3 kernel
+    KID_MIX_B_PAIR,          // bf16 A x float32 B on the 2-CTA bf16x3 kernel
     KID_SKINNY_ASYNC = 16,   // 24 ids: (float64 ? 12 : 0) + 2 * index of NB in {4,8,12,16,24,32} + A k-major
     KID_MIX_A = 40,          // float32 A (split into 3 bf16) x bf16 B -> float32
     KID_MIX_B,               // bf16 A x float32 B -> float32
@@ -548,6 +553,8 @@ const char *kernel_name(int kid)
     case KID_F64_DMMA: return "dmma-f64-128x128";
     case KID_F32X3_PAIR: return "tc2-3xtf32-256x256";
     case KID_TF32_PAIR: return "tc2-tf32-256x256";
+    case KID_MIX_A_PAIR: return "tc2-f32xbf16-bf16x3-256x256";
+    case KID_MIX_B_PAIR: return "tc2-bf16xf32-bf16x3-256x256";
     case KID_MIX_A: return "tc-f32xbf16-bf16x3-128x128";
     case KID_MIX_B: return "tc-bf16xf32-bf16x3-128x128";
     case KID_BF16_F32: return "tc-bf16-f32out-128x128";
@@ -763,16 +770,19 @@ int try_tc(const Problem &P, DeviceState *ds, cudaStream_t stream, int *kid_out)
         pair = t_path == 3 || (t_path != 1 && tiles_pair >= ds->sms / 4);
     if (wide_out || folded)
         bn = wide_out ? 128 : bn, pair = false;
-    // Strict float32: the 2-CTA 3xTF32 kernel runs a 256 x 256 tile in
-    // kPairTileCost single-CTA 128 x 128 tile times (measured on B200), so it
-    // is chosen when its rounds of co-resident clusters take less time than
-    // the single-CTA kernel's waves (or its split-K launch).
-    if (strict && P.forced_bn == 0) {
+    // Strict float32 and the mixed float32 x bf16 kinds: the 2-CTA split
+    // kernel runs a 256 x 256 tile in kPairTileCost single-CTA 128 x 128 tile
+    // times (measured on B200), so it is chosen when its rounds of
+    // co-resident clusters take less time than the single-CTA kernel's waves
+    // (or its split-K launch).
+    const bool mix = mix_side >= 0;
+    if ((strict || mix) && P.forced_bn == 0) {
         if (t_path == 3) {
             pair = true;
         } else if (t_path == 0) {
             const long long tiles1 = P.batches * m_blocks * ((P.N + 127) / 128);
-            const long long kb1 = static_cast<long long>((P.K + 31) / 32) * P.folds;
+            const int bk1 = 128 / es;
+            const long long kb1 = static_cast<long long>((P.K + bk1 - 1) / bk1) * P.folds;
             double t1 = std::ceil(static_cast<double>(tiles1) / ds->sms);
             if (tiles1 < ds->sms / 2) {
                 for (int g : {4, 2}) {
@@ -790,8 +800,9 @@ int try_tc(const Problem &P, DeviceState *ds, cudaStream_t stream, int *kid_out)
     if (pair)
         bn = 256;
     if (wide_out)
-        kid = mix_side == 0 ? KID_MIX_A
-                            : mix_side == 1 ? KID_MIX_B : (op_dt == DT_BF16 ? KID_BF16_F32 : KID_F16_F32);
+        kid = mix_side == 0   ? (pair ? KID_MIX_A_PAIR : KID_MIX_A)
+              : mix_side == 1 ? (pair ? KID_MIX_B_PAIR : KID_MIX_B)
+                              : (op_dt == DT_BF16 ? KID_BF16_F32 : KID_F16_F32);
     else if (fp32)
         kid = strict ? (pair ? KID_F32X3_PAIR : KID_F32X3_128)
                      : (pair ? KID_TF32_PAIR : (bn == 256 ? KID_TF32_256 : KID_TF32_128));
@@ -895,8 +906,16 @@ int try_tc(const Problem &P, DeviceState *ds, cudaStream_t stream, int *kid_out)
     case KID_F16_PAIR: err = launch_tc2_kernel<IN_F16, OUT_F16>(ds, kid, 1, tma_a, tma_b, tma_c, p, stream); break;
     case KID_TF32_PAIR: err = launch_tc2_kernel<IN_TF32, OUT_F32>(ds, kid, 3, tma_a, tma_b, tma_c, p, stream); break;
     case KID_F32X3_PAIR:
-        err = launch_pair_kernel<Tc2x3Config<kPairChunkKB>>(ds, kid, 2, tc2x3_gemm_kernel<kPairChunkKB>,
-                                                            tma_a, tma_b, tma_c, p, stream);
+        err = launch_pair_kernel<Tc2x3Config<IN_F32X3, kPairChunkKB>>(
+            ds, kid, 2, tc2x3_gemm_kernel<IN_F32X3, kPairChunkKB>, tma_a, tma_b, tma_c, p, stream);
+        break;
+    case KID_MIX_A_PAIR:
+        err = launch_pair_kernel<Tc2x3Config<IN_MIX_A, kMixPairChunkKB>>(
+            ds, kid, 4, tc2x3_gemm_kernel<IN_MIX_A, kMixPairChunkKB>, tma_a, tma_b, tma_c, p, stream);
+        break;
+    case KID_MIX_B_PAIR:
+        err = launch_pair_kernel<Tc2x3Config<IN_MIX_B, kMixPairChunkKB>>(
+            ds, kid, 5, tc2x3_gemm_kernel<IN_MIX_B, kMixPairChunkKB>, tma_a, tma_b, tma_c, p, stream);
         break;
     case KID_MIX_A: err = launch_tc_kernel<IN_MIX_A, 128, OUT_F32>(ds, kid, tma_a, tma_b, tma_c, p, stream); break;
     case KID_MIX_B: err = launch_tc_kernel<IN_MIX_B, 128, OUT_F32>(ds, kid, tma_a, tma_b, tma_c, p, stream); break;

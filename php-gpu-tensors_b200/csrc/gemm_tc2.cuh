@@ -386,28 +386,40 @@ __global__ void __launch_bounds__(Tc2Config<IN_KIND, OUT>::kThreads, 1)
 //                per CTA, committed by CTA 0's MMA thread to both CTAs.
 //   tempty       CTA 0, 2 x 4 arrivals: the epilogue warps of both CTAs
 //                drained the accumulator.
-template <int CHUNK_KB>
+template <int KIND, int CHUNK_KB>
 struct Tc2x3Config {
+    static constexpr bool kMix = KIND == IN_MIX_A || KIND == IN_MIX_B;
+    static constexpr bool kMixA = KIND == IN_MIX_A;      // the float32 operand is A
+    static_assert(KIND == IN_F32X3 || kMix, "3xTF32 or bf16x3 pair kernel");
     static constexpr int BM = 256, BN = 256;            // per CTA pair
     static constexpr int kRowsCta = 128, kColsCta = 128;
-    static constexpr int BK = 32;                        // 128 bytes of float32 K
-    static constexpr int kMmaK = 8;
+    // K per stage: one 128-byte row of the MMA operand type (float32 for
+    // 3xTF32, bfloat16 for the mixed kinds)
+    static constexpr int kOpBytes = kMix ? 2 : 4;
+    static constexpr int BK = 128 / kOpBytes;
+    static constexpr int kMmaK = 32 / kOpBytes;
     static constexpr int kKSteps = BK / kMmaK;
-    static constexpr int kChunk = 32;                    // MN elements per 128-byte row
-    static constexpr int kChunkBytes = 128 * BK;         // one MN-major box (4 KB)
-    static constexpr uint32_t kMnLayout = kLayoutSw128Base32B;
-    static constexpr uint32_t kMnSbo = 512;
+    static constexpr int kChunk = 128 / kOpBytes;        // MN elements per 128-byte row
+    static constexpr int kChunkBytes = 128 * BK;         // one MN-major box
+    static constexpr uint32_t kMnLayout = kMix ? kLayoutSw128 : kLayoutSw128Base32B;
+    static constexpr uint32_t kMnSbo = kMix ? 1024 : 512;
     static constexpr uint32_t kKLayout = kLayoutSw128;
     static constexpr uint32_t kKSbo = 1024;
-    static constexpr int kATile = kRowsCta * BK * 4;     // 16 KB
-    static constexpr int kBTile = kColsCta * BK * 4;     // 16 KB
-    static constexpr int kLoadBytes = kATile + kBTile;   // per CTA and stage
+    static constexpr int kATile = kRowsCta * BK * kOpBytes;   // 16 KB
+    static constexpr int kBTile = kColsCta * BK * kOpBytes;   // 16 KB
+    // mixed: the float32 operand lands raw (one unswizzled [128][BK] box,
+    // 32 KB) at the stage start and is split in place into its bf16 hi and
+    // mid tiles, lo after them; the bf16 operand's tile follows
+    static constexpr int kMixRawBytes = 128 * BK * 4;
+    static constexpr int kMixOtherOffset = kMixRawBytes + kATile;
+    static constexpr int kLoadBytes = kMix ? kMixRawBytes + kATile : kATile + kBTile;
+    static constexpr int kStageBytes = kMix ? kMixOtherOffset + kATile : kLoadBytes;
 #ifndef PTG_PAIR3_STAGES
 #define PTG_PAIR3_STAGES 4
 #endif
-    static constexpr int kStages = PTG_PAIR3_STAGES;
-    static constexpr int kLoStages = 6 - kStages;
-    static constexpr int kLoOffset = kStages * kLoadBytes;
+    static constexpr int kStages = kMix ? 3 : PTG_PAIR3_STAGES;
+    static constexpr int kLoStages = kMix ? 0 : 6 - kStages;
+    static constexpr int kLoOffset = kStages * kStageBytes;
     static constexpr int kRingBytes = kLoOffset + kLoStages * kLoadBytes;
     static constexpr int kEpiCols = 32;                  // 128 bytes of float32 output
     static constexpr int kEpiBufBytes = 32 * 128;
@@ -435,13 +447,13 @@ struct Tc2x3Config {
     static_assert(kSmemBytes <= 232448, "shared memory budget exceeded");
 };
 
-template <int CHUNK_KB>
-__global__ void __launch_bounds__(Tc2x3Config<CHUNK_KB>::kThreads, 1)
+template <int KIND, int CHUNK_KB>
+__global__ void __launch_bounds__(Tc2x3Config<KIND, CHUNK_KB>::kThreads, 1)
     tc2x3_gemm_kernel(const __grid_constant__ CUtensorMap tma_a,
                       const __grid_constant__ CUtensorMap tma_b,
                       const __grid_constant__ CUtensorMap tma_c, const TcParams p)
 {
-    using Cfg = Tc2x3Config<CHUNK_KB>;
+    using Cfg = Tc2x3Config<KIND, CHUNK_KB>;
     constexpr int S = Cfg::kStages;
     constexpr int BN = Cfg::BN;
 
@@ -531,12 +543,26 @@ __global__ void __launch_bounds__(Tc2x3Config<CHUNK_KB>::kThreads, 1)
                         ok = false;
                         break;
                     }
-                    uint8_t *sa = smem + stage * Cfg::kLoadBytes;
+                    uint8_t *sa = smem + stage * Cfg::kStageBytes;
                     uint8_t *sb = sa + Cfg::kATile;
+                    if constexpr (Cfg::kMix) {
+                        // the float32 operand raw at the stage start, the
+                        // bf16 one after its three parts
+                        if constexpr (Cfg::kMixA)
+                            sb = sa + Cfg::kMixOtherOffset;
+                        else
+                            sa = sa + Cfg::kMixOtherOffset, sb = smem + stage * Cfg::kStageBytes;
+                    }
                     mbar_arrive_expect_tx(&full[stage], Cfg::kLoadBytes);
                     const int k0 = kb * Cfg::BK;
+                    // A: K-major one box, MN-major one box per 128-byte chunk
+                    // of M (the raw float32 operand of a mixed kind is always
+                    // one unswizzled box); B likewise
+                    const bool a_raw = Cfg::kMixA, b_raw = Cfg::kMix && !Cfg::kMixA;
                     if (!p.a_mn_major) {
                         tma_load_5d(sa, &tma_a, &full[stage], k0, m0, ca[0], ca[1], ca[2]);
+                    } else if (a_raw) {
+                        tma_load_5d(sa, &tma_a, &full[stage], m0, k0, ca[0], ca[1], ca[2]);
                     } else {
 #pragma unroll
                         for (int j = 0; j < Cfg::kRowsCta / Cfg::kChunk; j++)
@@ -545,6 +571,8 @@ __global__ void __launch_bounds__(Tc2x3Config<CHUNK_KB>::kThreads, 1)
                     }
                     if (!p.b_mn_major) {
                         tma_load_5d(sb, &tma_b, &full[stage], k0, n0, cb[0], cb[1], cb[2]);
+                    } else if (b_raw) {
+                        tma_load_5d(sb, &tma_b, &full[stage], n0, k0, cb[0], cb[1], cb[2]);
                     } else {
 #pragma unroll
                         for (int j = 0; j < Cfg::kColsCta / Cfg::kChunk; j++)
@@ -599,35 +627,58 @@ __global__ void __launch_bounds__(Tc2x3Config<CHUNK_KB>::kThreads, 1)
                         break;
                     }
                     tc_fence_after();
-                    const uint32_t sa = smem_base + stage * Cfg::kLoadBytes;
-                    const uint32_t sb = sa + Cfg::kATile;
-                    const uint32_t la = smem_base + Cfg::kLoOffset +
-                                        static_cast<uint32_t>(lo_slot * Cfg::kLoadBytes);
-                    const uint32_t lb = la + Cfg::kATile;
+                    const uint32_t stage_base = smem_base + stage * Cfg::kStageBytes;
+                    if constexpr (Cfg::kMix) {
+                        // hi, mid and lo of the float32 operand (bf16 tiles at
+                        // 0, 16 and 32 KB of the stage) against the bf16 operand
+                        const uint32_t sa = Cfg::kMixA ? stage_base : stage_base + Cfg::kMixOtherOffset;
+                        const uint32_t sb = Cfg::kMixA ? stage_base + Cfg::kMixOtherOffset : stage_base;
 #pragma unroll
-                    for (int k = 0; k < Cfg::kKSteps; k++) {
-                        const uint32_t a_off = p.a_mn_major ? k * Cfg::kMmaK * 128 : k * 32;
-                        const uint32_t b_off = p.b_mn_major ? k * Cfg::kMmaK * 128 : k * 32;
-                        const uint64_t ad = smem_desc(sa + a_off, a_lbo, a_sbo, a_lay);
-                        const uint64_t bd = smem_desc(sb + b_off, b_lbo, b_sbo, b_lay);
-                        const uint64_t ad_lo = smem_desc(la + a_off, a_lbo, a_sbo, a_lay);
-                        const uint64_t bd_lo = smem_desc(lb + b_off, b_lbo, b_sbo, b_lay);
-                        umma_tf32_pair(tmem_base, ad, bd, p.idesc, (kc | k) != 0);
-                        umma_tf32_pair(tmem_base, ad, bd_lo, p.idesc, 1);
-                        umma_tf32_pair(tmem_base, ad_lo, bd, p.idesc, 1);
+                        for (int k = 0; k < Cfg::kKSteps; k++) {
+                            const uint32_t a_off = p.a_mn_major ? k * Cfg::kMmaK * 128 : k * 32;
+                            const uint32_t b_off = p.b_mn_major ? k * Cfg::kMmaK * 128 : k * 32;
+#pragma unroll
+                            for (int part = 0; part < 3; part++) {
+                                const uint32_t pa = Cfg::kMixA ? part * Cfg::kATile : 0;
+                                const uint32_t pb = Cfg::kMixA ? 0 : part * Cfg::kATile;
+                                umma_f16_pair(tmem_base, smem_desc(sa + pa + a_off, a_lbo, a_sbo, a_lay),
+                                              smem_desc(sb + pb + b_off, b_lbo, b_sbo, b_lay), p.idesc,
+                                              (kc | k | part) != 0);
+                            }
+                        }
+                    } else {
+                        const uint32_t sa = stage_base;
+                        const uint32_t sb = sa + Cfg::kATile;
+                        const uint32_t la = smem_base + Cfg::kLoOffset +
+                                            static_cast<uint32_t>(lo_slot * Cfg::kLoadBytes);
+                        const uint32_t lb = la + Cfg::kATile;
+#pragma unroll
+                        for (int k = 0; k < Cfg::kKSteps; k++) {
+                            const uint32_t a_off = p.a_mn_major ? k * Cfg::kMmaK * 128 : k * 32;
+                            const uint32_t b_off = p.b_mn_major ? k * Cfg::kMmaK * 128 : k * 32;
+                            const uint64_t ad = smem_desc(sa + a_off, a_lbo, a_sbo, a_lay);
+                            const uint64_t bd = smem_desc(sb + b_off, b_lbo, b_sbo, b_lay);
+                            const uint64_t ad_lo = smem_desc(la + a_off, a_lbo, a_sbo, a_lay);
+                            const uint64_t bd_lo = smem_desc(lb + b_off, b_lbo, b_sbo, b_lay);
+                            umma_tf32_pair(tmem_base, ad, bd, p.idesc, (kc | k) != 0);
+                            umma_tf32_pair(tmem_base, ad, bd_lo, p.idesc, 1);
+                            umma_tf32_pair(tmem_base, ad_lo, bd, p.idesc, 1);
+                        }
                     }
                     const uint32_t e0 = smem_addr(&empty[stage]);
                     umma_commit_pair(e0);
                     umma_commit_pair(map_to_cta(e0, 1));
-                    const uint32_t l0 = smem_addr(&lo_free[lo_slot]);
-                    umma_commit_pair(l0);
-                    umma_commit_pair(map_to_cta(l0, 1));
+                    if constexpr (!Cfg::kMix) {
+                        const uint32_t l0 = smem_addr(&lo_free[lo_slot]);
+                        umma_commit_pair(l0);
+                        umma_commit_pair(map_to_cta(l0, 1));
+                        if (++lo_slot == Cfg::kLoStages)
+                            lo_slot = 0;
+                    }
                     if (++stage == S) {
                         stage = 0;
                         phase ^= 1;
                     }
-                    if (++lo_slot == Cfg::kLoStages)
-                        lo_slot = 0;
                     if (kc == Cfg::kChunkKB - 1 || kb == p.k_blocks - 1) {
                         const uint32_t f0 = smem_addr(tfull);
                         umma_commit_pair(f0);
@@ -744,59 +795,117 @@ __global__ void __launch_bounds__(Tc2x3Config<CHUNK_KB>::kThreads, 1)
         __syncwarp();
     } else {
         // ------------------------------------------------------------ split warps (both CTAs)
-        // lo = tf32(x - trunc(x)) of this CTA's raw tiles into its lo ring;
-        // each warp then arrives on CTA 0's ready barrier.  Waits are made
-        // warp-uniform so a timeout leaves the warp together.
-        const int st = threadIdx.x - 32 * (2 + Cfg::kEpiWarps);   // 0..255
-        int stage = 0, lo_slot = 0;
-        uint32_t phase = 0, lo_phase = 0;
-        bool ok = true;
-        constexpr int kVecs = Cfg::kLoadBytes / 16;
-        constexpr int kPer = (kVecs + Cfg::kSplitWarps * 32 - 1) / (Cfg::kSplitWarps * 32);
-        auto lo_of = [](float x) { return isfinite(x) ? round_tf32(x - trunc_tf32(x)) : 0.0f; };
-        for (long long t = cluster; ok && t < p.tiles; t += nclusters) {
-            for (int kb = 0; kb < p.k_blocks; kb++) {
-                if (!__all_sync(0xffffffffu, mbar_wait(&full[stage], phase, abort))) {
-                    if (lane == 0)
+        if constexpr (Cfg::kMix) {
+            // float32 operand -> bf16 hi/mid/lo tiles in the 128-byte-swizzled
+            // layout a bf16 TMA load of it would produce, in place: every
+            // split thread first reads its raw elements, then (named barrier)
+            // the tiles are overwritten.  A failed wait sets the abort flag,
+            // after which every wait returns at once; the loop runs to the
+            // end so that all split threads meet at every barrier.
+            constexpr int kThr = Cfg::kSplitWarps * 32;
+            constexpr int kVecs = Cfg::kMixRawBytes / 16;
+            constexpr int kPer = (kVecs + kThr - 1) / kThr;
+            const int st = threadIdx.x - 32 * (2 + Cfg::kEpiWarps);
+            const bool f_mn = Cfg::kMixA ? p.a_mn_major : p.b_mn_major;
+            int stage = 0;
+            uint32_t phase = 0;
+            for (long long t = cluster; t < p.tiles; t += nclusters) {
+                for (int kb = 0; kb < p.k_blocks; kb++) {
+                    if (!mbar_wait(&full[stage], phase, abort))
                         record_failure(abort, p.status, DEV_TIMEOUT_SPLIT);
-                    ok = false;
-                    break;
-                }
-                const float4 *raw = reinterpret_cast<const float4 *>(smem + stage * Cfg::kLoadBytes);
-                float4 l[kPer];
+                    uint8_t *base = smem + stage * Cfg::kStageBytes;
+                    const float4 *raw = reinterpret_cast<const float4 *>(base);
+                    float4 x[kPer];
 #pragma unroll
-                for (int j = 0; j < kPer; j++) {
-                    const int i = st + j * Cfg::kSplitWarps * 32;
-                    if (kVecs % (Cfg::kSplitWarps * 32) == 0 || i < kVecs) {
-                        const float4 x = raw[i];
-                        l[j] = make_float4(lo_of(x.x), lo_of(x.y), lo_of(x.z), lo_of(x.w));
+                    for (int j = 0; j < kPer; j++) {
+                        const int e = st + j * kThr;
+                        if (kVecs % kThr == 0 || e < kVecs)
+                            x[j] = raw[e];
+                    }
+                    named_barrier_sync(1, kThr);
+#pragma unroll
+                    for (int j = 0; j < kPer; j++) {
+                        const int e = st + j * kThr;
+                        if (kVecs % kThr != 0 && e >= kVecs)
+                            continue;
+                        uint32_t off;
+                        if (!f_mn) {
+                            // raw [128 rows][64 k]: row e / 16, k 4 * (e % 16)
+                            const int r = e >> 4, k4 = e & 15;
+                            off = r * 128 + ((((k4 >> 1) ^ (r & 7))) << 4) + ((k4 & 1) << 3);
+                        } else {
+                            // raw [64 k][128 rows]: k e / 32, rows 4 * (e % 32)
+                            const int k = e >> 5, r4 = e & 31;
+                            off = (r4 >> 4) * Cfg::kChunkBytes + k * 128 +
+                                  ((((r4 & 15) >> 1) ^ (k & 7)) << 4) + ((r4 & 1) << 3);
+                        }
+                        split3_store(x[j], base, off, Cfg::kATile);
+                    }
+                    fence_proxy_async_smem();
+                    __syncwarp();
+                    if (lane == 0)
+                        mbar_arrive_cluster(map_to_cta(smem_addr(&ready[stage]), 0));
+                    if (++stage == S) {
+                        stage = 0;
+                        phase ^= 1;
                     }
                 }
-                if (!__all_sync(0xffffffffu, mbar_wait(&lo_free[lo_slot], lo_phase ^ 1, abort))) {
-                    if (lane == 0)
-                        record_failure(abort, p.status, DEV_TIMEOUT_SPLIT);
-                    ok = false;
-                    break;
-                }
-                float4 *lo = reinterpret_cast<float4 *>(smem + Cfg::kLoOffset +
-                                                        lo_slot * Cfg::kLoadBytes);
+            }
+        } else {
+            // lo = tf32(x - trunc(x)) of this CTA's raw tiles into its lo ring;
+            // each warp then arrives on CTA 0's ready barrier.  Waits are made
+            // warp-uniform so a timeout leaves the warp together.
+            const int st = threadIdx.x - 32 * (2 + Cfg::kEpiWarps);   // 0..255
+            int stage = 0, lo_slot = 0;
+            uint32_t phase = 0, lo_phase = 0;
+            bool ok = true;
+            constexpr int kVecs = Cfg::kLoadBytes / 16;
+            constexpr int kPer = (kVecs + Cfg::kSplitWarps * 32 - 1) / (Cfg::kSplitWarps * 32);
+            auto lo_of = [](float x) { return isfinite(x) ? round_tf32(x - trunc_tf32(x)) : 0.0f; };
+            for (long long t = cluster; ok && t < p.tiles; t += nclusters) {
+                for (int kb = 0; kb < p.k_blocks; kb++) {
+                    if (!__all_sync(0xffffffffu, mbar_wait(&full[stage], phase, abort))) {
+                        if (lane == 0)
+                            record_failure(abort, p.status, DEV_TIMEOUT_SPLIT);
+                        ok = false;
+                        break;
+                    }
+                    const float4 *raw = reinterpret_cast<const float4 *>(smem + stage * Cfg::kStageBytes);
+                    float4 l[kPer];
 #pragma unroll
-                for (int j = 0; j < kPer; j++) {
-                    const int i = st + j * Cfg::kSplitWarps * 32;
-                    if (kVecs % (Cfg::kSplitWarps * 32) == 0 || i < kVecs)
-                        lo[i] = l[j];
-                }
-                fence_proxy_async_smem();
-                __syncwarp();
-                if (lane == 0)
-                    mbar_arrive_cluster(map_to_cta(smem_addr(&ready[stage]), 0));
-                if (++stage == S) {
-                    stage = 0;
-                    phase ^= 1;
-                }
-                if (++lo_slot == Cfg::kLoStages) {
-                    lo_slot = 0;
-                    lo_phase ^= 1;
+                    for (int j = 0; j < kPer; j++) {
+                        const int i = st + j * Cfg::kSplitWarps * 32;
+                        if (kVecs % (Cfg::kSplitWarps * 32) == 0 || i < kVecs) {
+                            const float4 x = raw[i];
+                            l[j] = make_float4(lo_of(x.x), lo_of(x.y), lo_of(x.z), lo_of(x.w));
+                        }
+                    }
+                    if (!__all_sync(0xffffffffu, mbar_wait(&lo_free[lo_slot], lo_phase ^ 1, abort))) {
+                        if (lane == 0)
+                            record_failure(abort, p.status, DEV_TIMEOUT_SPLIT);
+                        ok = false;
+                        break;
+                    }
+                    float4 *lo = reinterpret_cast<float4 *>(smem + Cfg::kLoOffset +
+                                                            lo_slot * Cfg::kLoadBytes);
+#pragma unroll
+                    for (int j = 0; j < kPer; j++) {
+                        const int i = st + j * Cfg::kSplitWarps * 32;
+                        if (kVecs % (Cfg::kSplitWarps * 32) == 0 || i < kVecs)
+                            lo[i] = l[j];
+                    }
+                    fence_proxy_async_smem();
+                    __syncwarp();
+                    if (lane == 0)
+                        mbar_arrive_cluster(map_to_cta(smem_addr(&ready[stage]), 0));
+                    if (++stage == S) {
+                        stage = 0;
+                        phase ^= 1;
+                    }
+                    if (++lo_slot == Cfg::kLoStages) {
+                        lo_slot = 0;
+                        lo_phase ^= 1;
+                    }
                 }
             }
         }

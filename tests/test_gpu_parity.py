@@ -624,6 +624,33 @@ def test_mixed_precision_products(case):
     assert P.device_status() == 0
 
 
+MIXED_PAIR_CASES = [c[:7] for c in MIXED_CASES[:6]] + [
+    ("f32_bf16_ragged_chunks", [1100, 1300], [1300, 2104], False, False, "float32", "bfloat16"),
+    ("bf16_f32_more_tiles_than_clusters", [2560, 520], [520, 2048], True, False, "bfloat16",
+     "float32"),
+]
+
+
+@pytest.mark.parametrize("case", MIXED_PAIR_CASES, ids=[c[0] for c in MIXED_PAIR_CASES])
+def test_mixed_precision_pair(case):
+    """The mixed float32 x bf16 kinds on the 2-CTA bf16x3 kernel: within the
+    float32 bound of the oracle on the exact float32 upcast, bit-identical on
+    repetition."""
+    name, ashape, bshape, at, bt, adt, bdt = case
+    seed = sum(map(ord, name))
+    a = padded(O.seeded(ashape, seed, "normal"), ashape, 0, adt, at)
+    b = padded(O.seeded(bshape, seed + 1, "normal"), bshape, 0, bdt, bt)
+    P.set_kernel_path("tensor-core-pair")
+    c = mixed_product(a, adt, b, bdt)
+    got = P.cuda_get_backend_info()["kernel"]
+    assert got == ("tc2-f32xbf16-bf16x3-256x256" if adt == "float32"
+                   else "tc2-bf16xf32-bf16x3-256x256"), (name, got)
+    first = c.to_numpy()
+    check_fp32(first, as_f32_op(a, adt), as_f32_op(b, bdt), (name, got))
+    assert np.array_equal(mixed_product(a, adt, b, bdt).to_numpy(), first), name
+    assert P.device_status() == 0
+
+
 def _backward(a, b, gc, ga, gb):
     import ctypes
     rc = P.library().pt_tensor_matmul_backward(
