@@ -632,9 +632,12 @@ cudaError_t launch_pair_kernel(DeviceState *ds, int kid, int slot, Kernel kernel
 {
     if (!ensure_smem_attr(ds, kid, kernel, Cfg::kSmemBytes))
         return cudaErrorInvalidConfiguration;
+    // split-K (2-CTA split kernels only): clusters of G pairs, one tile each
+    const int G = p.ksplit > 1 ? p.ksplit : 1;
+    p.ksplit = G;
     cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.x = static_cast<unsigned>(2 * G);
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
     attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -651,19 +654,25 @@ cudaError_t launch_pair_kernel(DeviceState *ds, int kid, int slot, Kernel kernel
         clusters = ds->pair_clusters[slot];
     }
     if (clusters == 0) {
+        // co-resident pairs (the persistent, unsplit launch's grid); a failed
+        // query must not leave its error for the launch check below
+        attr[0].val.clusterDim.x = 2;
         cfg.gridDim = dim3(static_cast<unsigned>(ds->sms & ~1));
-        if (cudaOccupancyMaxActiveClusters(&clusters, kernel, &cfg) != cudaSuccess || clusters < 1)
+        if (cudaOccupancyMaxActiveClusters(&clusters, kernel, &cfg) != cudaSuccess || clusters < 1) {
+            (void)cudaGetLastError();
             clusters = ds->sms / 2;
+        }
+        attr[0].val.clusterDim.x = static_cast<unsigned>(2 * G);
         std::lock_guard<std::mutex> lock(g_mutex);
         ds->pair_clusters[slot] = clusters;
     }
     p.status = ds->status;
-    const long long n = std::min<long long>(p.tiles, clusters);
+    const long long n = G > 1 ? p.tiles * G : std::min<long long>(p.tiles, clusters);
     cfg.gridDim = dim3(static_cast<unsigned>(2 * n));
     const cudaError_t err = cudaLaunchKernelEx(&cfg, kernel, ma, mb, mc, p);
     t_last_grid = static_cast<int>(2 * n);
     t_last_block = Cfg::kThreads;
-    t_last_cluster = 2;
+    t_last_cluster = 2 * G;
     if (err != cudaSuccess)
         return err;
     return cudaGetLastError();
@@ -775,14 +784,29 @@ int try_tc(const Problem &P, DeviceState *ds, cudaStream_t stream, int *kid_out)
     // times (measured on B200), so it is chosen when its rounds of
     // co-resident clusters take less time than the single-CTA kernel's waves
     // (or its split-K launch).
+    // A forced pair launch (path 3) with fewer tiles than a quarter of the
+    // SMs splits K over clusters of G pairs (G in {4, 2}, each pair keeping at
+    // least kSplitMinKBlocks k-blocks).  The automatic choice never takes it:
+    // clusters of 4 or 8 CTAs of 230 KB each need that many free SMs in one
+    // GPC, and on B200 the config-4 dW products ran 153 us split over 8-CTA
+    // clusters against 75 us on the single-CTA split-K kernel.
     const bool mix = mix_side >= 0;
+    int pair_g = 1;
     if ((strict || mix) && P.forced_bn == 0) {
+        const int bk1 = 128 / es;
+        const long long kb1 = static_cast<long long>((P.K + bk1 - 1) / bk1) * P.folds;
+        if (2 * tiles_pair < ds->sms / 2) {
+            for (int g : {4, 2}) {
+                if (2 * tiles_pair * g <= ds->sms && kb1 >= kSplitMinKBlocks * g) {
+                    pair_g = g;
+                    break;
+                }
+            }
+        }
         if (t_path == 3) {
             pair = true;
         } else if (t_path == 0) {
             const long long tiles1 = P.batches * m_blocks * ((P.N + 127) / 128);
-            const int bk1 = 128 / es;
-            const long long kb1 = static_cast<long long>((P.K + bk1 - 1) / bk1) * P.folds;
             double t1 = std::ceil(static_cast<double>(tiles1) / ds->sms);
             if (tiles1 < ds->sms / 2) {
                 for (int g : {4, 2}) {
@@ -794,7 +818,7 @@ int try_tc(const Problem &P, DeviceState *ds, cudaStream_t stream, int *kid_out)
             }
             const double t2 =
                 std::ceil(static_cast<double>(tiles_pair) / (ds->sms / 2)) * kPairTileCost;
-            pair = t2 < t1;
+            pair = pair_g == 1 && t2 < t1;
         }
     }
     if (pair)
@@ -893,6 +917,7 @@ int try_tc(const Problem &P, DeviceState *ds, cudaStream_t stream, int *kid_out)
     p.idesc = make_idesc(fmt, a_mn, b_mn, bn, pair ? 256 : 128);
     p.bias = P.bias;
     p.act = P.act;
+    p.ksplit = pair ? pair_g : 1;
 
     cudaError_t err;
     switch (kid) {

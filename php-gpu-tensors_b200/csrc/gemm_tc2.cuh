@@ -444,6 +444,9 @@ struct Tc2x3Config {
     static constexpr int kChunkKB = CHUNK_KB;            // k-blocks per accumulator chunk
     static constexpr int kTotalCol = BN;
     static constexpr int kTmemCols = 512;
+    // split-K partial tile [128][BN + 4] floats at the start of the ring
+    static constexpr int kPartPitch = BN + 4;
+    static_assert(kRowsCta * kPartPitch * 4 <= kRingBytes, "partial tile fits in the ring");
     static_assert(kSmemBytes <= 232448, "shared memory budget exceeded");
 };
 
@@ -473,9 +476,19 @@ __global__ void __launch_bounds__(Tc2x3Config<KIND, CHUNK_KB>::kThreads, 1)
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
-    const uint32_t rank = cluster_cta_rank();
-    const long long cluster = blockIdx.x >> 1;
-    const long long nclusters = gridDim.x >> 1;
+    // CTA pairs are the cluster ranks (2 q, 2 q + 1).  Split-K (p.ksplit =
+    // G > 1): a cluster of G pairs shares one tile, pair q taking the q-th
+    // contiguous range of k-blocks.
+    const uint32_t crank = cluster_cta_rank();
+    const uint32_t rank = crank & 1u;        // CTA within the pair
+    const uint32_t leader = crank & ~1u;     // the pair's MMA-issuing CTA
+    const int G = p.ksplit;
+    const int krank = G > 1 ? static_cast<int>(crank >> 1) : 0;
+    const long long t_first = G > 1 ? blockIdx.x / (2 * G) : blockIdx.x >> 1;
+    const long long t_step = G > 1 ? p.tiles : gridDim.x >> 1;
+    const int kb_per = (p.k_blocks + G - 1) / G;
+    const int kb_begin = min(p.k_blocks, krank * kb_per);
+    const int kb_end = min(p.k_blocks, kb_begin + kb_per);
 
     if (warp == 0 && lane == 0) {
         prefetch_tensor_map(&tma_a);
@@ -513,7 +526,7 @@ __global__ void __launch_bounds__(Tc2x3Config<KIND, CHUNK_KB>::kThreads, 1)
             uint32_t phase = 0;
             uint32_t issued_mask = 0, parity_mask = 0;
             bool ok = true;
-            for (long long t = cluster; ok && t < p.tiles; t += nclusters) {
+            for (long long t = t_first; ok && t < p.tiles; t += t_step) {
                 const int nb = static_cast<int>(t % p.n_blocks);
                 const long long r = t / p.n_blocks;
                 const int mb = static_cast<int>(r % p.m_blocks);
@@ -524,7 +537,7 @@ __global__ void __launch_bounds__(Tc2x3Config<KIND, CHUNK_KB>::kThreads, 1)
                 operand_coords(c, p.b_slot, p.nbd, cb);
                 const int m0 = mb * Cfg::BM + static_cast<int>(rank) * Cfg::kRowsCta;
                 const int n0 = nb * BN + static_cast<int>(rank) * Cfg::kColsCta;
-                for (int kbf = 0; kbf < p.k_blocks; kbf++) {
+                for (int kbf = kb_begin; kbf < kb_end; kbf++) {
                     int kb = kbf;
                     if (p.nfd > 0) {
                         int f = kbf / p.k_per_fold;
@@ -599,6 +612,7 @@ __global__ void __launch_bounds__(Tc2x3Config<KIND, CHUNK_KB>::kThreads, 1)
     } else if (warp == 1) {
         // ------------------------------------------------------------ MMA issuer (CTA 0)
         if (lane == 0 && rank == 0) {
+            const uint32_t peer = leader + 1;
             int stage = 0, lo_slot = 0;
             uint32_t phase = 0;
             long long uses = 0;   // accumulator chunks issued
@@ -610,9 +624,9 @@ __global__ void __launch_bounds__(Tc2x3Config<KIND, CHUNK_KB>::kThreads, 1)
             const uint32_t b_sbo = p.b_mn_major ? Cfg::kMnSbo : Cfg::kKSbo;
             const uint32_t a_lay = p.a_mn_major ? Cfg::kMnLayout : Cfg::kKLayout;
             const uint32_t b_lay = p.b_mn_major ? Cfg::kMnLayout : Cfg::kKLayout;
-            for (long long t = cluster; ok && t < p.tiles; t += nclusters) {
-                for (int kb = 0; kb < p.k_blocks; kb++) {
-                    const int kc = kb % Cfg::kChunkKB;
+            for (long long t = t_first; ok && t < p.tiles; t += t_step) {
+                for (int kb = kb_begin; kb < kb_end; kb++) {
+                    const int kc = (kb - kb_begin) % Cfg::kChunkKB;
                     if (kc == 0) {
                         if (!mbar_wait_cluster(tempty, static_cast<uint32_t>(uses & 1) ^ 1u, abort)) {
                             record_failure(abort, p.status, DEV_TIMEOUT_MMA);
@@ -667,11 +681,11 @@ __global__ void __launch_bounds__(Tc2x3Config<KIND, CHUNK_KB>::kThreads, 1)
                     }
                     const uint32_t e0 = smem_addr(&empty[stage]);
                     umma_commit_pair(e0);
-                    umma_commit_pair(map_to_cta(e0, 1));
+                    umma_commit_pair(map_to_cta(e0, peer));
                     if constexpr (!Cfg::kMix) {
                         const uint32_t l0 = smem_addr(&lo_free[lo_slot]);
                         umma_commit_pair(l0);
-                        umma_commit_pair(map_to_cta(l0, 1));
+                        umma_commit_pair(map_to_cta(l0, peer));
                         if (++lo_slot == Cfg::kLoStages)
                             lo_slot = 0;
                     }
@@ -679,10 +693,10 @@ __global__ void __launch_bounds__(Tc2x3Config<KIND, CHUNK_KB>::kThreads, 1)
                         stage = 0;
                         phase ^= 1;
                     }
-                    if (kc == Cfg::kChunkKB - 1 || kb == p.k_blocks - 1) {
+                    if (kc == Cfg::kChunkKB - 1 || kb == kb_end - 1) {
                         const uint32_t f0 = smem_addr(tfull);
                         umma_commit_pair(f0);
-                        umma_commit_pair(map_to_cta(f0, 1));
+                        umma_commit_pair(map_to_cta(f0, peer));
                         uses++;
                     }
                 }
@@ -698,7 +712,7 @@ __global__ void __launch_bounds__(Tc2x3Config<KIND, CHUNK_KB>::kThreads, 1)
         constexpr int kGroups = BN / 32 / Cfg::kEpiParts;   // 32-column groups per warp
         const int g0 = (ew >> 2) * kGroups;
         uint8_t *stage_buf = smem + Cfg::kEpiOffset + ew * Cfg::kEpiBufs * Cfg::kEpiBufBytes;
-        const uint32_t tempty0 = map_to_cta(smem_addr(tempty), 0);
+        const uint32_t tempty0 = map_to_cta(smem_addr(tempty), leader);
         int buf = 0;
         long long uses = 0;
         bool ok = true;
@@ -731,10 +745,14 @@ __global__ void __launch_bounds__(Tc2x3Config<KIND, CHUNK_KB>::kThreads, 1)
             }
             buf ^= Cfg::kEpiBufs - 1;
         };
-        const int nchunks = (p.k_blocks + Cfg::kChunkKB - 1) / Cfg::kChunkKB;
+        const int nchunks = (kb_end - kb_begin + Cfg::kChunkKB - 1) / Cfg::kChunkKB;
         const uint32_t lane_base = tmem_base + (static_cast<uint32_t>(quad * 32) << 16);
         const uint32_t t_total = lane_base + static_cast<uint32_t>(Cfg::kTotalCol);
-        for (long long t = cluster; ok && t < p.tiles; t += nclusters) {
+        // split-K: this thread's row of the partial tile in the ring
+        float *part_row = reinterpret_cast<float *>(smem) + (quad * 32 + lane) * Cfg::kPartPitch;
+        int c_last[3] = {0, 0, 0};
+        int n0_last = 0, row0_last = 0;
+        for (long long t = t_first; ok && t < p.tiles; t += t_step) {
             const int nb = static_cast<int>(t % p.n_blocks);
             const long long r = t / p.n_blocks;
             const int mb = static_cast<int>(r % p.m_blocks);
@@ -743,6 +761,11 @@ __global__ void __launch_bounds__(Tc2x3Config<KIND, CHUNK_KB>::kThreads, 1)
             decode_batch(batch, p, c);
             const int row0 = mb * Cfg::BM + static_cast<int>(rank) * Cfg::kRowsCta + quad * 32;
             const int n0 = nb * BN;
+            c_last[0] = c[0];
+            c_last[1] = c[1];
+            c_last[2] = c[2];
+            n0_last = n0;
+            row0_last = row0;
             for (int ck = 0; ck < nchunks; ck++, uses++) {
                 const bool got = __all_sync(
                     0xffffffffu, mbar_wait(tfull, static_cast<uint32_t>(uses & 1), abort));
@@ -778,7 +801,14 @@ __global__ void __launch_bounds__(Tc2x3Config<KIND, CHUNK_KB>::kThreads, 1)
                             if (lane == 0)
                                 mbar_arrive_cluster(tempty0);
                         }
-                        emit(v, n0 + h * 32, row0, c);
+                        if (G > 1) {
+#pragma unroll
+                            for (int i = 0; i < 8; i++)
+                                *reinterpret_cast<float4 *>(part_row + h * 32 + 4 * i) =
+                                    make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+                        } else {
+                            emit(v, n0 + h * 32, row0, c);
+                        }
                     }
                 }
                 if (!last) {
@@ -789,6 +819,39 @@ __global__ void __launch_bounds__(Tc2x3Config<KIND, CHUNK_KB>::kThreads, 1)
                         mbar_arrive_cluster(tempty0);
                 }
             }
+        }
+        if (G > 1) {
+            // Every CTA's partial block is in its ring; CTA (q, c) of the
+            // cluster finishes columns [q * BN / G, (q + 1) * BN / G) of its
+            // 128 rows, adding the G partials of CTAs (0, c) .. (G - 1, c) in
+            // that order over DSMEM.  The two warps of a lane quadrant share
+            // the slice.
+            cluster_sync();
+            if (ok && t_first < p.tiles) {
+                const uint32_t row_s = smem_addr(part_row);
+                const int cols = BN / G, col_lo = krank * cols;
+                for (int h = col_lo / 32 + (ew >> 2); h < (col_lo + cols) / 32; h += Cfg::kEpiParts) {
+                    float v[32];
+#pragma unroll
+                    for (int i = 0; i < 8; i++) {
+                        const uint32_t off = static_cast<uint32_t>((h * 32 + 4 * i) * 4);
+                        float4 acc4 = ld_cluster_f4(map_to_cta(row_s + off, rank));
+                        for (int q = 1; q < G; q++) {
+                            const float4 x = ld_cluster_f4(map_to_cta(row_s + off, 2 * q + rank));
+                            acc4.x += x.x;
+                            acc4.y += x.y;
+                            acc4.z += x.z;
+                            acc4.w += x.w;
+                        }
+                        v[4 * i] = acc4.x;
+                        v[4 * i + 1] = acc4.y;
+                        v[4 * i + 2] = acc4.z;
+                        v[4 * i + 3] = acc4.w;
+                    }
+                    emit(v, n0_last + h * 32, row0_last, c_last);
+                }
+            }
+            cluster_sync();   // peers are done reading this CTA's partial block
         }
         if (lane == 0)
             bulk_wait_group<0>();
@@ -809,8 +872,8 @@ __global__ void __launch_bounds__(Tc2x3Config<KIND, CHUNK_KB>::kThreads, 1)
             const bool f_mn = Cfg::kMixA ? p.a_mn_major : p.b_mn_major;
             int stage = 0;
             uint32_t phase = 0;
-            for (long long t = cluster; t < p.tiles; t += nclusters) {
-                for (int kb = 0; kb < p.k_blocks; kb++) {
+            for (long long t = t_first; t < p.tiles; t += t_step) {
+                for (int kb = kb_begin; kb < kb_end; kb++) {
                     if (!mbar_wait(&full[stage], phase, abort))
                         record_failure(abort, p.status, DEV_TIMEOUT_SPLIT);
                     uint8_t *base = smem + stage * Cfg::kStageBytes;
@@ -844,7 +907,7 @@ __global__ void __launch_bounds__(Tc2x3Config<KIND, CHUNK_KB>::kThreads, 1)
                     fence_proxy_async_smem();
                     __syncwarp();
                     if (lane == 0)
-                        mbar_arrive_cluster(map_to_cta(smem_addr(&ready[stage]), 0));
+                        mbar_arrive_cluster(map_to_cta(smem_addr(&ready[stage]), leader));
                     if (++stage == S) {
                         stage = 0;
                         phase ^= 1;
@@ -862,8 +925,8 @@ __global__ void __launch_bounds__(Tc2x3Config<KIND, CHUNK_KB>::kThreads, 1)
             constexpr int kVecs = Cfg::kLoadBytes / 16;
             constexpr int kPer = (kVecs + Cfg::kSplitWarps * 32 - 1) / (Cfg::kSplitWarps * 32);
             auto lo_of = [](float x) { return isfinite(x) ? round_tf32(x - trunc_tf32(x)) : 0.0f; };
-            for (long long t = cluster; ok && t < p.tiles; t += nclusters) {
-                for (int kb = 0; kb < p.k_blocks; kb++) {
+            for (long long t = t_first; ok && t < p.tiles; t += t_step) {
+                for (int kb = kb_begin; kb < kb_end; kb++) {
                     if (!__all_sync(0xffffffffu, mbar_wait(&full[stage], phase, abort))) {
                         if (lane == 0)
                             record_failure(abort, p.status, DEV_TIMEOUT_SPLIT);
@@ -897,7 +960,7 @@ __global__ void __launch_bounds__(Tc2x3Config<KIND, CHUNK_KB>::kThreads, 1)
                     fence_proxy_async_smem();
                     __syncwarp();
                     if (lane == 0)
-                        mbar_arrive_cluster(map_to_cta(smem_addr(&ready[stage]), 0));
+                        mbar_arrive_cluster(map_to_cta(smem_addr(&ready[stage]), leader));
                     if (++stage == S) {
                         stage = 0;
                         phase ^= 1;
@@ -911,6 +974,11 @@ __global__ void __launch_bounds__(Tc2x3Config<KIND, CHUNK_KB>::kThreads, 1)
         }
     }
 
+    if (G > 1 && !(warp >= 2 && warp < 2 + Cfg::kEpiWarps)) {
+        // the epilogue warps' two split-K cluster barriers
+        cluster_sync();
+        cluster_sync();
+    }
     tc_fence_before();
     __syncthreads();
     cluster_sync();

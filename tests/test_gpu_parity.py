@@ -367,9 +367,9 @@ PAIR_3X_CASES = [
     # K chunks, every operand layout, batches with broadcast
     ("more_tiles_than_clusters", [2048, 256], [256, 2560], False, False),
     ("ragged_chunks", [600, 520], [520, 700], False, False),
-    ("a_transposed", [520, 1000], [1000, 300], True, False),
+    ("a_transposed", [2048, 1000], [1000, 2048], True, False),
     ("b_transposed", [300, 392], [392, 520], False, True),
-    ("both_transposed", [264, 200], [200, 264], True, True),
+    ("both_transposed", [2048, 200], [200, 2048], True, True),
     ("batched_broadcast", [3, 1, 260, 136], [2, 136, 264], False, False),
 ]
 
@@ -386,7 +386,8 @@ def test_pair_3xtf32(case):
     ad, bd = to_device(a, "float32"), to_device(b, "float32")
     c = ad.matmul(bd)
     assert P.cuda_get_backend_info()["kernel"] == "tc2-3xtf32-256x256", name
-    assert P.last_launch()[2] == 2
+    # few tiles split K over clusters of 2 or 4 pairs, 64 tiles and more do not
+    assert P.last_launch()[2] in (2, 4, 8)
     first = c.to_numpy()
     check_fp32(first, a, b, name)
     for _ in range(2):
@@ -417,6 +418,41 @@ def test_pair_tf32_mode(case):
     K = a[1][-1]
     bound = (2.0 ** -9 + K * 2.0 ** -23) * absp
     assert np.all(np.abs(first - c64) <= bound + 1e-30), name
+    assert P.device_status() == 0
+
+
+PAIR_SPLIT_CASES = [
+    # (name, a_shape, b_shape, a_transposed, b_transposed, a dtype, b dtype,
+    # expected cluster size = 2 x pairs splitting K)
+    ("f32_dw_g4", [1024, 4096], [4096, 1024], True, False, "float32", "float32", 8),
+    ("f32_ragged_g4", [300, 3000], [3000, 264], False, True, "float32", "float32", 8),
+    ("f32_g2", [1280, 1024], [1024, 1536], False, False, "float32", "float32", 4),
+    ("bf16xf32_dw_g4", [784, 4096], [4096, 1024], True, False, "bfloat16", "float32", 8),
+    ("f32xbf16_g2", [1280, 1024], [1024, 1536], False, True, "float32", "bfloat16", 4),
+]
+
+
+@pytest.mark.parametrize("case", PAIR_SPLIT_CASES, ids=[c[0] for c in PAIR_SPLIT_CASES])
+def test_pair_split_k(case):
+    """Split-K on the 2-CTA split kernels: clusters of G pairs share a tile,
+    the partial blocks are added over DSMEM in a fixed order -- within the
+    float32 bound of the oracle and bit-identical from call to call."""
+    name, ashape, bshape, at, bt, adt, bdt, cluster = case
+    seed = sum(map(ord, name))
+    a = padded(O.seeded(ashape, seed, "normal"), ashape, 0, adt, at)
+    b = padded(O.seeded(bshape, seed + 1, "normal"), bshape, 0, bdt, bt)
+    P.set_kernel_path("tensor-core-pair")
+    if adt == bdt:
+        ad, bd = to_device(a, adt), to_device(b, bdt)
+        run = lambda: ad.matmul(bd).to_numpy()
+    else:
+        run = lambda: mixed_product(a, adt, b, bdt).to_numpy()
+    first = run()
+    what = (name, P.cuda_get_backend_info()["kernel"], P.last_launch())
+    assert what[1].startswith("tc2-") and what[2][2] == cluster, what
+    check_fp32(first, as_f32_op(a, adt), as_f32_op(b, bdt), what)
+    for _ in range(2):
+        assert np.array_equal(run(), first), name
     assert P.device_status() == 0
 
 
