@@ -84,9 +84,11 @@ void pt_tensor_release(pt_tensor *t, cudaStream_t stream);
  * shape of its product, or the shape of its operand when the product
  * broadcast that operand (src/autograd.c:714-760, gradient_unbroadcast):
  * the sum over the broadcast axes is then fused -- one GEMM over the folded
- * (batch..., inner) axis when the tensors' strides allow it, otherwise a
- * scratch product and a fixed-order reduction.  Either result may be NULL to
- * skip that GEMM. */
+ * (batch..., inner) axis when the tensors' strides allow it, otherwise the
+ * summed axes are walked inside the product kernel.  Either result may be
+ * NULL to skip that GEMM.  With both requested, grad_b runs on a side stream
+ * forked from `stream` and joined back into it with events (capture-safe);
+ * on return every launch is ordered on `stream`. */
 int pt_tensor_matmul_backward(const pt_tensor *a, const pt_tensor *b, const pt_tensor *grad_c,
                               const pt_tensor *grad_a, const pt_tensor *grad_b,
                               cudaStream_t stream);

@@ -317,6 +317,61 @@ int gradient_product(const pt_tensor *x, const pt_tensor *y, const pt_tensor *ou
 
 } // namespace
 
+namespace {
+
+// The autograd node's side stream and fork/join events, per host thread and
+// device (created on first use, kept for the thread's lifetime).
+struct BackwardStreams {
+    cudaStream_t side = nullptr;
+    cudaEvent_t fork = nullptr, join = nullptr;
+};
+constexpr int kMaxBackwardDevices = 64;
+thread_local BackwardStreams t_backward[kMaxBackwardDevices];
+thread_local cudaStream_t t_backward_side = nullptr;
+thread_local cudaEvent_t t_backward_join = nullptr;
+
+// Forks a side stream off `stream`: returns it with the fork recorded, or
+// null when the stream or events cannot be made (the caller then runs both
+// products on `stream`).
+cudaStream_t backward_side_stream(cudaStream_t stream)
+{
+    int dev = -1;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxBackwardDevices)
+        return nullptr;
+    BackwardStreams &b = t_backward[dev];
+    if (!b.side) {
+        if (cudaStreamCreateWithFlags(&b.side, cudaStreamNonBlocking) != cudaSuccess ||
+            cudaEventCreateWithFlags(&b.fork, cudaEventDisableTiming) != cudaSuccess ||
+            cudaEventCreateWithFlags(&b.join, cudaEventDisableTiming) != cudaSuccess) {
+            (void)cudaGetLastError();
+            if (b.side) cudaStreamDestroy(b.side);
+            if (b.fork) cudaEventDestroy(b.fork);
+            if (b.join) cudaEventDestroy(b.join);
+            b = BackwardStreams();
+            return nullptr;
+        }
+    }
+    if (cudaEventRecord(b.fork, stream) != cudaSuccess ||
+        cudaStreamWaitEvent(b.side, b.fork, 0) != cudaSuccess) {
+        (void)cudaGetLastError();
+        return nullptr;
+    }
+    t_backward_side = b.side;
+    t_backward_join = b.join;
+    return b.side;
+}
+
+// Joins the side stream back into `stream`.
+int backward_join(cudaStream_t stream)
+{
+    if (cudaEventRecord(t_backward_join, t_backward_side) != cudaSuccess ||
+        cudaStreamWaitEvent(stream, t_backward_join, 0) != cudaSuccess)
+        return fail(PT_RUNTIME, "could not join the backward side stream");
+    return PT_OK;
+}
+
+} // namespace
+
 PT_API int pt_tensor_matmul_backward(const pt_tensor *a, const pt_tensor *b,
                                      const pt_tensor *grad_c, const pt_tensor *grad_a,
                                      const pt_tensor *grad_b, cudaStream_t stream)
@@ -331,14 +386,29 @@ PT_API int pt_tensor_matmul_backward(const pt_tensor *a, const pt_tensor *b,
                     "float32 or same-typed upstream gradient");
     if (a->ndims < 2 || b->ndims < 2)
         return fail(PT_INVALID_ARGUMENT, "Autograd matmul requires operands with rank at least 2");
+    const pt_tensor bt = transposed_view(b);
+    const pt_tensor at = transposed_view(a);
+    // Both gradients: dB runs on a side stream forked from and joined back
+    // into the caller's stream (events, so graph capture records the fork
+    // and join), letting the two products' launch tails, and small products
+    // such as a classifier layer's, overlap.
+    cudaStream_t side = grad_a && grad_b ? backward_side_stream(stream) : nullptr;
+    if (side) {
+        const int s1 = gradient_product(grad_c, &bt, grad_a, stream);
+        const int s2 = s1 == PT_OK ? gradient_product(&at, grad_c, grad_b, side) : s1;
+        const int sj = backward_join(stream);
+        if (s1 != PT_OK)
+            return s1;
+        if (s2 != PT_OK)
+            return s2;
+        return sj;
+    }
     if (grad_a) {
-        const pt_tensor bt = transposed_view(b);
         const int s = gradient_product(grad_c, &bt, grad_a, stream);
         if (s != PT_OK)
             return s;
     }
     if (grad_b) {
-        const pt_tensor at = transposed_view(a);
         const int s = gradient_product(&at, grad_c, grad_b, stream);
         if (s != PT_OK)
             return s;

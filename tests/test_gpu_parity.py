@@ -696,6 +696,36 @@ def _backward(a, b, gc, ga, gb):
     assert rc == P.PT_OK, P.library().pt_last_error()
 
 
+def test_backward_under_graph_capture():
+    """Both gradients run on a side stream forked from the caller's stream and
+    joined back; a CUDA graph captures the fork and join and its replay
+    equals the eager result."""
+    ashape, bshape = [3, 200, 136], [136, 264]
+    a = O.dense(O.to_storage(O.seeded(ashape, 91, "normal"), "bfloat16"), ashape)
+    b = O.dense(O.to_storage(O.seeded(bshape, 92, "normal"), "bfloat16"), bshape)
+    g = O.dense(O.seeded([3, 200, 264], 93, "normal"), [3, 200, 264])
+    ad, bd, gd = to_device(a, "bfloat16"), to_device(b, "bfloat16"), to_device(g, "float32")
+    ga0, gb0 = P.CudaArray.zeros(ashape), P.CudaArray.zeros(bshape)
+    _backward(ad, bd, gd, ga0, gb0)
+    ga, gb = P.CudaArray.zeros(ashape), P.CudaArray.zeros(bshape)
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        _backward(ad, bd, gd, ga, gb)
+    torch.cuda.current_stream().wait_stream(s)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        _backward(ad, bd, gd, ga, gb)
+    ga.to_torch().zero_()
+    gb.to_torch().zero_()
+    graph.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(ga.to_torch(), ga0.to_torch())
+    assert torch.equal(gb.to_torch(), gb0.to_torch())
+    del graph
+    assert P.device_status() == 0
+
+
 @pytest.mark.parametrize("dt,gdt", [("bfloat16", "float32"), ("bfloat16", "bfloat16"),
                                     ("float16", "float32")])
 def test_backward_low_precision_operands(dt, gdt):
