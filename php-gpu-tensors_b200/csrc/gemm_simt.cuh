@@ -114,6 +114,10 @@ __global__ void __launch_bounds__(256) simt_gemm_kernel(const SimtParams p)
     __shared__ Acc sa[kSimtBK][kSimtTile + 1];
     __shared__ Acc sb[kSimtBK][kSimtTile + 1];
 
+    // programmatic dependent launch: nothing global is touched before the
+    // previous kernel in the stream has completed
+    grid_dependency_wait();
+    grid_launch_dependents();
     const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
     const int n0 = blockIdx.x * kSimtTile;
     const int m_blocks = (p.M + kSimtTile - 1) / kSimtTile;

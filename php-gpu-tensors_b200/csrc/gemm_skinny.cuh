@@ -111,6 +111,10 @@ __global__ void __launch_bounds__(kSkinnyThreads) skinny_gemm_kernel(const SimtP
     __shared__ __align__(16) Acc sB[2][kSkinnyKC][NB];
     __shared__ __align__(16) Acc red[S::kKGroups][kSkinnyBM][NB];
 
+    // programmatic dependent launch: nothing global is touched before the
+    // previous kernel in the stream has completed
+    grid_dependency_wait();
+    grid_launch_dependents();
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int cg = warp % S::kColGroups, kg = warp / S::kColGroups;
     const int C = sa.cluster;
@@ -292,6 +296,8 @@ __global__ void __launch_bounds__(kSkinnyThreads) skinny_async_kernel(const Simt
     T *ringA = reinterpret_cast<T *>(skinny_smem);
     T *ringB = ringA + kStages * R::kAStage;
     T *red = ringA;   // after the main loop
+    grid_dependency_wait();   // programmatic dependent launch, as above
+    grid_launch_dependents();
 
     const T *A = static_cast<const T *>(p.a);
     const T *B = static_cast<const T *>(p.b);

@@ -1029,8 +1029,18 @@ cudaError_t launch_simt(const Problem &P, cudaStream_t stream)
     dim3 grid(static_cast<unsigned>(std::min<long long>(nb, 2147483647ll)),
               static_cast<unsigned>(std::min<long long>(mb, 65535)),
               static_cast<unsigned>(std::min<long long>(P.batches, 65535)));
-    simt_gemm_kernel<T, TA, TB><<<grid, 256, 0, stream>>>(s);
-    return cudaGetLastError();
+    cudaLaunchConfig_t cfg;
+    std::memset(&cfg, 0, sizeof(cfg));
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(256, 1, 1);
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    const cudaError_t err = cudaLaunchKernelEx(&cfg, simt_gemm_kernel<T, TA, TB>, s);
+    return err != cudaSuccess ? err : cudaGetLastError();
 }
 
 // Few-column products (N <= 32) on the split-K CUDA-core kernel.  The
@@ -1057,13 +1067,15 @@ cudaError_t launch_skinny_nb(const Problem &P, DeviceState *ds, cudaStream_t str
     cfg.gridDim = dim3(static_cast<unsigned>(xc * C), 1, static_cast<unsigned>(zb));
     cfg.blockDim = dim3(kSkinnyThreads, 1, 1);
     cfg.stream = stream;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = static_cast<unsigned>(C);
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = static_cast<unsigned>(C);
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = C > 1 ? 1 : 0;
+    cfg.numAttrs = C > 1 ? 2 : 1;
     cudaError_t err;
     if constexpr (sizeof(T) >= 4 && std::is_same<T, TA>::value && std::is_same<T, TB>::value) {
         // float32 / float64: the cp.async ring variant
