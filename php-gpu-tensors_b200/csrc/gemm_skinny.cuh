@@ -258,12 +258,20 @@ __device__ __forceinline__ void skinny_wait() { asm volatile("cp.async.wait_grou
 // float32 / float64 variant: eight k groups (one per warp), lane = row, every
 // thread accumulating all NB columns of its row, so each k costs a warp one
 // conflict-free A read and NB/4 broadcast B reads for NB FMAs.
-template <typename T, int NB>
+// AVEC (float32 only): A lands in 16-byte copies of four elements instead of
+// one 4-byte copy per element, so a chunk costs each thread one copy instead
+// of four.  An M-contiguous A keeps the [k][row] layout with the row pitch
+// padded to 36 floats (16-byte aligned groups of four rows); a K-contiguous
+// A is stored [row][k] with the 16-byte k-quads of row r at quad q ^ (r % 8),
+// so each warp reads its k-quad as one float4 per lane without bank
+// conflicts.
+template <typename T, int NB, bool AVEC = false>
 struct SkinnyRing {
     static constexpr int kStages = sizeof(T) == 4 ? 8 : 4;
     static constexpr int kKGroups = 8;
     static constexpr int kKPerGroup = kSkinnyKC / kKGroups;
-    static constexpr int kAPitch = kSkinnyBM + 1;
+    static constexpr int kAPitch = AVEC ? 36 : kSkinnyBM + 1;
+    static_assert(!AVEC || (sizeof(T) == 4 && kKPerGroup == 4), "float32 k-quads");
     static constexpr int kAStage = kSkinnyKC * kAPitch;
     static constexpr int kBStage = kSkinnyKC * NB;
     static constexpr int kAPerThread = kSkinnyBM * kSkinnyKC / kSkinnyThreads;   // 4
@@ -277,20 +285,26 @@ struct SkinnyRing {
         (kRingElems > kRedElems ? kRingElems : kRedElems) * static_cast<int>(sizeof(T));
 };
 
-template <typename T, int NB>
+template <typename T, int NB, bool AVEC = false>
 constexpr int skinny_async_smem_bytes()
 {
-    return SkinnyRing<T, NB>::kSmemBytes;
+    return SkinnyRing<T, NB, AVEC>::kSmemBytes;
+}
+
+__device__ __forceinline__ void cp_async_16(uint32_t d, const void *src, int bytes)
+{
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(d), "l"(src), "r"(bytes)
+                 : "memory");
 }
 
 // AKM: A is K-contiguous (loads walk k across the lanes) rather than
 // M-contiguous or strided (loads walk m).
-template <typename T, int NB, bool AKM>
+template <typename T, int NB, bool AKM, bool AVEC = false>
 __global__ void __launch_bounds__(kSkinnyThreads) skinny_async_kernel(const SimtParams p,
                                                                        const SkinnyArgs sa)
 {
     using E = Elem<T>;
-    using R = SkinnyRing<T, NB>;
+    using R = SkinnyRing<T, NB, AVEC>;
     constexpr int kStages = R::kStages;
     extern __shared__ __align__(16) unsigned char skinny_smem[];
     T *ringA = reinterpret_cast<T *>(skinny_smem);
@@ -326,6 +340,13 @@ __global__ void __launch_bounds__(kSkinnyThreads) skinny_async_kernel(const Simt
         a_kk[i] = AKM ? e % kSkinnyKC : e / kSkinnyBM;
         a_dst[i] = static_cast<uint32_t>((a_kk[i] * R::kAPitch + row) * sizeof(T));
     }
+    // AVEC: this thread's one 16-byte slot (four rows at one k, or one row's
+    // k-quad) and its byte offset inside a ring stage
+    const int v_a = threadIdx.x >> 3, v_b = threadIdx.x & 7;   // 32 x 8 slots
+    const int v_row = AKM ? v_a : 4 * v_b;                     // first row of the slot
+    const int v_k = AKM ? 4 * v_b : v_a;                       // first k of the slot
+    const uint32_t v_dst = static_cast<uint32_t>(
+        (AKM ? v_a * kSkinnyKC + ((v_b ^ (v_a & 7)) << 2) : v_a * R::kAPitch + 4 * v_b) * 4);
 #pragma unroll
     for (int i = 0; i < R::kBPerThread; i++) {
         const int e = threadIdx.x + kSkinnyThreads * i;
@@ -364,6 +385,12 @@ __global__ void __launch_bounds__(kSkinnyThreads) skinny_async_kernel(const Simt
             pa[i] = A + oa + static_cast<long long>(va[i] ? m : 0) * p.a_sm +
                     static_cast<long long>(kfirst + a_kk[i]) * p.a_sk;
         }
+        // AVEC: the slot's source and how many of its four elements exist
+        // (rows past M, or k past K in the last chunk, are zero-filled)
+        const int v_rows = AKM ? (m0 + v_row < p.M ? 1 : 0) : max(0, min(4, p.M - (m0 + v_row)));
+        const T *pav = v_rows ? A + oa + static_cast<long long>(m0 + v_row) * p.a_sm +
+                                    static_cast<long long>(kfirst + v_k) * p.a_sk
+                              : A;
         const T *pb[R::kBPerThread];
         bool vb[R::kBPerThread];
 #pragma unroll
@@ -379,9 +406,16 @@ __global__ void __launch_bounds__(kSkinnyThreads) skinny_async_kernel(const Simt
                 const uint32_t slot = static_cast<uint32_t>(j % kStages);
                 const uint32_t sA = ringA_s + slot * (R::kAStage * sizeof(T));
                 const uint32_t sB = ringB_s + slot * (R::kBStage * sizeof(T));
+                if constexpr (AVEC) {
+                    // bytes that exist: a row's k-quad cut at K, or four
+                    // rows cut at M
+                    const int n = AKM ? (v_rows ? 4 * min(4, max(0, p.K - (k0 + v_k))) : 0)
+                                      : (k0 + v_k < p.K ? 4 * v_rows : 0);
+                    cp_async_16(sA + v_dst, n ? pav : A, n);
+                }
                 if (k0 + kSkinnyKC <= p.K) {
 #pragma unroll
-                    for (int i = 0; i < R::kAPerThread; i++)
+                    for (int i = 0; i < (AVEC ? 0 : R::kAPerThread); i++)
                         cp_async_elem(sA + a_dst[i], va[i] ? pa[i] : A, va[i]);
 #pragma unroll
                     for (int i = 0; i < R::kBPerThread; i++)
@@ -389,7 +423,7 @@ __global__ void __launch_bounds__(kSkinnyThreads) skinny_async_kernel(const Simt
                             cp_async_elem(sB + b_dst[i], vb[i] ? pb[i] : B, vb[i]);
                 } else {   // the last chunk of K
 #pragma unroll
-                    for (int i = 0; i < R::kAPerThread; i++) {
+                    for (int i = 0; i < (AVEC ? 0 : R::kAPerThread); i++) {
                         const bool ok = va[i] && k0 + a_kk[i] < p.K;
                         cp_async_elem(sA + a_dst[i], ok ? pa[i] : A, ok);
                     }
@@ -404,6 +438,8 @@ __global__ void __launch_bounds__(kSkinnyThreads) skinny_async_kernel(const Simt
 #pragma unroll
                 for (int i = 0; i < R::kAPerThread; i++)
                     pa[i] += stepA;
+                if (v_rows)
+                    pav += stepA;
 #pragma unroll
                 for (int i = 0; i < R::kBPerThread; i++)
                     pb[i] += stepB;
@@ -428,9 +464,19 @@ __global__ void __launch_bounds__(kSkinnyThreads) skinny_async_kernel(const Simt
             const T *sB = ringB + (j % kStages) * R::kBStage;
             const T *wA = sA + warp * R::kKPerGroup * R::kAPitch + lane;
             const T *wB = sB + warp * R::kKPerGroup * NB;
+            T a4[R::kKPerGroup];
+            if constexpr (AVEC && AKM) {
+                // this lane's row, the warp's k-quad
+                const float4 v = *reinterpret_cast<const float4 *>(
+                    sA + lane * kSkinnyKC + ((warp ^ (lane & 7)) << 2));
+                a4[0] = v.x;
+                a4[1] = v.y;
+                a4[2] = v.z;
+                a4[3] = v.w;
+            }
 #pragma unroll
             for (int q = 0; q < R::kKPerGroup; q++) {
-                const T a = wA[q * R::kAPitch];
+                const T a = AVEC && AKM ? a4[q] : wA[q * R::kAPitch];
 #pragma unroll
                 for (int n4 = 0; n4 < NB; n4 += 4) {
                     T b[4];

@@ -536,6 +536,7 @@ enum KernelId : int {
     KID_MIX_B,               // bf16 A x float32 B -> float32
     KID_BF16_F32,            // bf16 x bf16 -> float32
     KID_F16_F32,             // f16 x f16 -> float32
+    KID_SKINNY_VEC,          // 12 ids: float32 few-column kernel with 16-byte A copies, 2 * NB index + A k-major
 };
 
 const char *kernel_name(int kid)
@@ -1077,6 +1078,32 @@ cudaError_t launch_skinny_nb(const Problem &P, DeviceState *ds, cudaStream_t str
     cfg.attrs = attr;
     cfg.numAttrs = C > 1 ? 2 : 1;
     cudaError_t err;
+    // float32 A in 16-byte copies: 16-byte aligned base, the non-contiguous
+    // axes (the other matrix axis and the batch axes) in multiples of four
+    bool a_vec = sizeof(T) == 4 && aligned16(P.a) &&
+                 (sa.a_k_major ? (P.a_sm % 4 == 0 || P.M == 1) : (P.a_sm == 1 && P.a_sk % 4 == 0));
+    for (int d = 0; d < P.nbd; d++)
+        a_vec = a_vec && P.a_bs[d] % 4 == 0;
+    if constexpr (sizeof(T) == 4 && std::is_same<T, TA>::value && std::is_same<T, TB>::value) {
+        if (a_vec) {
+            constexpr int smem = skinny_async_smem_bytes<T, NB, true>();
+            const int base = KID_SKINNY_VEC + 2 * (NB <= 16 ? NB / 4 - 1 : NB == 24 ? 4 : 5);
+            cfg.dynamicSmemBytes = smem;
+            if (sa.a_k_major) {
+                if (!ensure_smem_attr(ds, base + 1, skinny_async_kernel<T, NB, true, true>, smem))
+                    return cudaErrorInvalidConfiguration;
+                err = cudaLaunchKernelEx(&cfg, skinny_async_kernel<T, NB, true, true>, s, sa);
+            } else {
+                if (!ensure_smem_attr(ds, base, skinny_async_kernel<T, NB, false, true>, smem))
+                    return cudaErrorInvalidConfiguration;
+                err = cudaLaunchKernelEx(&cfg, skinny_async_kernel<T, NB, false, true>, s, sa);
+            }
+            t_last_grid = static_cast<int>(xc * C);
+            t_last_block = kSkinnyThreads;
+            t_last_cluster = C;
+            return err != cudaSuccess ? err : cudaGetLastError();
+        }
+    }
     if constexpr (sizeof(T) >= 4 && std::is_same<T, TA>::value && std::is_same<T, TB>::value) {
         // float32 / float64: the cp.async ring variant
         constexpr int smem = skinny_async_smem_bytes<T, NB>();

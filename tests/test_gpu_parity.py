@@ -181,6 +181,9 @@ CASES = [
     ("few_cols_a_transposed", [200, 2050], [2050, 3], True, False, 0),
     ("few_cols_b_transposed", [65, 777], [777, 17], False, True, 3),
     ("few_cols_broadcast", [4, 70, 520], [1, 520, 6], True, False, 0),
+    # M-contiguous A with a padded (16-byte) stride and M % 4 = 3: the vector
+    # copies' partial row groups
+    ("few_cols_a_t_ragged_m", [203, 600], [600, 12], True, False, 5),
 ]
 
 SKINNY_CASES = [c for c in CASES if c[2][-1] <= 32 and c[2][-2] >= 128]
