@@ -1046,7 +1046,7 @@ cudaError_t launch_simt(const Problem &P, cudaStream_t stream)
 
 // Few-column products (N <= 32) on the split-K CUDA-core kernel.  The
 // cluster size C (1, 2, 4 or 8 CTAs splitting K) is the smallest that puts
-// about four CTAs on every SM while each CTA keeps at least four chunks.
+// about 1.5 CTAs on every SM while each CTA keeps at least four chunks.
 template <typename T, int NB, typename TA = T, typename TB = T>
 cudaError_t launch_skinny_nb(const Problem &P, DeviceState *ds, cudaStream_t stream)
 {
@@ -1057,7 +1057,10 @@ cudaError_t launch_skinny_nb(const Problem &P, DeviceState *ds, cudaStream_t str
     const long long m_blocks = (P.M + kSkinnyBM - 1) / kSkinnyBM;
     const long long zb = std::min<long long>(P.batches, 65535);
     const long long chunks = (P.K + kSkinnyKC - 1) / kSkinnyKC;
-    const long long target = 4ll * ds->sms;
+    // about 1.5 CTAs per SM: measured on B200 (graph-timed, N = 10) the
+    // best split for 128 row blocks is C = 2 (11.3 us; C = 8: 14.3), for 32
+    // row blocks C = 8 (11.0 us; C = 2: 20.2), for 2048 row blocks C = 1
+    const long long target = 3ll * ds->sms / 2;
     int C = 1;
     while (C < kSkinnyMaxCluster && m_blocks * zb * C < target && chunks / (2 * C) >= 4)
         C *= 2;
