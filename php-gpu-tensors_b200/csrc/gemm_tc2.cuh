@@ -361,12 +361,14 @@ __global__ void __launch_bounds__(Tc2Config<IN_KIND, OUT>::kThreads, 1)
 // 128 x 256 output block, so per FLOP each SM streams and splits half the
 // bytes of the single-CTA 128 x 128 kernel.
 //
-// Per CTA: a 4-stage ring of raw float32 tiles (A 16 KB + B 16 KB), a 2-slot
-// lo ring, 6 split warps writing lo = tf32(x - trunc(x)) of the CTA's own
-// tiles and 8 epilogue warps (16 warps: 128 registers per thread).  The lo of k-block kb can be stored only when
-// the MMAs of k-block kb - 2 have released its slot, and must be in place
-// before the tensor core runs out of k-block kb - 1's work, a chain of
-// barrier round trips that measured on B200 held the kernel to 188 of the
+// Per CTA: a 3-stage ring of raw float32 tiles (A 16 KB + B 16 KB), a 3-slot
+// lo ring (4 + 2 measured 4 % slower once the split was register-staged),
+// 6 split warps writing lo = tf32(x - trunc(x)) of the CTA's own tiles and 8
+// epilogue warps (16 warps: 128 registers per thread).  The lo of k-block kb
+// can be stored only when the MMAs of k-block kb - L (L lo slots) have
+// released its slot, and must be in place before the tensor core runs out of
+// the k-blocks in between, a chain of barrier round trips that measured on
+// B200 (L = 2) held the kernel to 188 of the
 // 215 TFLOP/s it reached with the wait removed (8192^3, split skipped in both
 // timing builds).  So each split thread loads its raw elements and computes
 // lo into registers as soon as the tile lands, and only stores them once the
@@ -415,7 +417,7 @@ struct Tc2x3Config {
     static constexpr int kLoadBytes = kMix ? kMixRawBytes + kATile : kATile + kBTile;
     static constexpr int kStageBytes = kMix ? kMixOtherOffset + kATile : kLoadBytes;
 #ifndef PTG_PAIR3_STAGES
-#define PTG_PAIR3_STAGES 4
+#define PTG_PAIR3_STAGES 3
 #endif
     static constexpr int kStages = kMix ? 3 : PTG_PAIR3_STAGES;
     static constexpr int kLoStages = kMix ? 0 : 6 - kStages;
