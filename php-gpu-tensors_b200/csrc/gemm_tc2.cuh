@@ -353,40 +353,47 @@ __global__ void __launch_bounds__(Tc2Config<IN_KIND, OUT>::kThreads, 1)
 }
 
 // ---------------------------------------------------------------------------
-// 2-CTA strict float32 (3xTF32) GEMM.
+// 2-CTA split GEMMs: strict float32 (3xTF32, KIND = IN_F32X3) and float32 x
+// bfloat16 products (bf16x3, KIND = IN_MIX_A / IN_MIX_B).
 //
 // A CTA pair computes a 256 x 256 tile with M = 256, N = 256
 // tcgen05.mma.cta_group::2 instructions: CTA r holds rows [128 r, 128 r + 128)
 // of the A tile and columns [128 r, 128 r + 128) of the B tile and computes a
 // 128 x 256 output block, so per FLOP each SM streams and splits half the
-// bytes of the single-CTA 128 x 128 kernel.
+// bytes of the single-CTA 128 x 128 kernels.
 //
-// Per CTA: a 3-stage ring of raw float32 tiles (A 16 KB + B 16 KB), a 3-slot
-// lo ring (4 + 2 measured 4 % slower once the split was register-staged),
-// 6 split warps writing lo = tf32(x - trunc(x)) of the CTA's own tiles and 8
-// epilogue warps (16 warps: 128 registers per thread).  The lo of k-block kb
-// can be stored only when the MMAs of k-block kb - L (L lo slots) have
-// released its slot, and must be in place before the tensor core runs out of
-// the k-blocks in between, a chain of barrier round trips that measured on
-// B200 (L = 2) held the kernel to 188 of the
-// 215 TFLOP/s it reached with the wait removed (8192^3, split skipped in both
-// timing builds).  So each split thread loads its raw elements and computes
-// lo into registers as soon as the tile lands, and only stores them once the
-// slot is free.  (Stages of 16 K in the 64-byte swizzle, twice as many slots
-// in the same bytes, ran slower: 130 against 154 TFLOP/s.)
+// 3xTF32, per CTA: a 3-stage ring of raw float32 tiles (A 16 KB + B 16 KB), a
+// 3-slot lo ring (4 + 2 measured 4 % slower once the split was
+// register-staged), 6 split warps writing lo = tf32(x - trunc(x)) of the
+// CTA's own tiles and 8 epilogue warps (16 warps: 128 registers per thread).
+// The lo of k-block kb can be stored only when the MMAs of k-block kb - L (L
+// lo slots) have released its slot, and must be in place before the tensor
+// core runs out of the k-blocks in between, a chain of barrier round trips
+// that measured on B200 (L = 2) held the kernel to 188 of the 215 TFLOP/s it
+// reached with the wait removed (8192^3, split skipped in both timing
+// builds).  So each split thread loads its raw elements and computes lo into
+// registers as soon as the tile lands, and only stores them once the slot is
+// free.  (Stages of 16 K in the 64-byte swizzle, twice as many slots in the
+// same bytes, ran slower: 130 against 154 TFLOP/s.)
+//
+// bf16x3, per CTA: 3 stages of 64 KB: the float32 operand's raw [128][64]
+// box, split in place by the split warps into its bf16 hi, mid and lo tiles,
+// then the bf16 operand's tile; three kind::f16 MMAs per k16.
+//
 // TMEM: the accumulator (columns [0, 256)) and the running total of the
 // finished K chunks ([256, 512)); the accumulator is single-buffered, so the
 // MMA thread waits for each chunk's drain, which two epilogue warps per TMEM
 // lane quadrant share by columns (8192^3 on B200: 4 epilogue + 8 split warps
 // 163 TFLOP/s, 8 + 6 169.5).
 //
-// Barriers (no TMA multicast anywhere):
+// Barriers (no TMA multicast anywhere), with "leader" the pair's even
+// cluster rank (the only pair without split-K: ranks 0 and 1):
 //   full[s]      per CTA: its own TMA loads of stage s landed.
-//   ready[s]     CTA 0, 2 x 8 arrivals: every split warp of both CTAs wrote lo
-//                for stage s (remote arrive, release.cluster).
+//   ready[s]     leader, 2 x 6 arrivals: every split warp of both CTAs wrote
+//                its part of stage s (remote arrive, release.cluster).
 //   empty[s], lo_free[l], tfull
-//                per CTA, committed by CTA 0's MMA thread to both CTAs.
-//   tempty       CTA 0, 2 x 4 arrivals: the epilogue warps of both CTAs
+//                per CTA, committed by the leader's MMA thread to both CTAs.
+//   tempty       leader, 2 x 8 arrivals: the epilogue warps of both CTAs
 //                drained the accumulator.
 template <int KIND, int CHUNK_KB>
 struct Tc2x3Config {
