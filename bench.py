@@ -136,6 +136,46 @@ def traffic_for(kernel):
         return None
 
 
+def kernel_divisor(name):
+    """Tensor-rate divisor of a kernel against the measured bf16 peak: three
+    TF32 passes (strict float32) 6, one TF32 pass 2, three bf16 passes 3,
+    16-bit 1; None for the CUDA-core kernels."""
+    if "3xtf32" in name:
+        return 6.0
+    if "tf32" in name:
+        return 2.0
+    if "bf16x3" in name:
+        return 3.0
+    if name.startswith("tc"):
+        return 1.0
+    return None
+
+
+def kernel_roofline(per_kernel, peak_info, step_achieved, step_peak):
+    """Roofline of the kernel with the largest share of a multi-launch step:
+    its algorithmic FLOP over its own CUDA-event time; the whole step's
+    figures ride along under "step"."""
+    dom = max(per_kernel, key=lambda k: per_kernel[k]["ms"])
+    d = per_kernel[dom]
+    total_ms = sum(v["ms"] for v in per_kernel.values())
+    achieved = d["flop"] / (d["ms"] / 1e3) / 1e12
+    div = kernel_divisor(dom)
+    peak, src = peak_info
+    out = {"bound": "tensor" if div else "issue", "kernel": dom, "achieved": achieved,
+           "unit": "TFLOP/s", "share": d["ms"] / total_ms, "launches": d["launches"],
+           "ms_per_launch": d["ms"] / d["launches"], "traffic": traffic_for(dom),
+           "step": {"achieved": step_achieved, "peak": step_peak,
+                    "frac": step_achieved / step_peak}}
+    if div:
+        out["peak"] = peak / div
+        out["frac"] = achieved / out["peak"]
+        out["peak_source"] = "%s / %g" % (src, div)
+    out["per_kernel"] = {k: {"launches": v["launches"], "ms": v["ms"],
+                             "tflops": v["flop"] / (v["ms"] / 1e3) / 1e12}
+                         for k, v in sorted(per_kernel.items(), key=lambda kv: -kv[1]["ms"])}
+    return out
+
+
 # ------------------------------------------------------------------ clocks
 class ClockSampler:
     """Polls NVML (read-only) for SM clock and throttle reasons while running."""
@@ -521,11 +561,27 @@ def setup_config4(w, rank, torch, P, lib, stream):
         calls.append((hs[l], dCs[l], dWs[l], fi, batch, fo, 1, fi, fo, 1, fo, 1))
     flop = sum(2.0 * c[3] * c[4] * c[5] for c in calls)
 
+    def launch(call):
+        (a, b, c, m, n, k, a0, a1, b0, b1, c0, c1) = call
+        if not lib.cuda_matmul_launcher(a.data_ptr(), b.data_ptr(), c.data_ptr(), m, n, k,
+                                        a0, a1, b0, b1, c0, c1, sptr):
+            raise RuntimeError("launcher failed: %s" % P.cuda_get_backend_info())
+
     def step():
-        for (a, b, c, m, n, k, a0, a1, b0, b1, c0, c1) in calls:
-            if not lib.cuda_matmul_launcher(a.data_ptr(), b.data_ptr(), c.data_ptr(), m, n, k,
-                                            a0, a1, b0, b1, c0, c1, sptr):
-                raise RuntimeError("launcher failed: %s" % P.cuda_get_backend_info())
+        for call in calls:
+            launch(call)
+
+    def profile_step():
+        """One step with CUDA events around every launch (outside the timed
+        region: events between launches stop their programmatic overlap)."""
+        out = []
+        for call in calls:
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            launch(call)
+            e1.record(stream)
+            out.append((P.cuda_get_backend_info()["kernel"], 2.0 * call[3] * call[4] * call[5], e0, e1))
+        return out
 
     inputs = [x] + Ws + dCs
     outputs = dWs + [hs[3]]
@@ -540,8 +596,8 @@ def setup_config4(w, rank, torch, P, lib, stream):
             h.copy_(d, non_blocking=True)
 
     return {
-        "step": step, "e2e_step": e2e_step, "flop": flop, "launches": len(calls),
-        "dtype": "f32", "flush": True, "peak_div": 6.0,
+        "step": step, "e2e_step": e2e_step, "profile_step": profile_step, "flop": flop,
+        "launches": len(calls), "dtype": "f32", "flush": True, "peak_div": 6.0,
         "data": "synthetic x U[0,1), W N(0,1/fan_in), dC N(0,1) on device",
         "config": {"batch": batch, "layers": "784->1024->1024->10",
                    "gemms_per_step": len(calls), "precision": "fp32-strict",
@@ -632,6 +688,25 @@ def run_ours(args, w):
     e2e_ms = max_over_ranks(start.elapsed_time(stop), world, "cuda")
     e2e_value = flop_rank * world * e2e_steps / (e2e_ms / 1e3) / 1e12
 
+    # Multi-launch steps: every launch timed on its own (CUDA events on the
+    # launching stream, L2 flushed before each step as in the timed region);
+    # the kernel with the largest share is the one the roofline describes.
+    per_kernel, prof_steps = None, 0
+    if "profile_step" in wl:
+        recs = []
+        prof_steps = max(3, min(args.steps, 10))
+        for _ in range(prof_steps):
+            if flush is not None:
+                flush.add_(1)
+            recs.extend(wl["profile_step"]())
+        torch.cuda.synchronize()
+        per_kernel = {}
+        for name, fl, e0, e1 in recs:
+            d = per_kernel.setdefault(name, {"launches": 0, "ms": 0.0, "flop": 0.0})
+            d["launches"] += 1
+            d["ms"] += e0.elapsed_time(e1)
+            d["flop"] += fl
+
     cpu = None
     if rank == 0 and world == 1:
         v, cores, dt, text = cpu_sample(w, args.cpu_seconds)
@@ -669,6 +744,10 @@ def run_ours(args, w):
             "gpu_launches": args.steps * wl["launches"],
             "clocks": sampler.summary(),
         }
+        if per_kernel:
+            line["roofline"] = kernel_roofline(per_kernel, peaks(), achieved, peak)
+            line["config"]["kernels"] = {k: v["launches"] // prof_steps
+                                         for k, v in per_kernel.items()}
         print(json.dumps(line), flush=True)
     if world > 1:
         import torch.distributed as dist
