@@ -34,6 +34,7 @@ constexpr int kSkinnyBM = 32;      // rows per CTA (one per lane)
 constexpr int kSkinnyKC = 32;      // k per staged chunk
 constexpr int kSkinnyThreads = 256;
 constexpr int kSkinnyMaxCluster = 8;
+constexpr int kSkinnyRegChunks = 4;   // register-staged kernel: chunks loaded ahead
 
 template <int NB>
 struct SkinnyShape {
@@ -138,8 +139,11 @@ __global__ void __launch_bounds__(kSkinnyThreads) skinny_gemm_kernel(const SimtP
         }
         const int m0 = mb * kSkinnyBM;
 
-        Acc ra[S::kAPerThread], rb[S::kBPerThread];
-        auto load_chunk = [&](int c) {
+        // kSkinnyRegChunks chunks in flight in registers (a chunk is only
+        // kAPerThread + kBPerThread values per thread), so the loop does not
+        // wait a global-load round trip per chunk
+        Acc ra_ring[kSkinnyRegChunks][S::kAPerThread], rb_ring[kSkinnyRegChunks][S::kBPerThread];
+        auto load_chunk = [&](int c, Acc (&ra)[S::kAPerThread], Acc (&rb)[S::kBPerThread]) {
             const int k0 = c * kSkinnyKC;
 #pragma unroll
             for (int i = 0; i < S::kAPerThread; i++) {
@@ -164,7 +168,8 @@ __global__ void __launch_bounds__(kSkinnyThreads) skinny_gemm_kernel(const SimtP
                             : Acc(0);
             }
         };
-        auto store_chunk = [&](int buf) {
+        auto store_chunk = [&](int buf, const Acc (&ra)[S::kAPerThread],
+                               const Acc (&rb)[S::kBPerThread]) {
 #pragma unroll
             for (int i = 0; i < S::kAPerThread; i++) {
                 const int e = threadIdx.x + kSkinnyThreads * i;
@@ -184,22 +189,30 @@ __global__ void __launch_bounds__(kSkinnyThreads) skinny_gemm_kernel(const SimtP
         };
 
         Acc acc[4] = {Acc(0), Acc(0), Acc(0), Acc(0)};
-        if (c_begin < c_end)
-            load_chunk(c_begin);
-        for (int c = c_begin; c < c_end; c++) {
-            const int buf = (c - c_begin) & 1;
-            store_chunk(buf);
-            __syncthreads();
-            if (c + 1 < c_end)
-                load_chunk(c + 1);   // global loads in flight during the math below
 #pragma unroll
-            for (int kk = kg * S::kKPerGroup; kk < (kg + 1) * S::kKPerGroup; kk++) {
-                const Acc a = sA[buf][kk][lane];
-                Acc b[4];
-                load4(&sB[buf][kk][cg * 4], b);
+        for (int j = 0; j < kSkinnyRegChunks; j++)
+            if (c_begin + j < c_end)
+                load_chunk(c_begin + j, ra_ring[j], rb_ring[j]);
+        for (int c0 = c_begin; c0 < c_end; c0 += kSkinnyRegChunks) {
 #pragma unroll
-                for (int j = 0; j < 4; j++)
-                    acc[j] = E::fma_(a, b[j], acc[j]);
+            for (int j = 0; j < kSkinnyRegChunks; j++) {   // static ring slot j
+                const int c = c0 + j;
+                if (c >= c_end)
+                    break;   // uniform over the block
+                const int buf = (c - c_begin) & 1;
+                store_chunk(buf, ra_ring[j], rb_ring[j]);
+                __syncthreads();
+                if (c + kSkinnyRegChunks < c_end)   // refill the slot just stored
+                    load_chunk(c + kSkinnyRegChunks, ra_ring[j], rb_ring[j]);
+#pragma unroll
+                for (int kk = kg * S::kKPerGroup; kk < (kg + 1) * S::kKPerGroup; kk++) {
+                    const Acc a = sA[buf][kk][lane];
+                    Acc b[4];
+                    load4(&sB[buf][kk][cg * 4], b);
+#pragma unroll
+                    for (int q = 0; q < 4; q++)
+                        acc[q] = E::fma_(a, b[q], acc[q]);
+                }
             }
         }
 #pragma unroll
