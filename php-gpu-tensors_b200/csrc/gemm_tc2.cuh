@@ -230,12 +230,14 @@ __global__ void __launch_bounds__(Tc2Config<IN_KIND, OUT>::kThreads, 1)
                     for (int k = 0; k < Cfg::kKSteps; k++) {
                         const uint32_t a_off = p.a_mn_major ? k * Cfg::kMmaK * 128 : k * 32;
                         const uint32_t b_off = p.b_mn_major ? k * Cfg::kMmaK * 128 : k * 32;
-                        const uint64_t ad =
-                            p.a_mn_major ? smem_desc(sa + a_off, Cfg::kChunkBytes, Cfg::kMnSbo, Cfg::kMnLayout)
-                                         : smem_desc(sa + a_off, 16, 1024, kLayoutSw128);
-                        const uint64_t bd =
-                            p.b_mn_major ? smem_desc(sb + b_off, Cfg::kChunkBytes, Cfg::kMnSbo, Cfg::kMnLayout)
-                                         : smem_desc(sb + b_off, 16, 1024, kLayoutSw128);
+                        // (for 16-bit operands the MN-major SBO and layout equal
+                        // the K-major ones, so only the LBO depends on the layout)
+                        const uint64_t ad = smem_desc(sa + a_off, p.a_mn_major ? Cfg::kChunkBytes : 16,
+                                                      p.a_mn_major ? Cfg::kMnSbo : 1024,
+                                                      p.a_mn_major ? Cfg::kMnLayout : kLayoutSw128);
+                        const uint64_t bd = smem_desc(sb + b_off, p.b_mn_major ? Cfg::kChunkBytes : 16,
+                                                      p.b_mn_major ? Cfg::kMnSbo : 1024,
+                                                      p.b_mn_major ? Cfg::kMnLayout : kLayoutSw128);
                         if constexpr (Cfg::kTf32)
                             umma_tf32_pair(d_tmem, ad, bd, p.idesc, (kb | k) != 0);
                         else
