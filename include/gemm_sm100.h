@@ -222,7 +222,8 @@ int cuda_matmul_epilogue_nd_launcher(
     const void *bias, int activation, cudaStream_t stream);
 
 /* Name of the kernel the last successful launch on this thread used, e.g.
- * "tc-bf16-128x256", "tc-3xtf32-128x128", "simt-f32"; "none" before any. */
+ * "tc2-bf16-256x256", "tc2-3xtf32-256x256", "tc-3xtf32-128x128",
+ * "skinny-f32", "simt-f32"; "none" before any. */
 const char *gemm_sm100_last_kernel(void);
 
 /* Grid size (CTAs), CTA size (threads) and cluster size of the last
@@ -233,9 +234,12 @@ void gemm_sm100_last_launch(int *grid, int *block, int *cluster);
 /* Selects the kernel family for this thread's later launches and returns the
  * previous setting: 0 = automatic, 1 = single-CTA tensor-core kernel whenever
  * the layout allows it (ignoring the size heuristic), 2 = CUDA-core kernel
- * only, 3 = 2-CTA tensor-core kernel for float16/bfloat16 whenever the layout
- * allows it (other dtypes as 1), 4 = few-column split-K CUDA-core kernel
- * whenever N <= 32 and K >= 128 (otherwise as 0). */
+ * only, 3 = 2-CTA tensor-core kernel whenever the layout allows it: 16-bit,
+ * tf32 mode, strict float32 (3xTF32) and float32 x bf16 products, the split
+ * kinds splitting K over clusters of 2 or 4 pairs when they have fewer tiles
+ * than a quarter of the SMs (float64 and bf16/f16 x bf16/f16 -> float32 as 1),
+ * 4 = few-column split-K CUDA-core kernel whenever N <= 32 and K >= 128
+ * (otherwise as 0). */
 int gemm_sm100_set_path(int path);
 
 /* Reads (and with clear != 0 resets) the device status word of `device`:
