@@ -174,6 +174,7 @@ int cuda_low_precision_matmul_nd_launcher(
 #define GEMM_SM100_STATUS_NO_DEVICE 9003   /* no current CUDA device / not sm_100 */
 #define GEMM_SM100_STATUS_NCCL 9004        /* NCCL failure (multi-GPU entry points) */
 #define GEMM_SM100_STATUS_SCRATCH_LIMIT 9005 /* product larger than the library-owned buffer */
+#define GEMM_SM100_STATUS_INVALID_ARGUMENT 9006 /* a multi-GPU entry point rejected its arguments */
 
 /* float32 C = A.B where A and B are float32, float16 or bfloat16 (not float16
  * with bfloat16), with the batched launcher's shape/broadcast rules: the
@@ -291,7 +292,9 @@ size_t gemm_mgpu_nsplit_workspace_bytes(int nranks, dtype_t dtype, int M, int N)
  * computed into slot r of `workspace`, the slots are all-gathered in place
  * (ncclAllGather), and a permute kernel writes C.  dtype FLOAT64, FLOAT32,
  * FLOAT16 or BFLOAT16; N % nranks == 0.  Returns 1 / 0 (last_blas_status has
- * the CUDA error or GEMM_SM100_STATUS_NCCL). */
+ * the CUDA error, GEMM_SM100_STATUS_NCCL, or GEMM_SM100_STATUS_INVALID_ARGUMENT
+ * for a null pointer, a negative extent, N not divisible by the rank count or
+ * a workspace smaller than M * N elements). */
 int gemm_mgpu_nsplit_matmul(gemm_mgpu_comm *comm, dtype_t dtype,
                             const void *a, size_t a_s0, size_t a_s1,
                             const void *b_local, size_t b_s0, size_t b_s1,
@@ -314,7 +317,16 @@ void gemm_mgpu_window_destroy(gemm_mgpu_window *win);
  * After the call's work completes on `stream` (a one-element NCCL all-reduce
  * follows the kernel), every rank's window holds the whole row-major C
  * [M, N].  dtype FLOAT64; N divisible by the rank count with an even block
- * width; M * N * 8 <= the window's bytes.  Returns 1 / 0. */
+ * width; M * N * 8 <= the window's bytes.  Returns 1 / 0 (last_blas_status as
+ * for gemm_mgpu_nsplit_matmul).
+ *
+ * Reuse of a window: the kernel of call k + 1 stores into every peer's
+ * window, which a peer may still be reading from call k.  So every call first
+ * runs a one-element NCCL all-reduce on `stream` and launches the kernel
+ * behind it: no rank's stores of call k + 1 start before every rank's
+ * `stream` has reached call k + 1.  A rank must therefore finish reading its
+ * window (on `stream`, or on a stream that `stream` waits for) before it
+ * makes the next call; reads on an unrelated stream are not ordered. */
 int gemm_mgpu_nsplit_matmul_fused(gemm_mgpu_window *win, dtype_t dtype,
                                   const void *a, size_t a_s0, size_t a_s1,
                                   const void *b_local, size_t b_s0, size_t b_s1,

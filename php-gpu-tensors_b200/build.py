@@ -72,8 +72,21 @@ def build_library(force=False, verbose=False):
     return LIB
 
 
+def reference_src():
+    """src/ of the reference tree used to build oracle/_ref: PTG_REFERENCE_ROOT
+    when set, else a `reference` directory beside the repository; None when
+    neither exists (e.g. on a GPU box, which uses the prebuilt files)."""
+    root = os.environ.get("PTG_REFERENCE_ROOT") or os.path.join(os.path.dirname(ROOT),
+                                                                "reference")
+    src = os.path.join(root, "src")
+    return src if os.path.isdir(src) else None
+
+
 def build_oracle(verbose=False):
     cmd = ["make", "-s", "-C", os.path.join(ROOT, "oracle"), "all"]
+    src = reference_src()
+    if src:
+        cmd.append("REF_SRC=" + src)
     if verbose:
         print(" ".join(cmd), flush=True)
     subprocess.run(cmd, check=True)

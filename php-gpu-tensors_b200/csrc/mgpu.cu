@@ -163,15 +163,19 @@ PT_API int gemm_mgpu_nsplit_matmul(gemm_mgpu_comm *comm, dtype_t dtype, const vo
                                    size_t workspace_bytes, cudaStream_t stream)
 {
     const size_t es = element_bytes(dtype);
-    if (!comm || es == 0 || M < 0 || N < 0 || K < 0 || N % comm->nranks != 0)
+    if (!comm || es == 0 || M < 0 || N < 0 || K < 0 || N % comm->nranks != 0) {
+        ptg_set_last_status(GEMM_SM100_STATUS_INVALID_ARGUMENT);
         return 0;
+    }
     if (M == 0 || N == 0)
         return 1;
     const int G = comm->nranks;
     const int nb = N / G;
     const size_t slot = static_cast<size_t>(M) * nb;
-    if (!workspace || !c || workspace_bytes < slot * G * es)
+    if (!workspace || !c || workspace_bytes < slot * G * es) {
+        ptg_set_last_status(GEMM_SM100_STATUS_INVALID_ARGUMENT);
         return 0;
+    }
     // 1. this rank's column block into its slot of the gather buffer
     void *mine = static_cast<char *>(workspace) + slot * comm->rank * es;
     int sa[2] = {M, K}, sb[2] = {K, nb}, sc[2] = {M, nb};
@@ -277,8 +281,10 @@ PT_API int gemm_mgpu_nsplit_matmul_noalloc(gemm_mgpu_comm *comm, dtype_t dtype, 
                                            int K, cudaStream_t stream)
 {
     const size_t es = element_bytes(dtype);
-    if (!comm || es == 0 || M < 0 || N < 0 || K < 0)
+    if (!comm || es == 0 || M < 0 || N < 0 || K < 0) {
+        ptg_set_last_status(GEMM_SM100_STATUS_INVALID_ARGUMENT);
         return 0;
+    }
     const size_t need = static_cast<size_t>(M) * static_cast<size_t>(N) * es;
     if (need > GEMM_MGPU_NSPLIT_SCRATCH_BYTES) {
         ptg_set_last_status(GEMM_SM100_STATUS_SCRATCH_LIMIT);
@@ -306,7 +312,9 @@ PT_API int gemm_mgpu_nsplit_matmul_noalloc(gemm_mgpu_comm *comm, dtype_t dtype, 
 // row into all ranks' results directly.  No gather buffer, no permute; the
 // peer stores overlap the remaining tiles' tensor-core work.  A one-element
 // NCCL all-reduce after the kernel orders every rank's stores before any rank
-// goes on to read its result.
+// goes on to read its result, and another one before the kernel keeps a
+// rank's stores of the next call out of a peer's window until that peer has
+// reached the call (it may still be reading the previous result).
 
 struct gemm_mgpu_window {
     gemm_mgpu_comm *comm;
@@ -389,15 +397,28 @@ PT_API int gemm_mgpu_nsplit_matmul_fused(gemm_mgpu_window *win, dtype_t dtype, c
                                          size_t b_s0, size_t b_s1, int M, int N, int K,
                                          cudaStream_t stream)
 {
-    if (!win || dtype != DTYPE_FLOAT64 || M < 0 || N < 0 || K < 0)
+    if (!win || dtype != DTYPE_FLOAT64 || M < 0 || N < 0 || K < 0) {
+        ptg_set_last_status(GEMM_SM100_STATUS_INVALID_ARGUMENT);
         return 0;
+    }
     gemm_mgpu_comm *comm = win->comm;
     const int G = comm->nranks;
     if (N % G != 0 || (N / G) % 2 != 0 ||
-        static_cast<size_t>(M) * static_cast<size_t>(N) * 8 > win->bytes)
+        static_cast<size_t>(M) * static_cast<size_t>(N) * 8 > win->bytes) {
+        ptg_set_last_status(GEMM_SM100_STATUS_INVALID_ARGUMENT);
         return 0;
+    }
     if (M == 0 || N == 0)
         return 1;
+    // Entry ordering: this call's kernel stores into every peer's window, and
+    // a peer may still be reading the previous call's result there.  The
+    // one-element all-reduce completes on this stream only once every rank's
+    // stream has reached it, i.e. once every rank is done with call k.
+    if (G > 1 && g_nccl.all_reduce(win->sync, win->sync, 1, ncclInt32, ncclSum, comm->nccl,
+                                   stream) != ncclSuccess) {
+        ptg_set_last_status(GEMM_SM100_STATUS_NCCL);
+        return 0;
+    }
     ptg::F64PeerOut po;
     std::memset(&po, 0, sizeof(po));
     for (int g = 0; g < G; g++)

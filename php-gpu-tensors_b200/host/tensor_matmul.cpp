@@ -604,11 +604,15 @@ int host_matmul_devices(const void *a, const void *b, void *c, dtype_t dtype, in
         return fail(PT_INVALID_ARGUMENT, "Matrix multiplication failed - incompatible dimensions");
     if (ndev < 1 || ndev > kMaxPipeDevices || !devices)
         return fail(PT_INVALID_ARGUMENT, "host matmul needs between 1 and 64 devices");
-    for (int g = 0; g < ndev; g++)
+    for (int g = 0; g < ndev; g++) {
+        if (devices[g] < 0 || devices[g] >= kMaxPipeDevices)
+            return fail(PT_INVALID_ARGUMENT, "host matmul device %d is out of range",
+                        devices[g]);
         for (int h = 0; h < g; h++)
-            if (devices[g] == devices[h] || devices[g] < 0 || devices[g] >= kMaxPipeDevices)
+            if (devices[g] == devices[h])
                 return fail(PT_INVALID_ARGUMENT, "host matmul devices must be distinct, got %d",
                             devices[g]);
+    }
     if (batches == 0 || M == 0 || N == 0)
         return ok();
     HostJob j;

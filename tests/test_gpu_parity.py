@@ -919,22 +919,32 @@ def test_host_matmul_streams_equal_device_product(dtype, shared):
 @pytest.mark.parametrize("dtype", ["bfloat16", "float32"])
 def test_host_matmul_sharded_over_devices(dtype):
     """pt_host_matmul_sharded: the batch cut over every GPU of this process
-    (one on a single-GPU box), chunks pipelined per device, equals the device
-    product; a shared B reaches every device."""
+    (one on a single-GPU box), chunks pipelined per device, against the CPU
+    oracle (HostArray::matmul restated) on the same operands, every batch;
+    a shared B reaches every device."""
     tdt = TORCH_DT[dtype]
     devices = list(range(torch.cuda.device_count()))
-    g = torch.Generator().manual_seed(12)
     batches, M, N, K = 9, 256, 264, 320
-    a = torch.randn(batches, M, K, generator=g).to(tdt).pin_memory()
+
+    def host(storage, shape):
+        s = np.ascontiguousarray(storage)
+        t = torch.from_numpy(s.view(np.int16).copy()).view(tdt) if dtype == "bfloat16" \
+            else torch.from_numpy(s.copy())
+        return t.reshape(shape).pin_memory()
+
+    av = O.to_storage(O.seeded([batches, M, K], 12, "normal"), dtype)
+    a = host(av, [batches, M, K])
+    th = O.oracle().orc_host_threads()
     for shared in (False, True):
-        b = (torch.randn(K, N, generator=g) if shared
-             else torch.randn(batches, K, N, generator=g)).to(tdt).pin_memory()
+        bshape = [K, N] if shared else [batches, K, N]
+        bv = O.to_storage(O.seeded(bshape, 13 + shared, "normal"), dtype)
+        b = host(bv, bshape)
         c = torch.full((batches, M, N), float("nan"), dtype=tdt).pin_memory()
         P.host_matmul(a, b, c, chunks=2, devices=devices)
         torch.cuda.set_device(0)
-        ref = torch.matmul(a.cuda().double(), b.cuda().double()).cpu()
-        err = (c.double() - ref).abs().max() / ref.abs().max()
-        assert err <= (1e-2 if dtype == "bfloat16" else 1e-5), (shared, float(err))
+        ref = O.host_matmul(O.dense(av, [batches, M, K]), O.dense(bv, bshape), dtype, th)
+        got = c.view(torch.int16).numpy().view(np.uint16) if dtype == "bfloat16" else c.numpy()
+        check_close(got, ref, dtype, ("sharded", shared))
         assert torch.cuda.current_device() == 0
 
 

@@ -4,10 +4,11 @@ CPU (gloo, world size 2, no GPU calls): batch sharding and N-split column
 ranges tile the work exactly once, the library's N-split workspace size is
 consistent across ranks, and the bench's max-over-ranks timing rule.
 
-GPU: the N-split entry points (NCCL all-gather + permute, and the fused
-kernel whose epilogue stores into every rank's window) with one rank equal
-the plain product bit for bit; with two ranks every rank receives the full
-product, again bit-identical to the single-GPU product.
+GPU: the N-split entry points (NCCL all-gather + permute, the fused kernel
+whose epilogue stores into every rank's window, and the allocation-free
+variant) with one rank equal the plain product bit for bit; with two ranks
+every rank receives the full product, bit-identical to the single-GPU
+product, on two calls in a row with different inputs.
 """
 import os
 import socket
@@ -114,8 +115,16 @@ def test_nsplit_single_rank_equals_plain_product():
 
 
 def _nccl_worker(rank, world, port, q):
+    """One rank of the 2-rank N-split test.  Each entry point is called twice
+    with different inputs, so a result that kept data of the previous call
+    (or a peer's stores into this rank's window that raced ahead of this
+    rank's reads) shows up as a mismatch.  The reference for every call is
+    the single-GPU product of the full operands; rank 0 also checks sampled
+    rows of it against the oracle's double twin of HostArray::matmul."""
     import torch.distributed as dist
     sys.path.insert(0, os.path.join(ROOT, "php-gpu-tensors_b200"))
+    sys.path.insert(0, os.path.join(ROOT, "tests"))
+    import oracle_lib as O
     import phptensors as P
     import datetime
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
@@ -124,25 +133,50 @@ def _nccl_worker(rank, world, port, q):
                             timeout=datetime.timedelta(seconds=60),
                             device_id=torch.device("cuda", rank))
     comm = None
+    results = {}
     try:
         M, N, K = 1024, 2048, 1536
-        g = torch.Generator(device="cuda").manual_seed(11)
-        a = torch.rand(M, K, device="cuda", generator=g, dtype=torch.float64) - 0.5
-        b = torch.rand(K, N, device="cuda", generator=g, dtype=torch.float64) - 0.5
         lo, hi = P.nsplit_columns(N, rank, world)
         comm = P.MgpuComm(rank, world)
-        bl = P.CudaArray.from_torch(b[:, lo:hi].contiguous())
-        c = P.nsplit_matmul(comm, P.CudaArray.from_torch(a), bl, N)
-        full = P.CudaArray.from_torch(a).matmul(P.CudaArray.from_torch(b), allow_float64=True)
         win = P.MgpuWindow(comm, M, N)
-        fused_ok = True
-        for _ in range(2):
-            f = P.nsplit_matmul_fused(win, P.CudaArray.from_torch(a), bl)
+        lib = P.library()
+        for call in range(2):
+            # the same seed on every rank: all ranks hold the same A and B
+            g = torch.Generator(device="cuda").manual_seed(11 + call)
+            a = torch.rand(M, K, device="cuda", generator=g, dtype=torch.float64) - 0.5
+            b = torch.rand(K, N, device="cuda", generator=g, dtype=torch.float64) - 0.5
+            bl = b[:, lo:hi].contiguous()
+            full = P.CudaArray.from_torch(a).matmul(P.CudaArray.from_torch(b),
+                                                    allow_float64=True).to_torch()
+            c = P.nsplit_matmul(comm, P.CudaArray.from_torch(a), P.CudaArray.from_torch(bl), N)
+            results[("nccl", call)] = bool(torch.equal(c.to_torch(), full))
+            f = P.nsplit_matmul_fused(win, P.CudaArray.from_torch(a), P.CudaArray.from_torch(bl))
             torch.cuda.synchronize()
-            fused_ok = fused_ok and bool(torch.equal(f, full.to_torch()))
-        dist.barrier()
+            results[("fused", call)] = bool(torch.equal(f, full))
+            # the allocation-free entry point: its gather runs in the
+            # library's own device buffer at rank offsets
+            na = torch.full((M, N), float("nan"), device="cuda", dtype=torch.float64)
+            ok = lib.gemm_mgpu_nsplit_matmul_noalloc(
+                comm.handle, P.DTYPE_CODES["float64"], a.data_ptr(), a.stride(0), a.stride(1),
+                bl.data_ptr(), bl.stride(0), bl.stride(1), na.data_ptr(), M, N, K,
+                P.current_stream())
+            torch.cuda.synchronize()
+            results[("noalloc", call)] = ok == 1 and bool(torch.equal(na, full))
+            if rank == 0:
+                rows = [0, 517, M - 1]
+                ao = O.dense(a.cpu().numpy(), [M, K])
+                bo = O.dense(b.cpu().numpy(), [K, N])
+                th = O.oracle().orc_host_threads()
+                got = full.cpu().numpy()
+                good = True
+                for r in rows:
+                    ref = O.host_matmul_f64_range(ao, bo, "float64", r * N, N, th)
+                    err = np.max(np.abs(got[r] - ref)) / max(1.0, float(np.max(np.abs(ref))))
+                    good = good and err <= 1e-12
+                results[("oracle", call)] = good
+            dist.barrier()
         win.close()
-        q.put((rank, bool(torch.equal(c.to_torch(), full.to_torch())) and fused_ok))
+        q.put((rank, results))
     finally:
         if comm is not None:
             comm.close()
@@ -164,4 +198,7 @@ def test_nsplit_two_ranks_all_gather():
     for p in procs:
         p.join(timeout=120)
         assert p.exitcode == 0
-    assert got == {0: True, 1: True}
+    for rank in range(world):
+        for key, good in got[rank].items():
+            assert good, (rank, key)
+    assert ("oracle", 1) in got[0] and ("noalloc", 1) in got[1]

@@ -26,6 +26,7 @@ pytestmark = pytest.mark.gpu
 
 SCRATCH_BYTES = 32 << 20          # GEMM_MGPU_NSPLIT_SCRATCH_BYTES
 STATUS_SCRATCH_LIMIT = 9005       # GEMM_SM100_STATUS_SCRATCH_LIMIT
+STATUS_INVALID_ARGUMENT = 9006    # GEMM_SM100_STATUS_INVALID_ARGUMENT
 
 
 def _call_noalloc(lib, comm, a, b, c, M, N, K, dtype):
@@ -85,5 +86,8 @@ def test_noalloc_rejects_products_larger_than_its_buffer():
         assert P.cuda_get_backend_info()["lastBlasStatus"] == STATUS_SCRATCH_LIMIT
         torch.cuda.synchronize()
         assert bool((c == 7.0).all())      # nothing was enqueued
+        # an argument the N-split rejects sets its own status, not a stale one
+        assert _call_noalloc(lib, comm, a, b, c, 64, 64, -1, "float64") == 0
+        assert P.cuda_get_backend_info()["lastBlasStatus"] == STATUS_INVALID_ARGUMENT
     finally:
         comm.close()
