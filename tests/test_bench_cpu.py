@@ -42,3 +42,19 @@ def test_kernel_roofline_cuda_core_kernel_has_no_tensor_peak():
     per = {"simt-f32": {"launches": 2, "ms": 0.2, "flop": 2e6}}
     r = bench.kernel_roofline(per, (1635.7, "measured"), 1.0, 272.6)
     assert r["bound"] == "issue" and "peak" not in r and "frac" not in r
+
+
+def test_default_run_is_config5a_with_the_other_configs_as_blocks():
+    args = bench.parse([])
+    assert args.workload == "config5a"
+    assert args.blocks == ["config2", "config3", "config4", "config5b"]
+    assert bench.parse(["--workload", "config2"]).blocks == []
+    assert bench.parse(["--blocks", "none"]).blocks == []
+    assert bench.parse(["--workload", "config2", "--blocks", "config2,config4"]).blocks == \
+        ["config4"]
+
+
+def test_traffic_is_looked_up_per_workload_and_kernel():
+    assert bench.traffic_for("config2", "tc2-bf16-256x256") > 0
+    assert bench.traffic_for("config2", "no-such-kernel") is None
+    assert bench.traffic_for("no-such-workload", "tc2-bf16-256x256") is None
