@@ -18,9 +18,11 @@ One step = one pass of a workload through the library's launchers:
            row-major, so B is a transposed view) with the fused +bias[4096],
            tanh epilogue (cuda_matmul_epilogue_nd_launcher); one per rank (weak).
   config4  BASELINE config 4: the float32 MLP GEMM set, batch 4096,
-           784->1024->1024->10: per layer the forward product, dA = dC.W^T and
-           dW = h^T.dC on transposed views, nine cuda_matmul_launcher calls in
-           strict float32 (3xTF32 / few-column kernels); one per rank (weak).
+           784->1024->1024->10: per layer the forward product
+           (cuda_matmul_launcher) and the autograd node's dA = dC.W^T and
+           dW = h^T.dC on transposed views (pt_tensor_matmul_backward, dW on a
+           forked side stream), nine products in strict float32 (3xTF32 /
+           few-column kernels); one per rank (weak).
   config5b BASELINE config 5b: float64 [8192,8192]^2 split along N over the
            ranks.  Timed three ways: the fused N-split (the column block's
            epilogue stores into every rank's result over NVLink), the NCCL
@@ -628,7 +630,12 @@ def setup_config4_bf16(ctx, w):
 
 
 def setup_config4(ctx, w):
-    """config4: the float32 MLP GEMM set (forward, dA, dW per layer)."""
+    """config4: the float32 MLP GEMM set: per layer the forward product
+    through cuda_matmul_launcher (CudaArray::matmul's 2-D float32 entry) and
+    the backward node's two products through pt_tensor_matmul_backward (the
+    autograd matmul node, src/autograd.c:1539-1585: dA = dC.W^T on the
+    caller's stream, dW = h^T.dC on a side stream forked from and joined back
+    into it)."""
     torch, P, lib = ctx.torch, ctx.P, ctx.lib
     dims = w["mlp"]
     batch = w["M"]
@@ -652,6 +659,9 @@ def setup_config4(ctx, w):
         calls.append((dCs[l], Ws[l], dAs[l], batch, fo, fi, fo, 1, 1, fo, fi, 1))
         calls.append((hs[l], dCs[l], dWs[l], fi, batch, fo, 1, fi, fo, 1, fo, 1))
     flop = sum(2.0 * c[3] * c[4] * c[5] for c in calls)
+    wrap = [P.CudaArray.from_torch(t) for t in hs + Ws + dCs + dAs + dWs]
+    pts = [t._pt() for t in wrap]
+    H, W, DC, DA, DW = pts[0:4], pts[4:7], pts[7:10], pts[10:13], pts[13:16]
 
     def launch(call):
         (a, b, c, m, n, k, a0, a1, b0, b1, c0, c1) = call
@@ -660,12 +670,20 @@ def setup_config4(ctx, w):
             raise RuntimeError("launcher failed: %s" % P.cuda_get_backend_info())
 
     def step():
-        for call in calls:
+        for call in calls[:3]:
             launch(call)
+        for l in range(3):
+            rc = lib.pt_tensor_matmul_backward(ctypes.byref(H[l]), ctypes.byref(W[l]),
+                                               ctypes.byref(DC[l]), ctypes.byref(DA[l]),
+                                               ctypes.byref(DW[l]), sptr)
+            if rc != P.PT_OK:
+                raise RuntimeError(lib.pt_last_error())
 
     def profile_step():
-        """One step with CUDA events around every launch (outside the timed
-        region: events between launches stop their programmatic overlap)."""
+        """The step's nine products one by one on the caller's stream, with
+        CUDA events around every launch (outside the timed region: events
+        between launches stop their programmatic overlap, and the backward
+        node's side stream is not used), to attribute time to kernels."""
         out = []
         for call in calls:
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -710,9 +728,12 @@ def setup_config4(ctx, w):
         "data": "synthetic x U[0,1), W N(0,1/fan_in), dC N(0,1) on device",
         "config": {"batch": batch, "layers": "784->1024->1024->10",
                    "gemms_per_step": len(calls), "precision": "fp32-strict",
+                   "calls": "forward: cuda_matmul_launcher; backward: pt_tensor_matmul_backward "
+                            "(dW on a forked side stream)",
                    "l2": "L2 flushed before every step (256 MB write, outside the timing)"},
         "h2d": sum(t.numel() for t in inputs) * 4, "d2h": sum(t.numel() for t in outputs) * 4,
-        "api": "cuda_matmul_launcher x9 with pinned-host copies on the stream",
+        "api": "cuda_matmul_launcher x3 + pt_tensor_matmul_backward x3 with pinned-host "
+               "copies on the stream",
     }
 
 

@@ -979,9 +979,7 @@ cudaError_t launch_f64_dmma(const Problem &P, DeviceState *ds, cudaStream_t stre
     dim3 grid(static_cast<unsigned>(std::min<long long>(nb, 2147483647ll)),
               static_cast<unsigned>(std::min<long long>(mb, 65535)),
               static_cast<unsigned>(std::min<long long>(P.batches, 65535)));
-    F64PeerOut none;
-    std::memset(&none, 0, sizeof(none));
-    f64_dmma_kernel<<<grid, 256, kF64SmemBytes, stream>>>(s, a_vec ? 1 : 0, b_vec ? 1 : 0, none);
+    f64_dmma_kernel<<<grid, 256, kF64SmemBytes, stream>>>(s, a_vec ? 1 : 0, b_vec ? 1 : 0);
     return cudaGetLastError();
 }
 
@@ -1378,13 +1376,14 @@ cudaError_t ptg_launch_f64_peer(const double *a, size_t a_s0, size_t a_s1, const
                        reinterpret_cast<uintptr_t>(a) % 16 == 0;
     const bool b_vec = P.b_sn == 1 && P.N % 2 == 0 && (P.b_sk % 2 == 0 || P.K == 1) &&
                        reinterpret_cast<uintptr_t>(b) % 16 == 0;
-    auto kernel = f64_dmma_kernel_t<true>;
-    if (!ensure_smem_attr(ds, KID_F64_DMMA_PEER, kernel, kF64SmemBytes))
+    auto kernel = f64_dmma_peer_kernel;
+    if (!ensure_smem_attr(ds, KID_F64_DMMA_PEER, kernel, kF64PeerSmemBytes))
         return cudaErrorInvalidConfiguration;
     const long long mb = (P.M + kF64BM - 1) / kF64BM;
     const long long nbk = (P.N + kF64BN - 1) / kF64BN;
-    dim3 grid(static_cast<unsigned>(nbk), static_cast<unsigned>(std::min<long long>(mb, 65535)), 1);
-    kernel<<<grid, 256, kF64SmemBytes, stream>>>(s, a_vec ? 1 : 0, b_vec ? 1 : 0, po);
+    const long long grid = std::min<long long>(mb * nbk, ds->sms);
+    kernel<<<static_cast<unsigned>(grid), 256, kF64PeerSmemBytes, stream>>>(
+        s, a_vec ? 1 : 0, b_vec ? 1 : 0, po);
     const cudaError_t err = cudaGetLastError();
     if (err == cudaSuccess) {
         t_info.builtin_matmul_calls++;

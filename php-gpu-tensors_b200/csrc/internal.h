@@ -14,6 +14,7 @@ namespace ptg {
 struct F64PeerOut {
     double *dst[8];
     int ndst;
+    int rot;              // this rank: destination (rot + i) % ndst is stored i-th
     long long ldc;
     long long col_off;
 };

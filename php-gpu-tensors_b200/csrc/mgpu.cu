@@ -424,6 +424,7 @@ PT_API int gemm_mgpu_nsplit_matmul_fused(gemm_mgpu_window *win, dtype_t dtype, c
     for (int g = 0; g < G; g++)
         po.dst[g] = static_cast<double *>(win->peer[g]);
     po.ndst = G;
+    po.rot = comm->rank;
     po.ldc = N;
     po.col_off = static_cast<long long>(comm->rank) * (N / G);
     const cudaError_t err = ptg_launch_f64_peer(
