@@ -791,8 +791,10 @@ def measure_workload(ctx, name, args, with_e2e):
         torch.cuda.synchronize()
         e2e_ms = ctx.max(start.elapsed_time(stop))
         e2e = {"value": flop_rank * ctx.world * e2e_steps / (e2e_ms / 1e3) / 1e12,
-               "unit": "TFLOP/s", "h2d_bytes_per_step": wl["h2d"],
-               "d2h_bytes_per_step": wl["d2h"], "steps": e2e_steps, "api": wl["api"]}
+               "unit": "TFLOP/s", "h2d_bytes_per_step": wl["h2d"] * ctx.world,
+               "d2h_bytes_per_step": wl["d2h"] * ctx.world,
+               "h2d_bytes_per_rank": wl["h2d"], "d2h_bytes_per_rank": wl["d2h"],
+               "steps": e2e_steps, "api": wl["api"]}
 
     # Multi-launch steps: every launch timed on its own (CUDA events on the
     # launching stream, L2 flushed before each step as in the timed region);

@@ -261,6 +261,28 @@ def test_float64_dmma(case):
     check_fp64(c.to_numpy(), a, b, name)
 
 
+def test_float64_half_tile_tail_is_bit_identical():
+    """A launch whose last wave would be at most half full runs that wave's
+    tiles as 128 x 64 halves.  Every output element sees the same k order in
+    either width, so one 8192 x 1024 product (512 tiles: 444 full, 68 as
+    halves on 148 SMs) equals, bit for bit, the same product as batch 0 of a
+    2-batch launch (1024 tiles, no halves), and matches the oracle."""
+    M, N, K = 8192, 1024, 512
+    av = O.seeded([M, K], 60, "uniform").astype(np.float64)
+    bv = O.seeded([K, N], 61, "uniform").astype(np.float64)
+    a, b = O.dense(av, [M, K]), O.dense(bv, [K, N])
+    single = to_device(a, "float64").matmul(to_device(b, "float64"), allow_float64=True)
+    assert P.cuda_get_backend_info()["kernel"] == "dmma-f64-128x128"
+    a2 = O.dense(np.concatenate([av, av]), [2, M, K])
+    b2 = O.dense(np.concatenate([bv, bv]), [2, K, N])
+    pair = to_device(a2, "float64").matmul(to_device(b2, "float64"), allow_float64=True)
+    s_out = single.to_numpy().reshape(-1)
+    p_out = pair.to_numpy().reshape(2, -1)
+    assert np.array_equal(s_out, p_out[0]) and np.array_equal(s_out, p_out[1])
+    for row in (0, 5000, M - 1):
+        check_fp64(s_out[row * N:(row + 1) * N], a, b, row, row * N, N)
+
+
 def test_config5b_fp64_full_size_sampled():
     """float64 [8192,8192] x [8192,8192], U[-1,1): the single-GPU product (each
     rank's N-split column block is a slice of it) on sampled rows."""

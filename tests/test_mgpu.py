@@ -176,6 +176,21 @@ def _nccl_worker(rank, world, port, q):
                 results[("oracle", call)] = good
             dist.barrier()
         win.close()
+        # ragged edges: partial row and column tiles in every rank's block
+        Mr, Nr, Kr = 1000, 1200, 776
+        g = torch.Generator(device="cuda").manual_seed(21)
+        a = torch.rand(Mr, Kr, device="cuda", generator=g, dtype=torch.float64) - 0.5
+        b = torch.rand(Kr, Nr, device="cuda", generator=g, dtype=torch.float64) - 0.5
+        lo, hi = P.nsplit_columns(Nr, rank, world)
+        bl = b[:, lo:hi].contiguous()
+        full = P.CudaArray.from_torch(a).matmul(P.CudaArray.from_torch(b),
+                                                allow_float64=True).to_torch()
+        win = P.MgpuWindow(comm, Mr, Nr)
+        f = P.nsplit_matmul_fused(win, P.CudaArray.from_torch(a), P.CudaArray.from_torch(bl))
+        torch.cuda.synchronize()
+        results[("fused_ragged", 0)] = bool(torch.equal(f, full))
+        dist.barrier()
+        win.close()
         q.put((rank, results))
     finally:
         if comm is not None:
