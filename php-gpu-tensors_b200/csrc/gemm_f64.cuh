@@ -8,6 +8,13 @@
 // distinct banks.  A K-contiguous A and an N-contiguous B with 16-byte aligned
 // rows use 16-byte cp.async copies with zero fill at the edges; any other
 // layout goes through the same ring with element loads.
+//
+// Tail: when the tiles of a launch leave the last wave of CTAs at most half
+// full, its tiles run as two 128 x 64 halves each (8 warps in a 4 x 2 grid of
+// 32 x 32 blocks), so that wave takes half as long.  Every output element
+// sees the same sequence of k4 steps in either tile width, so the results are
+// bit-identical.  (8192 x 1024 x 8192, the column block of one rank of an
+// 8-way N-split, is 512 tiles: three full waves of 148 and 68 tiles left.)
 #pragma once
 
 #include "gemm_simt.cuh"
@@ -16,12 +23,6 @@
 namespace ptg {
 
 constexpr int kF64BM = 128, kF64BN = 128, kF64BK = 16;
-// Tiles run in groups of kF64GroupM row blocks, row block fastest: the CTAs
-// resident at one time share a few A row blocks and B column blocks, so the
-// operands of a large product come from DRAM a few times instead of once
-// per resident row of tiles (8192^3 with the row-major tile order read
-// 15.8 GB for 1.6 GB of operands).
-constexpr int kF64GroupM = 16;
 constexpr int kF64Stages = 3;
 constexpr int kF64PitchA = kF64BK + 4;    // doubles per A row in shared memory
 constexpr int kF64PitchB = kF64BN + 4;    // doubles per B row
@@ -51,57 +52,58 @@ __device__ __forceinline__ void dmma_16x8x4(double (&d)[4], const double (&a)[2]
         : "d"(a[0]), "d"(a[1]), "d"(b));
 }
 
-// Ring stage geometry for a k-block depth BK (16 for the plain kernel, 8
-// for the N-split peer kernel): A rows pitched BK + 4 doubles and B rows
-// kF64PitchB doubles, so every fragment read of a half-warp hits distinct
-// banks.
-template <int BK>
-struct F64Stage {
-    static constexpr int kPitchA = BK + 4;
-    static constexpr int kA = kF64BM * kPitchA;   // doubles
-    static constexpr int kB = BK * kF64PitchB;
+// Tile geometry: WN warps along N (4: the full 128 x 128 tile, warps 2 x 4
+// of 64 x 32; 2: the 128 x 64 half tile, warps 4 x 2 of 32 x 32).
+template <int WN>
+struct F64Tile {
+    static constexpr int kWarpsM = 8 / WN;
+    static constexpr int TJ = 4;                         // n8 fragments per warp
+    static constexpr int kWarpN = TJ * 8;                // 32 columns per warp
+    static constexpr int kWarpM = kF64BM / kWarpsM;      // 64 or 32 rows per warp
+    static constexpr int TI = kWarpM / 16;               // m16 fragments per warp
+    static constexpr int BN = WN * kWarpN;               // 128 or 64
 };
 
-// Fills one ring stage with the A tile [m0, m0+128) x [k0, k0+BK) and the B
-// tile [k0, k0+BK) x [n0, n0+128).
-template <int BK>
-__device__ __forceinline__ void f64_load_stage_k(const SimtParams &p, double *sa, double *sb,
-                                                 long long oa, long long ob, int m0, int n0,
-                                                 int k0, bool a_vec, bool b_vec)
+// Fills one ring stage with the A tile [m0, m0+128) x [k0, k0+16) and the B
+// tile [k0, k0+16) x [n0, n0+BN).
+template <int BN>
+__device__ __forceinline__ void f64_load_stage(const SimtParams &p, double *sa, double *sb,
+                                               long long oa, long long ob, int m0, int n0, int k0,
+                                               bool a_vec, bool b_vec)
 {
-    constexpr int kPitchA = F64Stage<BK>::kPitchA;
     const double *A = static_cast<const double *>(p.a);
     const double *B = static_cast<const double *>(p.b);
     const int tid = threadIdx.x;
     if (a_vec) {
-        // 128 rows x BK / 2 pairs of k
+        // 128 rows x 8 pairs of k
 #pragma unroll
-        for (int r = 0; r < BK / 4; r++) {
+        for (int r = 0; r < 4; r++) {
             const int e = tid + 256 * r;
-            const int row = e / (BK / 2), kp = (e % (BK / 2)) * 2;
+            const int row = e >> 3, kp = (e & 7) * 2;
             const int m = m0 + row, k = k0 + kp;
             const bool ok = m < p.M && k < p.K;   // K even: a pair is all in or all out
             const double *src = ok ? A + oa + static_cast<long long>(m) * p.a_sm + k : A;
-            cp_async16(sa + row * kPitchA + kp, src, ok);
+            cp_async16(sa + row * kF64PitchA + kp, src, ok);
         }
     } else {
 #pragma unroll
-        for (int r = 0; r < BK / 2; r++) {
+        for (int r = 0; r < 8; r++) {
             const int e = tid + 256 * r;
-            const int row = e / BK, kk = e % BK;
+            const int row = e >> 4, kk = e & 15;
             const int m = m0 + row, k = k0 + kk;
-            sa[row * kPitchA + kk] =
+            sa[row * kF64PitchA + kk] =
                 (m < p.M && k < p.K) ? A[oa + static_cast<long long>(m) * p.a_sm +
                                          static_cast<long long>(k) * p.a_sk]
                                      : 0.0;
         }
     }
+    constexpr int kPairs = BN / 2;   // pairs of n per k row
     if (b_vec) {
-        // BK k rows x 64 pairs of n
+        // 16 k rows x BN / 2 pairs of n
 #pragma unroll
-        for (int r = 0; r < BK / 4; r++) {
+        for (int r = 0; r < kF64BK * kPairs / 256; r++) {
             const int e = tid + 256 * r;
-            const int kr = e >> 6, np = (e & 63) * 2;
+            const int kr = e / kPairs, np = (e % kPairs) * 2;
             const int k = k0 + kr, n = n0 + np;
             const bool ok = k < p.K && n < p.N;   // N even: a pair is all in or all out
             const double *src = ok ? B + ob + static_cast<long long>(k) * p.b_sk + n : B;
@@ -109,9 +111,9 @@ __device__ __forceinline__ void f64_load_stage_k(const SimtParams &p, double *sa
         }
     } else {
 #pragma unroll
-        for (int r = 0; r < BK / 2; r++) {
+        for (int r = 0; r < kF64BK * BN / 256; r++) {
             const int e = tid + 256 * r;
-            const int kr = e >> 7, col = e & 127;
+            const int kr = e / BN, col = e % BN;
             const int k = k0 + kr, n = n0 + col;
             sb[kr * kF64PitchB + col] =
                 (k < p.K && n < p.N) ? B[ob + static_cast<long long>(k) * p.b_sk +
@@ -121,41 +123,34 @@ __device__ __forceinline__ void f64_load_stage_k(const SimtParams &p, double *sa
     }
 }
 
-__device__ __forceinline__ void f64_load_stage(const SimtParams &p, double *sa, double *sb,
-                                               long long oa, long long ob, int m0, int n0, int k0,
-                                               bool a_vec, bool b_vec)
-{
-    f64_load_stage_k<kF64BK>(p, sa, sb, oa, ob, m0, n0, k0, a_vec, b_vec);
-}
-
-// One k-block of MMAs of a warp's 64 x 32 block: BK / 4 k4 steps of 4 x 4
-// m16n8 fragments.
-template <int BK = kF64BK>
-__device__ __forceinline__ void f64_mma_kblock(double (&acc)[4][4][4], const double *sa,
+// One k-block of MMAs of a warp's block: 4 k4 steps of TI x TJ m16n8
+// fragments.
+template <int TI, int TJ>
+__device__ __forceinline__ void f64_mma_kblock(double (&acc)[TI][TJ][4], const double *sa,
                                                const double *sb, int wm, int wn, int g, int t)
 {
-    constexpr int kPitchA = F64Stage<BK>::kPitchA;
 #pragma unroll
-    for (int kk = 0; kk < BK; kk += 4) {
-        double af[4][2], bf[4];
+    for (int kk = 0; kk < kF64BK; kk += 4) {
+        double af[TI][2], bf[TJ];
 #pragma unroll
-        for (int i = 0; i < 4; i++) {
-            af[i][0] = sa[(wm + i * 16 + g) * kPitchA + kk + t];
-            af[i][1] = sa[(wm + i * 16 + g + 8) * kPitchA + kk + t];
+        for (int i = 0; i < TI; i++) {
+            af[i][0] = sa[(wm + i * 16 + g) * kF64PitchA + kk + t];
+            af[i][1] = sa[(wm + i * 16 + g + 8) * kF64PitchA + kk + t];
         }
 #pragma unroll
-        for (int j = 0; j < 4; j++)
+        for (int j = 0; j < TJ; j++)
             bf[j] = sb[(kk + t) * kF64PitchB + wn + j * 8 + g];
 #pragma unroll
-        for (int i = 0; i < 4; i++)
+        for (int i = 0; i < TI; i++)
 #pragma unroll
-            for (int j = 0; j < 4; j++)
+            for (int j = 0; j < TJ; j++)
                 dmma_16x8x4(acc[i][j], af[i], bf[j]);
     }
 }
 
-// Tile (mb, nb) of tile index L in the grouped order: kF64GroupM row blocks
-// per group, row block fastest.
+// Persistent peer kernel's order of the full tiles: groups of kF64GroupM row
+// blocks, row block fastest (rank-2 products, one batch).
+constexpr int kF64GroupM = 16;
 __device__ __forceinline__ void f64_grouped_tile(long long L, int m_blocks, int n_blocks,
                                                  int &mb, int &nb)
 {
@@ -168,9 +163,148 @@ __device__ __forceinline__ void f64_grouped_tile(long long L, int m_blocks, int 
     nb = static_cast<int>(r / gm);
 }
 
-// The plain product into p.c (optional bias / activation).
+// A launch's work list: `full` tiles of 128 x 128 in row-major tile order
+// (column block fastest, then row block, then batch), then, when the last
+// wave is at most half full, its tiles as 2 x `tail` half tiles.
+struct F64Work {
+    long long full;
+    long long tail;       // tiles run as two halves each (0 = none)
+    int m_blocks, n_blocks;
+};
+
+__host__ __device__ inline F64Work f64_work(int M, int N, long long batches, long long ctas)
+{
+    F64Work w;
+    w.m_blocks = (M + kF64BM - 1) / kF64BM;
+    w.n_blocks = (N + kF64BN - 1) / kF64BN;
+    const long long tiles = batches * w.m_blocks * w.n_blocks;
+    const long long rem = ctas > 0 ? tiles % ctas : 0;
+    w.tail = (rem > 0 && 2 * rem <= ctas) ? rem : 0;
+    w.full = tiles - w.tail;
+    return w;
+}
+
+// Runs the k loop of tile (batch, mb, nb) -- the half `half` of it when
+// WN == 2 -- into acc, calling hook(kb) after each k-block's MMAs.
+template <int WN, typename Hook>
+__device__ __forceinline__ void f64_tile_mainloop(
+    const SimtParams &p, double *sa_all, double *sb_all, long long oa, long long ob, int m0,
+    int n0, bool a_vec, bool b_vec, double (&acc)[F64Tile<WN>::TI][F64Tile<WN>::TJ][4],
+    Hook &&hook)
+{
+    using T = F64Tile<WN>;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int g = lane >> 2, t = lane & 3;
+    const int wm = (warp / WN) * T::kWarpM, wn = (warp % WN) * T::kWarpN;
+    const int k_blocks = (p.K + kF64BK - 1) / kF64BK;
+#pragma unroll
+    for (int i = 0; i < T::TI; i++)
+#pragma unroll
+        for (int j = 0; j < T::TJ; j++)
+#pragma unroll
+            for (int r = 0; r < 4; r++)
+                acc[i][j][r] = 0.0;
+    __syncthreads();   // the previous tile's readers are done with the ring
+#pragma unroll
+    for (int s = 0; s < kF64Stages - 1; s++) {
+        if (s < k_blocks)
+            f64_load_stage<T::BN>(p, sa_all + s * kF64StageA, sb_all + s * kF64StageB, oa, ob,
+                                  m0, n0, s * kF64BK, a_vec, b_vec);
+        cp_async_commit();
+    }
+    for (int kb = 0; kb < k_blocks; kb++) {
+        cp_async_wait<kF64Stages - 2>();
+        __syncthreads();
+        const int nxt = kb + kF64Stages - 1;
+        if (nxt < k_blocks)
+            f64_load_stage<T::BN>(p, sa_all + (nxt % kF64Stages) * kF64StageA,
+                                  sb_all + (nxt % kF64Stages) * kF64StageB, oa, ob, m0, n0,
+                                  nxt * kF64BK, a_vec, b_vec);
+        cp_async_commit();
+        f64_mma_kblock<T::TI, T::TJ>(acc, sa_all + (kb % kF64Stages) * kF64StageA,
+                                     sb_all + (kb % kF64Stages) * kF64StageB, wm, wn, g, t);
+        hook(kb, k_blocks);
+    }
+    cp_async_wait<0>();
+}
+
+// Origin of work unit u: a full tile for u < w.full, else half (u - full) % 2
+// of tile full + (u - full) / 2.  Returns the tile width (128 or 64).
+__device__ __forceinline__ int f64_unit(const F64Work &w, long long u, long long &batch, int &m0,
+                                        int &n0)
+{
+    long long tile = u;
+    int half = -1;
+    if (u >= w.full) {
+        tile = w.full + (u - w.full) / 2;
+        half = static_cast<int>((u - w.full) % 2);
+    }
+    const long long per_batch = static_cast<long long>(w.m_blocks) * w.n_blocks;
+    batch = tile / per_batch;
+    const long long r = tile - batch * per_batch;
+    m0 = static_cast<int>(r / w.n_blocks) * kF64BM;
+    n0 = static_cast<int>(r % w.n_blocks) * kF64BN + (half > 0 ? kF64BN / 2 : 0);
+    return half < 0 ? kF64BN : kF64BN / 2;
+}
+
+__device__ __forceinline__ void f64_batch_offsets(const SimtParams &p, long long batch,
+                                                  long long &oa, long long &ob, long long &oc)
+{
+    oa = ob = oc = 0;
+    long long rem = batch;
+    for (int d = p.nbd - 1; d >= 0; d--) {
+        const long long coord = rem % p.bshape[d];
+        rem /= p.bshape[d];
+        oa += coord * p.a_bs[d];
+        ob += coord * p.b_bs[d];
+        oc += coord * p.c_bs[d];
+    }
+}
+
+// The plain product into p.c (optional bias / activation): one CTA per work
+// unit of f64_work(M, N, batches, resident CTAs).
+template <int WN>
+__device__ __forceinline__ void f64_plain_unit(const SimtParams &p, double *sa_all,
+                                               double *sb_all, long long batch, int m0, int n0,
+                                               bool a_vec, bool b_vec)
+{
+    using T = F64Tile<WN>;
+    long long oa, ob, oc;
+    f64_batch_offsets(p, batch, oa, ob, oc);
+    double acc[T::TI][T::TJ][4];
+    f64_tile_mainloop<WN>(p, sa_all, sb_all, oa, ob, m0, n0, a_vec, b_vec, acc,
+                          [](int, int) {});
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int g = lane >> 2, t = lane & 3;
+    const int wm = (warp / WN) * T::kWarpM, wn = (warp % WN) * T::kWarpN;
+    double *C = static_cast<double *>(p.c);
+    const double *bias = static_cast<const double *>(p.bias);
+#pragma unroll
+    for (int i = 0; i < T::TI; i++)
+#pragma unroll
+        for (int j = 0; j < T::TJ; j++)
+#pragma unroll
+            for (int r = 0; r < 4; r++) {
+                const int m = m0 + wm + i * 16 + g + (r >> 1) * 8;
+                const int n = n0 + wn + j * 8 + t * 2 + (r & 1);
+                if (m < p.M && n < p.N) {
+                    double v = acc[i][j][r];
+                    if (bias != nullptr || p.act != ACT_NONE) {
+                        if (bias != nullptr) v += bias[n];
+                        v = apply_activation_d(v, p.act);
+                    }
+                    C[oc + static_cast<long long>(m) * p.c_sm + static_cast<long long>(n) * p.c_sn] = v;
+                }
+            }
+}
+
+// Full tiles: grid (column blocks, row blocks, batches), each CTA walking
+// row blocks and batches by the grid's extents (more than 65535 of either);
+// tiles from w.full on (row-major tile index) are left to the half-tile
+// launch.  The loop form measured 1-3 % faster than one tile per CTA
+// through f64_plain_unit on B200 (8192^3 and 4096^3).
 __global__ void __launch_bounds__(256, 1)
-    f64_dmma_kernel(const SimtParams p, int a_vec, int b_vec)
+    f64_dmma_kernel(const SimtParams p, int a_vec, int b_vec, const F64Work w)
 {
     extern __shared__ __align__(16) double f64_smem[];
     double *sa_all = f64_smem;
@@ -179,29 +313,17 @@ __global__ void __launch_bounds__(256, 1)
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int g = lane >> 2, t = lane & 3;
     const int wm = (warp >> 2) * 64, wn = (warp & 3) * 32;
-    const int m_blocks = (p.M + kF64BM - 1) / kF64BM;
+    const int m_blocks = w.m_blocks;
     const int k_blocks = (p.K + kF64BK - 1) / kF64BK;
-    // grouped tile order when the grid covers every row block (the launch
-    // grid is (column blocks, row blocks, batches), x fastest)
-    int mb_first = blockIdx.y, nb = blockIdx.x, mb_step = gridDim.y;
-    if (static_cast<int>(gridDim.y) == m_blocks) {
-        f64_grouped_tile(static_cast<long long>(blockIdx.y) * gridDim.x + blockIdx.x, m_blocks,
-                         gridDim.x, mb_first, nb);
-        mb_step = m_blocks;
-    }
-    const int n0 = nb * kF64BN;
+    const int n0 = blockIdx.x * kF64BN;
 
     for (long long batch = blockIdx.z; batch < p.batches; batch += gridDim.z)
-    for (int mb = mb_first; mb < m_blocks; mb += mb_step) {
+    for (int mb = blockIdx.y; mb < m_blocks; mb += gridDim.y) {
+        if ((batch * m_blocks + mb) * w.n_blocks + blockIdx.x >= w.full)
+            continue;
         const int m0 = mb * kF64BM;
-        long long oa = 0, ob = 0, oc = 0, rem = batch;
-        for (int d = p.nbd - 1; d >= 0; d--) {
-            const long long coord = rem % p.bshape[d];
-            rem /= p.bshape[d];
-            oa += coord * p.a_bs[d];
-            ob += coord * p.b_bs[d];
-            oc += coord * p.c_bs[d];
-        }
+        long long oa, ob, oc;
+        f64_batch_offsets(p, batch, oa, ob, oc);
         double acc[4][4][4];
 #pragma unroll
         for (int i = 0; i < 4; i++)
@@ -215,8 +337,8 @@ __global__ void __launch_bounds__(256, 1)
 #pragma unroll
         for (int s = 0; s < kF64Stages - 1; s++) {
             if (s < k_blocks)
-                f64_load_stage(p, sa_all + s * kF64StageA, sb_all + s * kF64StageB, oa, ob, m0,
-                               n0, s * kF64BK, a_vec, b_vec);
+                f64_load_stage<kF64BN>(p, sa_all + s * kF64StageA, sb_all + s * kF64StageB, oa,
+                                       ob, m0, n0, s * kF64BK, a_vec, b_vec);
             cp_async_commit();
         }
         for (int kb = 0; kb < k_blocks; kb++) {
@@ -224,12 +346,12 @@ __global__ void __launch_bounds__(256, 1)
             __syncthreads();
             const int nxt = kb + kF64Stages - 1;
             if (nxt < k_blocks)
-                f64_load_stage(p, sa_all + (nxt % kF64Stages) * kF64StageA,
-                               sb_all + (nxt % kF64Stages) * kF64StageB, oa, ob, m0, n0,
-                               nxt * kF64BK, a_vec, b_vec);
+                f64_load_stage<kF64BN>(p, sa_all + (nxt % kF64Stages) * kF64StageA,
+                                       sb_all + (nxt % kF64Stages) * kF64StageB, oa, ob, m0, n0,
+                                       nxt * kF64BK, a_vec, b_vec);
             cp_async_commit();
-            f64_mma_kblock(acc, sa_all + (kb % kF64Stages) * kF64StageA,
-                           sb_all + (kb % kF64Stages) * kF64StageB, wm, wn, g, t);
+            f64_mma_kblock<4, 4>(acc, sa_all + (kb % kF64Stages) * kF64StageA,
+                                 sb_all + (kb % kF64Stages) * kF64StageB, wm, wn, g, t);
         }
         cp_async_wait<0>();
 
@@ -255,60 +377,132 @@ __global__ void __launch_bounds__(256, 1)
     }
 }
 
+// The last wave's tiles as halves: one CTA per half tile, units
+// w.full + [0, 2 w.tail).
+__global__ void __launch_bounds__(256, 1)
+    f64_dmma_half_kernel(const SimtParams p, int a_vec, int b_vec, const F64Work w)
+{
+    extern __shared__ __align__(16) double f64_smem[];
+    long long batch;
+    int m0, n0;
+    f64_unit(w, w.full + blockIdx.x, batch, m0, n0);
+    f64_plain_unit<2>(p, f64_smem, f64_smem + kF64Stages * kF64StageA, batch, m0, n0, a_vec,
+                      b_vec);
+}
+
 // ---------------------------------------------------------------------------
 // The N-split block product whose results go to every rank's window over
-// NVLink (rank-2 operands, no batch).  Persistent: one CTA per SM walks the
-// tiles in the grouped order with the plain kernel's ring.  When a tile's k
-// loop ends, the CTA writes the tile into this rank's own window (local HBM,
-// fragment layout), and during the NEXT tile's k loop every thread copies a
-// few 16-byte pieces of it per k-block from there to the other ranks'
-// windows, the next rank first and so on around the ring, so every rank
-// spreads its traffic over all peers and the NVLink transfer runs under the
-// DMMA work instead of after it.  (A non-persistent kernel that stored each
-// tile to every window when it finished held each wave's SMs idle during the
-// stores; staging the tile in shared memory instead left room only for a ring
-// of 2 x 16-deep or 4 x 8-deep k-blocks, which slowed the math by 4-13 %.)
-// Only the last tile of each CTA is copied after the math.
+// NVLink (rank-2 operands, no batch).  Persistent: CTA c of the grid takes
+// units c, c + grid, ...; the full tiles run in groups of kF64GroupM row
+// blocks, row block fastest, which kept the CTAs' working set in L2 better
+// than the row-major order here (8192^3 on one GPU: 1.5 % against 4 % over
+// the plain kernel; taking units from an atomic counter in row-major order
+// instead measured 13 % over).  When a unit's k loop ends, the CTA writes its tile into this
+// rank's own window (local HBM, fragment layout), and during the NEXT unit's
+// k loop every thread copies a few 16-byte pieces of it per k-block from
+// there to the other ranks' windows, the next rank first and so on around
+// the ring, so every rank spreads its traffic over all peers and the NVLink
+// transfer runs under the DMMA work instead of after it.  (A non-persistent
+// kernel that stored each tile to every window when it finished held each
+// wave's SMs idle during the stores; staging the tile in shared memory
+// instead left room only for a ring of 2 x 16-deep or 4 x 8-deep k-blocks,
+// which slowed the math by 4-13 %.)  Only each CTA's last unit is copied
+// after the math.
 constexpr int kF64PeerSmemBytes = kF64SmemBytes;
-// 16-byte pieces of one tile per thread
-constexpr int kF64PeerPieces = kF64BM * (kF64BN / 2) / 256;
+
+// Pending remote copies of the last finished unit: its origin and width.
+struct F64Pending {
+    int m0, n0, width;
+    int done, ops;
+};
+
+// Issues copy number e of the pending unit: piece e / peers of the unit
+// (consecutive threads on consecutive 16-byte column pairs of a row) to
+// destination rank (rot + 1 + e % peers) % ndst.
+__device__ __forceinline__ void f64_copy_piece(const SimtParams &p, const F64PeerOut &po,
+                                               const F64Pending &q, int e)
+{
+    const int peers = po.ndst - 1;
+    const int d = (po.rot + 1 + e % peers) % po.ndst;
+    const int pairs = q.width / 2;
+    const int idx = threadIdx.x + 256 * (e / peers);
+    const int row = idx / pairs, pair = idx % pairs;
+    const int m = q.m0 + row, n = q.n0 + 2 * pair;
+    if (m < p.M && n < p.N) {
+        const long long off = static_cast<long long>(m) * po.ldc + po.col_off + n;
+        const double2 v = __ldcg(reinterpret_cast<const double2 *>(po.dst[po.rot] + off));
+        *reinterpret_cast<double2 *>(po.dst[d] + off) = v;
+    }
+}
+
+template <int WN>
+__device__ __forceinline__ void f64_peer_unit(const SimtParams &p, const F64PeerOut &po,
+                                              double *sa_all, double *sb_all, int m0, int n0,
+                                              bool a_vec, bool b_vec, F64Pending &q)
+{
+    using T = F64Tile<WN>;
+    double acc[T::TI][T::TJ][4];
+    // a share of the previous unit's remote copies after each k-block,
+    // spread evenly over the k loop
+    f64_tile_mainloop<WN>(p, sa_all, sb_all, 0, 0, m0, n0, a_vec, b_vec, acc,
+                          [&](int kb, int k_blocks) {
+                              const int target = static_cast<int>(
+                                  (static_cast<long long>(kb + 1) * q.ops + k_blocks - 1) /
+                                  k_blocks);
+                              for (; q.done < target; q.done++)
+                                  f64_copy_piece(p, po, q, q.done);
+                          });
+    for (; q.done < q.ops; q.done++)
+        f64_copy_piece(p, po, q, q.done);
+    // this unit into the rank's own window
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int g = lane >> 2, t = lane & 3;
+    const int wm = (warp / WN) * T::kWarpM, wn = (warp % WN) * T::kWarpN;
+    double *own = po.dst[po.rot];
+#pragma unroll
+    for (int i = 0; i < T::TI; i++)
+#pragma unroll
+        for (int j = 0; j < T::TJ; j++)
+#pragma unroll
+            for (int r = 0; r < 4; r += 2) {
+                const int m = m0 + wm + i * 16 + g + (r >> 1) * 8;
+                const int n = n0 + wn + j * 8 + t * 2;
+                if (m < p.M && n < p.N)
+                    *reinterpret_cast<double2 *>(own + static_cast<long long>(m) * po.ldc +
+                                                 po.col_off + n) =
+                        make_double2(acc[i][j][r], acc[i][j][r + 1]);
+            }
+    __syncthreads();   // the unit is in the own window for every thread's copies
+    q.m0 = m0;
+    q.n0 = n0;
+    q.width = T::BN;
+    q.done = 0;
+    q.ops = (po.ndst - 1) * (kF64BM * T::BN / 2 / 256);
+}
 
 __global__ void __launch_bounds__(256, 1)
-    f64_dmma_peer_kernel(const SimtParams p, int a_vec, int b_vec, const F64PeerOut po)
+    f64_dmma_peer_kernel(const SimtParams p, int a_vec, int b_vec, const F64PeerOut po,
+                         const F64Work w)
 {
     extern __shared__ __align__(16) double f64_smem[];
     double *sa_all = f64_smem;
     double *sb_all = f64_smem + kF64Stages * kF64StageA;
-
+    F64Pending q;
+    q.m0 = q.n0 = 0;
+    q.width = kF64BN;
+    q.done = q.ops = 0;
+    const long long units = w.full + 2 * w.tail;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int g = lane >> 2, t = lane & 3;
     const int wm = (warp >> 2) * 64, wn = (warp & 3) * 32;
-    const int m_blocks = (p.M + kF64BM - 1) / kF64BM;
-    const int n_blocks = (p.N + kF64BN - 1) / kF64BN;
     const int k_blocks = (p.K + kF64BK - 1) / kF64BK;
-    const long long tiles = static_cast<long long>(m_blocks) * n_blocks;
     double *own = po.dst[po.rot];
-    const int peers = po.ndst - 1;
-    const int ops = kF64PeerPieces * peers;   // remote copies per thread and tile
-
-    // origin of the tile whose remote copies are pending, and how many of
-    // them this thread has issued
-    int pm0 = 0, pn0 = 0, done = ops;
-    auto copy_op = [&](int e) {
-        const int d = (po.rot + 1 + e % peers) % po.ndst;
-        const int idx = threadIdx.x + 256 * (e / peers);
-        const int row = idx / (kF64BN / 2), pair = idx % (kF64BN / 2);
-        const int m = pm0 + row, n = pn0 + 2 * pair;
-        if (m < p.M && n < p.N) {
-            const long long off = static_cast<long long>(m) * po.ldc + po.col_off + n;
-            const double2 v = __ldcg(reinterpret_cast<const double2 *>(own + off));
-            *reinterpret_cast<double2 *>(po.dst[d] + off) = v;
-        }
-    };
-
-    for (long long L = blockIdx.x; L < tiles; L += gridDim.x) {
+    // full tiles: the plain kernel's loop body (written out here rather than
+    // through f64_tile_mainloop, which measured a few % slower), with the
+    // previous unit's remote copies after each k-block
+    for (long long u = blockIdx.x; u < w.full; u += gridDim.x) {
         int mb, nb;
-        f64_grouped_tile(L, m_blocks, n_blocks, mb, nb);
+        f64_grouped_tile(u, w.m_blocks, w.n_blocks, mb, nb);
         const int m0 = mb * kF64BM, n0 = nb * kF64BN;
         double acc[4][4][4];
 #pragma unroll
@@ -323,8 +517,8 @@ __global__ void __launch_bounds__(256, 1)
 #pragma unroll
         for (int s = 0; s < kF64Stages - 1; s++) {
             if (s < k_blocks)
-                f64_load_stage(p, sa_all + s * kF64StageA, sb_all + s * kF64StageB, 0, 0, m0,
-                               n0, s * kF64BK, a_vec, b_vec);
+                f64_load_stage<kF64BN>(p, sa_all + s * kF64StageA, sb_all + s * kF64StageB, 0, 0,
+                                       m0, n0, s * kF64BK, a_vec, b_vec);
             cp_async_commit();
         }
         for (int kb = 0; kb < k_blocks; kb++) {
@@ -332,23 +526,20 @@ __global__ void __launch_bounds__(256, 1)
             __syncthreads();
             const int nxt = kb + kF64Stages - 1;
             if (nxt < k_blocks)
-                f64_load_stage(p, sa_all + (nxt % kF64Stages) * kF64StageA,
-                               sb_all + (nxt % kF64Stages) * kF64StageB, 0, 0, m0, n0,
-                               nxt * kF64BK, a_vec, b_vec);
+                f64_load_stage<kF64BN>(p, sa_all + (nxt % kF64Stages) * kF64StageA,
+                                       sb_all + (nxt % kF64Stages) * kF64StageB, 0, 0, m0, n0,
+                                       nxt * kF64BK, a_vec, b_vec);
             cp_async_commit();
-            f64_mma_kblock(acc, sa_all + (kb % kF64Stages) * kF64StageA,
-                           sb_all + (kb % kF64Stages) * kF64StageB, wm, wn, g, t);
-            // a share of the previous tile's remote copies, spread evenly
-            // over the k loop
+            f64_mma_kblock<4, 4>(acc, sa_all + (kb % kF64Stages) * kF64StageA,
+                                 sb_all + (kb % kF64Stages) * kF64StageB, wm, wn, g, t);
             const int target = static_cast<int>(
-                (static_cast<long long>(kb + 1) * ops + k_blocks - 1) / k_blocks);
-            for (; done < target; done++)
-                copy_op(done);
+                (static_cast<long long>(kb + 1) * q.ops + k_blocks - 1) / k_blocks);
+            for (; q.done < target; q.done++)
+                f64_copy_piece(p, po, q, q.done);
         }
         cp_async_wait<0>();
-        for (; done < ops; done++)
-            copy_op(done);
-        // this tile into the rank's own window
+        for (; q.done < q.ops; q.done++)
+            f64_copy_piece(p, po, q, q.done);
 #pragma unroll
         for (int i = 0; i < 4; i++)
 #pragma unroll
@@ -363,12 +554,24 @@ __global__ void __launch_bounds__(256, 1)
                             make_double2(acc[i][j][r], acc[i][j][r + 1]);
                 }
         __syncthreads();   // the tile is in the own window for every thread's copies
-        pm0 = m0;
-        pn0 = n0;
-        done = 0;
+        q.m0 = m0;
+        q.n0 = n0;
+        q.width = kF64BN;
+        q.done = 0;
+        q.ops = (po.ndst - 1) * (kF64BM * kF64BN / 2 / 256);
     }
-    for (; done < ops; done++)
-        copy_op(done);
+    // the last wave's tiles as halves, when the launch has them: the tiles
+    // from w.full on in the same grouped order
+    for (long long u = w.full + (blockIdx.x + gridDim.x - w.full % gridDim.x) % gridDim.x;
+         u < units; u += gridDim.x) {
+        int mb, nb;
+        f64_grouped_tile(w.full + (u - w.full) / 2, w.m_blocks, w.n_blocks, mb, nb);
+        const int m0 = mb * kF64BM;
+        const int n0 = nb * kF64BN + ((u - w.full) % 2 != 0 ? kF64BN / 2 : 0);
+        f64_peer_unit<2>(p, po, sa_all, sb_all, m0, n0, a_vec, b_vec, q);
+    }
+    for (; q.done < q.ops; q.done++)
+        f64_copy_piece(p, po, q, q.done);
     // make this thread's peer stores visible system-wide before the kernel
     // can be observed complete
     __threadfence_system();

@@ -537,7 +537,9 @@ enum KernelId : int {
     KID_BF16_F32,            // bf16 x bf16 -> float32
     KID_F16_F32,             // f16 x f16 -> float32
     KID_SKINNY_VEC,          // 12 ids: float32 few-column kernel with 16-byte A copies, 2 * NB index + A k-major
+    KID_F64_DMMA_HALF = KID_SKINNY_VEC + 12,   // float64 half tiles of a launch's last wave
 };
+static_assert(KID_F64_DMMA_HALF < 64, "kernel ids index a 64-bit attribute mask");
 
 const char *kernel_name(int kid)
 {
@@ -972,14 +974,21 @@ cudaError_t launch_f64_dmma(const Problem &P, DeviceState *ds, cudaStream_t stre
         a_vec = a_vec && P.a_bs[d] % 2 == 0;
         b_vec = b_vec && P.b_bs[d] % 2 == 0;
     }
-    if (!ensure_smem_attr(ds, KID_F64_DMMA, f64_dmma_kernel, kF64SmemBytes))
+    if (!ensure_smem_attr(ds, KID_F64_DMMA, f64_dmma_kernel, kF64SmemBytes) ||
+        !ensure_smem_attr(ds, KID_F64_DMMA_HALF, f64_dmma_half_kernel, kF64SmemBytes))
         return cudaErrorInvalidConfiguration;
-    const long long mb = (P.M + kF64BM - 1) / kF64BM;
-    const long long nb = (P.N + kF64BN - 1) / kF64BN;
-    dim3 grid(static_cast<unsigned>(std::min<long long>(nb, 2147483647ll)),
-              static_cast<unsigned>(std::min<long long>(mb, 65535)),
-              static_cast<unsigned>(std::min<long long>(P.batches, 65535)));
-    f64_dmma_kernel<<<grid, 256, kF64SmemBytes, stream>>>(s, a_vec ? 1 : 0, b_vec ? 1 : 0);
+    // full tiles, one resident CTA per SM; then -- when the last wave would
+    // be at most half full -- its tiles as half tiles in a second launch
+    const F64Work w = f64_work(P.M, P.N, P.batches, ds->sms);
+    if (w.full > 0) {
+        dim3 grid(static_cast<unsigned>(w.n_blocks),
+                  static_cast<unsigned>(std::min<long long>(w.m_blocks, 65535)),
+                  static_cast<unsigned>(std::min<long long>(P.batches, 65535)));
+        f64_dmma_kernel<<<grid, 256, kF64SmemBytes, stream>>>(s, a_vec ? 1 : 0, b_vec ? 1 : 0, w);
+    }
+    if (w.tail > 0)
+        f64_dmma_half_kernel<<<static_cast<unsigned>(2 * w.tail), 256, kF64SmemBytes, stream>>>(
+            s, a_vec ? 1 : 0, b_vec ? 1 : 0, w);
     return cudaGetLastError();
 }
 
@@ -1379,11 +1388,11 @@ cudaError_t ptg_launch_f64_peer(const double *a, size_t a_s0, size_t a_s1, const
     auto kernel = f64_dmma_peer_kernel;
     if (!ensure_smem_attr(ds, KID_F64_DMMA_PEER, kernel, kF64PeerSmemBytes))
         return cudaErrorInvalidConfiguration;
-    const long long mb = (P.M + kF64BM - 1) / kF64BM;
-    const long long nbk = (P.N + kF64BN - 1) / kF64BN;
-    const long long grid = std::min<long long>(mb * nbk, ds->sms);
+    // persistent: one CTA per SM over the work units (see f64_work)
+    const F64Work w = f64_work(P.M, P.N, 1, ds->sms);
+    const long long grid = std::min<long long>(w.full + 2 * w.tail, ds->sms);
     kernel<<<static_cast<unsigned>(grid), 256, kF64PeerSmemBytes, stream>>>(
-        s, a_vec ? 1 : 0, b_vec ? 1 : 0, po);
+        s, a_vec ? 1 : 0, b_vec ? 1 : 0, po, w);
     const cudaError_t err = cudaGetLastError();
     if (err == cudaSuccess) {
         t_info.builtin_matmul_calls++;

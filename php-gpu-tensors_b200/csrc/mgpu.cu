@@ -321,7 +321,7 @@ struct gemm_mgpu_window {
     void *local;
     size_t bytes;
     void *peer[8];
-    int *sync;   // one int for the completion all-reduce
+    int *sync;   // one int for the ordering all-reduces
 };
 
 PT_API int gemm_mgpu_window_create(gemm_mgpu_comm *comm, size_t bytes, gemm_mgpu_window **win,

@@ -97,6 +97,31 @@ def test_fused_nsplit_single_rank_equals_plain_product():
 
 
 @pytest.mark.gpu
+def test_fused_nsplit_full_and_half_tiles_single_rank():
+    """A column block of 512 tiles (8192 x 1024: one rank's block of an
+    8-way N-split) runs three waves of full tiles and its last 68 tiles as
+    half tiles; every tile must come out once and equal the plain product."""
+    sys.path.insert(0, os.path.join(ROOT, "php-gpu-tensors_b200"))
+    import phptensors as P
+    torch.cuda.set_device(0)
+    g = torch.Generator(device="cuda").manual_seed(7)
+    M, N, K = 8192, 1024, 256
+    a = torch.rand(M, K, device="cuda", generator=g, dtype=torch.float64) - 0.5
+    b = torch.rand(K, N, device="cuda", generator=g, dtype=torch.float64) - 0.5
+    comm = P.MgpuComm(0, 1)
+    win = P.MgpuWindow(comm, M, N)
+    try:
+        for _ in range(2):
+            c = P.nsplit_matmul_fused(win, P.CudaArray.from_torch(a), P.CudaArray.from_torch(b))
+            ref = P.CudaArray.from_torch(a).matmul(P.CudaArray.from_torch(b), allow_float64=True)
+            torch.cuda.synchronize()
+            assert torch.equal(c, ref.to_torch())
+    finally:
+        win.close()
+        comm.close()
+
+
+@pytest.mark.gpu
 def test_nsplit_single_rank_equals_plain_product():
     sys.path.insert(0, os.path.join(ROOT, "php-gpu-tensors_b200"))
     import phptensors as P
