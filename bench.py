@@ -889,21 +889,38 @@ def measure_nsplit(ctx, args):
             raise RuntimeError("launcher failed: %s" % P.cuda_get_backend_info())
 
     results = {}
-    variants = [("fused", lambda: results.__setitem__("fused", P.nsplit_matmul_fused(win, A, Bl))),
+
+    def fused(mode):
+        def run():
+            win.set_exchange(mode)
+            results["fused_" + mode] = P.nsplit_matmul_fused(win, A, Bl)
+        return run
+
+    # the fused entry point's two exchanges (auto picks epilogue stores up to
+    # 4 ranks, copies under the next tile's math above), NCCL, compute alone
+    variants = [("store", fused("store")), ("overlap", fused("overlap")),
                 ("nccl", lambda: results.__setitem__("nccl", P.nsplit_matmul(comm, A, Bl, N, ws))),
                 ("compute", compute_only)]
     flop = 2.0 * M * N * K
     kernel = None
+    compute_kernel = None
+    auto = "store" if world <= 4 else "overlap"
     for vname, fn in variants:
         for _ in range(args.warmup):
             fn()
-        if vname == "fused":
+        if vname == auto:
             kernel = P.cuda_get_backend_info()["kernel"]
+        elif vname == "compute":
+            compute_kernel = P.cuda_get_backend_info()["kernel"]
         ms_local, ms, clocks = ctx.time_region(fn, args.steps)
         ctx.device_status()
+        if vname in ("store", "overlap"):
+            # both write the same window: keep this exchange's result
+            results["fused_" + vname] = results["fused_" + vname].clone()
         out[vname] = {"value": flop * args.steps / (ms / 1e3) / 1e12,
                       "ms_per_step": ms / args.steps, "clocks": clocks}
-    for vname in ("fused", "nccl"):
+    win.set_exchange("auto")
+    for vname in ("fused_store", "fused_overlap", "nccl"):
         c = results[vname]
         c = c if isinstance(c, torch.Tensor) else c.to_torch()
         got = c[rows]
@@ -916,8 +933,9 @@ def measure_nsplit(ctx, args):
         ctx.check("config5b_" + vname, err if same else float("inf"), CHECK_TOL["f64"],
                   {"what": "sampled rows vs cuBLAS float64; identical on every rank",
                    "identical_across_ranks": same})
-    for k in ("fused", "nccl"):
+    for k in ("store", "overlap", "nccl"):
         out[k]["exchange_ms_per_step"] = out[k]["ms_per_step"] - out["compute"]["ms_per_step"]
+    out["fused"] = dict(out[auto], exchange=auto)
     head = out[args.nsplit] if args.workload == "config5b" else out["fused"]
     ctx.barrier()
     win.close()
@@ -934,13 +952,16 @@ def measure_nsplit(ctx, args):
                    "allgather_bytes_received_per_rank": M * (N - (hi - lo)) * 8,
                    "l2": "inputs larger than L2 (%.0f MB)" % ((M * K + K * N + M * N) * 8 / 1e6)},
         "paths": out,
-        "roofline": {"bound": "tensor (DMMA)", "kernel": kernel, "achieved": achieved_c,
+        "roofline": {"bound": "tensor (DMMA)", "kernel": compute_kernel, "achieved": achieved_c,
                      "peak": NOMINAL_FP64_TFLOPS, "unit": "TFLOP/s",
                      "frac": achieved_c / NOMINAL_FP64_TFLOPS,
                      "peak_source": "nominal B200 dense FP64 tensor rate (no measured FP64 peak)",
                      "of": "the local column-block product (compute path)",
-                     "traffic": traffic_for("config5b", kernel)},
+                     "traffic": traffic_for("config5b%s" % ("" if world == 1 else "_x%d" % world),
+                                            compute_kernel)},
         "gpu_launches": args.steps * (1 if args.nsplit == "fused" else 2),
+        "exchange": "fused = %s: epilogue stores up to 4 ranks, copies under the next "
+                    "tile's math above" % auto,
         "clocks": head["clocks"],
         "check": {k: v for k, v in ctx.checks.items() if k.startswith("config5b")},
     }

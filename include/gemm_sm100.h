@@ -310,10 +310,11 @@ int gemm_mgpu_window_create(gemm_mgpu_comm *comm, size_t bytes, gemm_mgpu_window
                             void **local);
 void gemm_mgpu_window_destroy(gemm_mgpu_window *win);
 
-/* The float64 N-split product with the exchange fused into the GEMM: the
- * epilogue of this rank's column-block product stores every finished output
- * row into all ranks' windows at this rank's column offset, so the transfer
- * overlaps the remaining tiles, and no gather buffer or permute exists.
+/* The float64 N-split product with the exchange fused into the GEMM: this
+ * rank's column-block product puts every finished tile into all ranks'
+ * windows at this rank's column offset while the remaining tiles compute
+ * (see gemm_mgpu_window_set_exchange for the two ways), and no gather buffer
+ * or permute exists.
  * After the call's work completes on `stream` (a one-element NCCL all-reduce
  * follows the kernel), every rank's window holds the whole row-major C
  * [M, N].  dtype FLOAT64; N divisible by the rank count with an even block
@@ -331,6 +332,21 @@ int gemm_mgpu_nsplit_matmul_fused(gemm_mgpu_window *win, dtype_t dtype,
                                   const void *a, size_t a_s0, size_t a_s1,
                                   const void *b_local, size_t b_s0, size_t b_s1,
                                   int M, int N, int K, cudaStream_t stream);
+
+/* How gemm_mgpu_nsplit_matmul_fused moves a finished tile into the other
+ * ranks' windows (no counterpart in the reference):
+ *   GEMM_MGPU_EXCHANGE_AUTO (default): epilogue stores up to 4 ranks,
+ *     copies under the next tile's math above that;
+ *   GEMM_MGPU_EXCHANGE_STORE: the tile's epilogue stores its rows into every
+ *     window (one CTA per tile);
+ *   GEMM_MGPU_EXCHANGE_OVERLAP: one persistent CTA per SM writes the tile to
+ *     this rank's window and copies it to the peers during its next tile.
+ * Both give the same bits.  Returns 1, or 0 for an unknown mode or a null
+ * window. */
+#define GEMM_MGPU_EXCHANGE_AUTO 0
+#define GEMM_MGPU_EXCHANGE_STORE 1
+#define GEMM_MGPU_EXCHANGE_OVERLAP 2
+int gemm_mgpu_window_set_exchange(gemm_mgpu_window *win, int mode);
 
 /* Size of the library-owned gather buffer of gemm_mgpu_nsplit_matmul_noalloc:
  * 32 MiB of device memory on every GPU that loads the library, held until the

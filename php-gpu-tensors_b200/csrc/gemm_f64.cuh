@@ -303,8 +303,14 @@ __device__ __forceinline__ void f64_plain_unit(const SimtParams &p, double *sa_a
 // tiles from w.full on (row-major tile index) are left to the half-tile
 // launch.  The loop form measured 1-3 % faster than one tile per CTA
 // through f64_plain_unit on B200 (8192^3 and 4096^3).
+// PEER = false: the plain product into p.c.  PEER = true: the N-split block
+// product (rank-2, one batch) whose epilogue stages the tile in shared
+// memory, half at a time, and stores its rows into every rank's window
+// (16 bytes per thread, consecutive threads on consecutive columns).
+template <bool PEER>
 __global__ void __launch_bounds__(256, 1)
-    f64_dmma_kernel(const SimtParams p, int a_vec, int b_vec, const F64Work w)
+    f64_dmma_kernel(const SimtParams p, int a_vec, int b_vec, const F64Work w,
+                    const F64PeerOut po)
 {
     extern __shared__ __align__(16) double f64_smem[];
     double *sa_all = f64_smem;
@@ -355,6 +361,41 @@ __global__ void __launch_bounds__(256, 1)
         }
         cp_async_wait<0>();
 
+        if constexpr (PEER) {
+            __syncthreads();   // every warp is done with the ring
+            double *st = f64_smem;
+            for (int h = 0; h < 2; h++) {
+                if ((warp >> 2) == h) {
+#pragma unroll
+                    for (int i = 0; i < 4; i++)
+#pragma unroll
+                        for (int j = 0; j < 4; j++)
+#pragma unroll
+                            for (int r = 0; r < 4; r += 2)
+                                *reinterpret_cast<double2 *>(
+                                    st + (i * 16 + g + (r >> 1) * 8) * kF64PitchB + wn + j * 8 +
+                                    t * 2) = make_double2(acc[i][j][r], acc[i][j][r + 1]);
+                }
+                __syncthreads();
+                for (int idx = threadIdx.x; idx < 64 * (kF64BN / 2); idx += 256) {
+                    const int row = idx / (kF64BN / 2), pair = idx % (kF64BN / 2);
+                    const int m = m0 + h * 64 + row, n = n0 + 2 * pair;
+                    if (m < p.M && n < p.N) {
+                        const double2 v = *reinterpret_cast<const double2 *>(
+                            st + row * kF64PitchB + 2 * pair);
+                        const long long off = static_cast<long long>(m) * po.ldc + po.col_off + n;
+                        for (int d = 0; d < po.ndst; d++)
+                            *reinterpret_cast<double2 *>(po.dst[(po.rot + d) % po.ndst] + off) = v;
+                    }
+                }
+                __syncthreads();
+            }
+            // make this thread's peer stores visible system-wide before the
+            // kernel can be observed complete
+            __threadfence_system();
+            continue;
+        }
+
         double *C = static_cast<double *>(p.c);
         const double *bias = static_cast<const double *>(p.bias);
 #pragma unroll
@@ -378,16 +419,45 @@ __global__ void __launch_bounds__(256, 1)
 }
 
 // The last wave's tiles as halves: one CTA per half tile, units
-// w.full + [0, 2 w.tail).
+// w.full + [0, 2 w.tail); PEER as in f64_dmma_kernel (each thread stores its
+// fragment pairs into every window).
+template <bool PEER>
 __global__ void __launch_bounds__(256, 1)
-    f64_dmma_half_kernel(const SimtParams p, int a_vec, int b_vec, const F64Work w)
+    f64_dmma_half_kernel(const SimtParams p, int a_vec, int b_vec, const F64Work w,
+                         const F64PeerOut po)
 {
     extern __shared__ __align__(16) double f64_smem[];
     long long batch;
     int m0, n0;
     f64_unit(w, w.full + blockIdx.x, batch, m0, n0);
-    f64_plain_unit<2>(p, f64_smem, f64_smem + kF64Stages * kF64StageA, batch, m0, n0, a_vec,
-                      b_vec);
+    double *sa_all = f64_smem, *sb_all = f64_smem + kF64Stages * kF64StageA;
+    if constexpr (!PEER) {
+        f64_plain_unit<2>(p, sa_all, sb_all, batch, m0, n0, a_vec, b_vec);
+    } else {
+        using T = F64Tile<2>;
+        double acc[T::TI][T::TJ][4];
+        f64_tile_mainloop<2>(p, sa_all, sb_all, 0, 0, m0, n0, a_vec, b_vec, acc,
+                             [](int, int) {});
+        const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+        const int g = lane >> 2, t = lane & 3;
+        const int wm = (warp / 2) * T::kWarpM, wn = (warp % 2) * T::kWarpN;
+#pragma unroll
+        for (int i = 0; i < T::TI; i++)
+#pragma unroll
+            for (int j = 0; j < T::TJ; j++)
+#pragma unroll
+                for (int r = 0; r < 4; r += 2) {
+                    const int m = m0 + wm + i * 16 + g + (r >> 1) * 8;
+                    const int n = n0 + wn + j * 8 + t * 2;
+                    if (m < p.M && n < p.N) {
+                        const long long off = static_cast<long long>(m) * po.ldc + po.col_off + n;
+                        for (int d = 0; d < po.ndst; d++)
+                            *reinterpret_cast<double2 *>(po.dst[(po.rot + d) % po.ndst] + off) =
+                                make_double2(acc[i][j][r], acc[i][j][r + 1]);
+                    }
+                }
+        __threadfence_system();
+    }
 }
 
 // ---------------------------------------------------------------------------

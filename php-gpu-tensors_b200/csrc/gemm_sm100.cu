@@ -64,6 +64,14 @@ constexpr double kPairTileCost = 1.79;
 // 256 K as in the single-CTA mixed kernel
 constexpr int kMixPairChunkKB = 4;
 constexpr double kTuneMinWork = 10000000.0; // matmul_kernels.cu:24 (MATMUL_LT_MIN_WORK)
+// Fused float64 N-split: up to this many ranks each tile's epilogue stores
+// it into every window (the stores of a wave's tiles finish within the next
+// wave's start); above it the persistent kernel copies a tile to the peers
+// during the next tile's math.
+#ifndef PTG_PEER_STORE_MAX_RANKS
+#define PTG_PEER_STORE_MAX_RANKS 4
+#endif
+constexpr int kPeerStoreMaxRanks = PTG_PEER_STORE_MAX_RANKS;
 
 struct Problem {
     int dt;
@@ -538,8 +546,10 @@ enum KernelId : int {
     KID_F16_F32,             // f16 x f16 -> float32
     KID_SKINNY_VEC,          // 12 ids: float32 few-column kernel with 16-byte A copies, 2 * NB index + A k-major
     KID_F64_DMMA_HALF = KID_SKINNY_VEC + 12,   // float64 half tiles of a launch's last wave
+    KID_F64_DMMA_PEER_STORE,                   // N-split block, epilogue stores to every window
+    KID_F64_DMMA_PEER_HALF,                    // its half tiles
 };
-static_assert(KID_F64_DMMA_HALF < 64, "kernel ids index a 64-bit attribute mask");
+static_assert(KID_F64_DMMA_PEER_HALF < 64, "kernel ids index a 64-bit attribute mask");
 
 const char *kernel_name(int kid)
 {
@@ -974,9 +984,11 @@ cudaError_t launch_f64_dmma(const Problem &P, DeviceState *ds, cudaStream_t stre
         a_vec = a_vec && P.a_bs[d] % 2 == 0;
         b_vec = b_vec && P.b_bs[d] % 2 == 0;
     }
-    if (!ensure_smem_attr(ds, KID_F64_DMMA, f64_dmma_kernel, kF64SmemBytes) ||
-        !ensure_smem_attr(ds, KID_F64_DMMA_HALF, f64_dmma_half_kernel, kF64SmemBytes))
+    if (!ensure_smem_attr(ds, KID_F64_DMMA, f64_dmma_kernel<false>, kF64SmemBytes) ||
+        !ensure_smem_attr(ds, KID_F64_DMMA_HALF, f64_dmma_half_kernel<false>, kF64SmemBytes))
         return cudaErrorInvalidConfiguration;
+    F64PeerOut none;
+    std::memset(&none, 0, sizeof(none));
     // full tiles, one resident CTA per SM; then -- when the last wave would
     // be at most half full -- its tiles as half tiles in a second launch
     const F64Work w = f64_work(P.M, P.N, P.batches, ds->sms);
@@ -984,11 +996,12 @@ cudaError_t launch_f64_dmma(const Problem &P, DeviceState *ds, cudaStream_t stre
         dim3 grid(static_cast<unsigned>(w.n_blocks),
                   static_cast<unsigned>(std::min<long long>(w.m_blocks, 65535)),
                   static_cast<unsigned>(std::min<long long>(P.batches, 65535)));
-        f64_dmma_kernel<<<grid, 256, kF64SmemBytes, stream>>>(s, a_vec ? 1 : 0, b_vec ? 1 : 0, w);
+        f64_dmma_kernel<false><<<grid, 256, kF64SmemBytes, stream>>>(s, a_vec ? 1 : 0,
+                                                                     b_vec ? 1 : 0, w, none);
     }
     if (w.tail > 0)
-        f64_dmma_half_kernel<<<static_cast<unsigned>(2 * w.tail), 256, kF64SmemBytes, stream>>>(
-            s, a_vec ? 1 : 0, b_vec ? 1 : 0, w);
+        f64_dmma_half_kernel<false><<<static_cast<unsigned>(2 * w.tail), 256, kF64SmemBytes,
+                                      stream>>>(s, a_vec ? 1 : 0, b_vec ? 1 : 0, w, none);
     return cudaGetLastError();
 }
 
@@ -1385,14 +1398,32 @@ cudaError_t ptg_launch_f64_peer(const double *a, size_t a_s0, size_t a_s1, const
                        reinterpret_cast<uintptr_t>(a) % 16 == 0;
     const bool b_vec = P.b_sn == 1 && P.N % 2 == 0 && (P.b_sk % 2 == 0 || P.K == 1) &&
                        reinterpret_cast<uintptr_t>(b) % 16 == 0;
-    auto kernel = f64_dmma_peer_kernel;
-    if (!ensure_smem_attr(ds, KID_F64_DMMA_PEER, kernel, kF64PeerSmemBytes))
-        return cudaErrorInvalidConfiguration;
-    // persistent: one CTA per SM over the work units (see f64_work)
     const F64Work w = f64_work(P.M, P.N, 1, ds->sms);
-    const long long grid = std::min<long long>(w.full + 2 * w.tail, ds->sms);
-    kernel<<<static_cast<unsigned>(grid), 256, kF64PeerSmemBytes, stream>>>(
-        s, a_vec ? 1 : 0, b_vec ? 1 : 0, po, w);
+    const bool store = po.exchange == GEMM_MGPU_EXCHANGE_STORE ||
+                       (po.exchange == GEMM_MGPU_EXCHANGE_AUTO && po.ndst <= kPeerStoreMaxRanks);
+    if (store) {
+        // few ranks: each tile's epilogue stores it into every window
+        if (!ensure_smem_attr(ds, KID_F64_DMMA_PEER_STORE, f64_dmma_kernel<true>, kF64SmemBytes) ||
+            !ensure_smem_attr(ds, KID_F64_DMMA_PEER_HALF, f64_dmma_half_kernel<true>,
+                              kF64SmemBytes))
+            return cudaErrorInvalidConfiguration;
+        if (w.full > 0)
+            f64_dmma_kernel<true><<<dim3(static_cast<unsigned>(w.n_blocks),
+                                         static_cast<unsigned>(std::min(w.m_blocks, 65535))),
+                                    256, kF64SmemBytes, stream>>>(s, a_vec ? 1 : 0, b_vec ? 1 : 0,
+                                                                  w, po);
+        if (w.tail > 0)
+            f64_dmma_half_kernel<true><<<static_cast<unsigned>(2 * w.tail), 256, kF64SmemBytes,
+                                         stream>>>(s, a_vec ? 1 : 0, b_vec ? 1 : 0, w, po);
+    } else {
+        // many ranks: persistent, the remote copies under the next tile's math
+        auto kernel = f64_dmma_peer_kernel;
+        if (!ensure_smem_attr(ds, KID_F64_DMMA_PEER, kernel, kF64PeerSmemBytes))
+            return cudaErrorInvalidConfiguration;
+        const long long grid = std::min<long long>(w.full + 2 * w.tail, ds->sms);
+        kernel<<<static_cast<unsigned>(grid), 256, kF64PeerSmemBytes, stream>>>(
+            s, a_vec ? 1 : 0, b_vec ? 1 : 0, po, w);
+    }
     const cudaError_t err = cudaGetLastError();
     if (err == cudaSuccess) {
         t_info.builtin_matmul_calls++;

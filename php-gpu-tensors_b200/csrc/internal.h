@@ -17,6 +17,7 @@ struct F64PeerOut {
     int rot;              // this rank: destination (rot + i) % ndst is stored i-th
     long long ldc;
     long long col_off;
+    int exchange;         // GEMM_MGPU_EXCHANGE_*: store, overlap, or by rank count
 };
 
 } // namespace ptg

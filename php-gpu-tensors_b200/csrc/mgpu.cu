@@ -322,6 +322,7 @@ struct gemm_mgpu_window {
     size_t bytes;
     void *peer[8];
     int *sync;   // one int for the ordering all-reduces
+    int exchange;  // GEMM_MGPU_EXCHANGE_*
 };
 
 PT_API int gemm_mgpu_window_create(gemm_mgpu_comm *comm, size_t bytes, gemm_mgpu_window **win,
@@ -379,6 +380,17 @@ PT_API int gemm_mgpu_window_create(gemm_mgpu_comm *comm, size_t bytes, gemm_mgpu
     return 1;
 }
 
+PT_API int gemm_mgpu_window_set_exchange(gemm_mgpu_window *win, int mode)
+{
+    if (!win || (mode != GEMM_MGPU_EXCHANGE_AUTO && mode != GEMM_MGPU_EXCHANGE_STORE &&
+                 mode != GEMM_MGPU_EXCHANGE_OVERLAP)) {
+        ptg_set_last_status(GEMM_SM100_STATUS_INVALID_ARGUMENT);
+        return 0;
+    }
+    win->exchange = mode;
+    return 1;
+}
+
 PT_API void gemm_mgpu_window_destroy(gemm_mgpu_window *win)
 {
     if (!win)
@@ -425,6 +437,7 @@ PT_API int gemm_mgpu_nsplit_matmul_fused(gemm_mgpu_window *win, dtype_t dtype, c
         po.dst[g] = static_cast<double *>(win->peer[g]);
     po.ndst = G;
     po.rot = comm->rank;
+    po.exchange = win->exchange;
     po.ldc = N;
     po.col_off = static_cast<long long>(comm->rank) * (N / G);
     const cudaError_t err = ptg_launch_f64_peer(

@@ -135,6 +135,7 @@ _SIGNATURES = {
                                                ctypes.POINTER(ctypes.c_void_p),
                                                ctypes.POINTER(ctypes.c_void_p)]),
     "gemm_mgpu_window_destroy": (None, [ctypes.c_void_p]),
+    "gemm_mgpu_window_set_exchange": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int]),
     "gemm_mgpu_nsplit_matmul_fused": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int,
                                                      ctypes.c_void_p, ctypes.c_size_t,
                                                      ctypes.c_size_t, ctypes.c_void_p,
@@ -585,6 +586,15 @@ class MgpuWindow:
             raise RuntimeException("gemm_mgpu_window_create failed (status %d)"
                                    % cuda_get_backend_info()["lastBlasStatus"])
         self.handle, self.local, self.comm, self.M, self.N = h, local.value, comm, M, N
+
+    EXCHANGE = {"auto": 0, "store": 1, "overlap": 2}
+
+    def set_exchange(self, mode):
+        """'auto', 'store' (epilogue stores into every window) or 'overlap'
+        (persistent kernel, copies under the next tile's math)."""
+        if mode not in self.EXCHANGE or not library().gemm_mgpu_window_set_exchange(
+                self.handle, self.EXCHANGE[mode]):
+            raise InvalidArgumentException("unknown exchange mode %r" % (mode,))
 
     def result(self):
         """The window as a torch view (float64 [M, N]); valid after a fused call."""

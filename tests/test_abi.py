@@ -194,3 +194,10 @@ def test_gradient_and_host_staging_errors_without_gpu():
                                       2, 2, 0) == P.PT_INVALID_ARGUMENT
     assert lib.pt_host_matmul_sharded(16, 16, 16, P.DTYPE_CODES["float32"], 4, 2, 2, 2, 0, devs,
                                       0, 2, 0) == P.PT_INVALID_ARGUMENT
+
+
+def test_window_exchange_mode_rejects_a_null_window():
+    """Argument checks of gemm_mgpu_window_set_exchange run before any CUDA call."""
+    lib = P.library()
+    assert lib.gemm_mgpu_window_set_exchange(None, 0) == 0
+    assert P.cuda_get_backend_info()["lastBlasStatus"] == 9006

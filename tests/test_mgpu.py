@@ -86,11 +86,17 @@ def test_fused_nsplit_single_rank_equals_plain_product():
     comm = P.MgpuComm(0, 1)
     win = P.MgpuWindow(comm, M, N)
     try:
-        for _ in range(2):
-            c = P.nsplit_matmul_fused(win, P.CudaArray.from_torch(a), P.CudaArray.from_torch(b))
-            ref = P.CudaArray.from_torch(a).matmul(P.CudaArray.from_torch(b), allow_float64=True)
-            torch.cuda.synchronize()
-            assert torch.equal(c, ref.to_torch())
+        for mode in ("auto", "store", "overlap"):
+            win.set_exchange(mode)
+            for _ in range(2):
+                c = P.nsplit_matmul_fused(win, P.CudaArray.from_torch(a),
+                                          P.CudaArray.from_torch(b))
+                ref = P.CudaArray.from_torch(a).matmul(P.CudaArray.from_torch(b),
+                                                       allow_float64=True)
+                torch.cuda.synchronize()
+                assert torch.equal(c, ref.to_torch()), mode
+        with pytest.raises(P.InvalidArgumentException):
+            win.set_exchange("sideways")
     finally:
         win.close()
         comm.close()
@@ -111,11 +117,14 @@ def test_fused_nsplit_full_and_half_tiles_single_rank():
     comm = P.MgpuComm(0, 1)
     win = P.MgpuWindow(comm, M, N)
     try:
-        for _ in range(2):
-            c = P.nsplit_matmul_fused(win, P.CudaArray.from_torch(a), P.CudaArray.from_torch(b))
-            ref = P.CudaArray.from_torch(a).matmul(P.CudaArray.from_torch(b), allow_float64=True)
-            torch.cuda.synchronize()
-            assert torch.equal(c, ref.to_torch())
+        ref = P.CudaArray.from_torch(a).matmul(P.CudaArray.from_torch(b), allow_float64=True)
+        for mode in ("store", "overlap"):
+            win.set_exchange(mode)
+            for _ in range(2):
+                c = P.nsplit_matmul_fused(win, P.CudaArray.from_torch(a),
+                                          P.CudaArray.from_torch(b))
+                torch.cuda.synchronize()
+                assert torch.equal(c, ref.to_torch()), mode
     finally:
         win.close()
         comm.close()
@@ -175,9 +184,12 @@ def _nccl_worker(rank, world, port, q):
                                                     allow_float64=True).to_torch()
             c = P.nsplit_matmul(comm, P.CudaArray.from_torch(a), P.CudaArray.from_torch(bl), N)
             results[("nccl", call)] = bool(torch.equal(c.to_torch(), full))
-            f = P.nsplit_matmul_fused(win, P.CudaArray.from_torch(a), P.CudaArray.from_torch(bl))
-            torch.cuda.synchronize()
-            results[("fused", call)] = bool(torch.equal(f, full))
+            for mode in ("store", "overlap"):
+                win.set_exchange(mode)
+                f = P.nsplit_matmul_fused(win, P.CudaArray.from_torch(a),
+                                          P.CudaArray.from_torch(bl))
+                torch.cuda.synchronize()
+                results[("fused_" + mode, call)] = bool(torch.equal(f, full))
             # the allocation-free entry point: its gather runs in the
             # library's own device buffer at rank offsets
             na = torch.full((M, N), float("nan"), device="cuda", dtype=torch.float64)
@@ -211,9 +223,11 @@ def _nccl_worker(rank, world, port, q):
         full = P.CudaArray.from_torch(a).matmul(P.CudaArray.from_torch(b),
                                                 allow_float64=True).to_torch()
         win = P.MgpuWindow(comm, Mr, Nr)
-        f = P.nsplit_matmul_fused(win, P.CudaArray.from_torch(a), P.CudaArray.from_torch(bl))
-        torch.cuda.synchronize()
-        results[("fused_ragged", 0)] = bool(torch.equal(f, full))
+        for mode in ("store", "overlap"):
+            win.set_exchange(mode)
+            f = P.nsplit_matmul_fused(win, P.CudaArray.from_torch(a), P.CudaArray.from_torch(bl))
+            torch.cuda.synchronize()
+            results[("fused_ragged_" + mode, 0)] = bool(torch.equal(f, full))
         dist.barrier()
         win.close()
         q.put((rank, results))
