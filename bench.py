@@ -896,15 +896,15 @@ def measure_nsplit(ctx, args):
             results["fused_" + mode] = P.nsplit_matmul_fused(win, A, Bl)
         return run
 
-    # the fused entry point's two exchanges (auto picks epilogue stores up to
-    # 4 ranks, copies under the next tile's math above), NCCL, compute alone
+    # the fused entry point's two exchanges (auto: epilogue stores), NCCL,
+    # and the compute alone
     variants = [("store", fused("store")), ("overlap", fused("overlap")),
                 ("nccl", lambda: results.__setitem__("nccl", P.nsplit_matmul(comm, A, Bl, N, ws))),
                 ("compute", compute_only)]
     flop = 2.0 * M * N * K
     kernel = None
     compute_kernel = None
-    auto = "store" if world <= 4 else "overlap"
+    auto = "store"
     for vname, fn in variants:
         for _ in range(args.warmup):
             fn()
@@ -960,8 +960,7 @@ def measure_nsplit(ctx, args):
                      "traffic": traffic_for("config5b%s" % ("" if world == 1 else "_x%d" % world),
                                             compute_kernel)},
         "gpu_launches": args.steps * (1 if args.nsplit == "fused" else 2),
-        "exchange": "fused = %s: epilogue stores up to 4 ranks, copies under the next "
-                    "tile's math above" % auto,
+        "exchange": "fused = %s (gemm_mgpu_window_set_exchange AUTO: epilogue stores)" % auto,
         "clocks": head["clocks"],
         "check": {k: v for k, v in ctx.checks.items() if k.startswith("config5b")},
     }
