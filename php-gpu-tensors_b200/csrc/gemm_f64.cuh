@@ -148,21 +148,6 @@ __device__ __forceinline__ void f64_mma_kblock(double (&acc)[TI][TJ][4], const d
     }
 }
 
-// Persistent peer kernel's order of the full tiles: groups of kF64GroupM row
-// blocks, row block fastest (rank-2 products, one batch).
-constexpr int kF64GroupM = 16;
-__device__ __forceinline__ void f64_grouped_tile(long long L, int m_blocks, int n_blocks,
-                                                 int &mb, int &nb)
-{
-    const long long per_group = static_cast<long long>(kF64GroupM) * n_blocks;
-    const long long group = L / per_group;
-    const int first_m = static_cast<int>(group) * kF64GroupM;
-    const int gm = min(kF64GroupM, m_blocks - first_m);
-    const long long r = L - group * per_group;
-    mb = first_m + static_cast<int>(r % gm);
-    nb = static_cast<int>(r / gm);
-}
-
 // A launch's work list: `full` tiles of 128 x 128 in row-major tile order
 // (column block fastest, then row block, then batch), then, when the last
 // wave is at most half full, its tiles as 2 x `tail` half tiles.
@@ -461,32 +446,27 @@ __global__ void __launch_bounds__(256, 1)
 }
 
 // ---------------------------------------------------------------------------
-// The N-split block product whose results go to every rank's window over
-// NVLink (rank-2 operands, no batch).  Persistent: CTA c of the grid takes
-// units c, c + grid, ...; the full tiles run in groups of kF64GroupM row
-// blocks, row block fastest, which kept the CTAs' working set in L2 better
-// than the row-major order here (8192^3 on one GPU: 1.5 % against 4 % over
-// the plain kernel; taking units from an atomic counter in row-major order
-// instead measured 13 % over).  When a unit's k loop ends, the CTA writes its tile into this
-// rank's own window (local HBM, fragment layout), and during the NEXT unit's
-// k loop every thread copies a few 16-byte pieces of it per k-block from
-// there to the other ranks' windows, the next rank first and so on around
-// the ring, so every rank spreads its traffic over all peers and the NVLink
-// transfer runs under the DMMA work instead of after it.  (A non-persistent
-// kernel that stored each tile to every window when it finished held each
-// wave's SMs idle during the stores; staging the tile in shared memory
-// instead left room only for a ring of 2 x 16-deep or 4 x 8-deep k-blocks,
-// which slowed the math by 4-13 %.)  Only each CTA's last unit is copied
-// after the math.
-constexpr int kF64PeerSmemBytes = kF64SmemBytes;
+// The N-split block product with the exchange under the math (rank-2
+// operands, one batch): one CTA per tile, as the plain kernel.  A CTA writes
+// its tile into this rank's own window (local HBM) and leaves the tile's id
+// in a slot for its SM (po.slots[%smid]); the next CTA to start on that SM
+// claims the slot and, while its own k loop runs, copies a few 16-byte
+// pieces of the claimed tile per k-block from the own window to the other
+// ranks' windows (the next rank first, then around the ring).  So each
+// tile's NVLink transfer runs under a later tile's DMMA work instead of
+// holding its SM, and the hardware keeps scheduling the tiles.  A flush
+// launch copies the tiles still in the slots when the last CTAs end.  The
+// claims and hand-offs are atomic exchanges, never waits: a tile is copied
+// once, by whoever takes it out of its slot.  (A persistent kernel doing the
+// same with a fixed tile order lost 4-5 % of its math to the fixed order.)
 
-// Pending remote copies of the last finished unit: its origin and width.
+// Pending remote copies of a claimed tile: its origin and width.
 struct F64Pending {
     int m0, n0, width;
     int done, ops;
 };
 
-// Issues copy number e of the pending unit: piece e / peers of the unit
+// Issues copy number e of the pending tile: piece e / peers of it
 // (consecutive threads on consecutive 16-byte column pairs of a row) to
 // destination rank (rot + 1 + e % peers) % ndst.
 __device__ __forceinline__ void f64_copy_piece(const SimtParams &p, const F64PeerOut &po,
@@ -505,26 +485,75 @@ __device__ __forceinline__ void f64_copy_piece(const SimtParams &p, const F64Pee
     }
 }
 
+// The copies owed for slot code `code` (work unit + 1; 0 = nothing).
+__device__ __forceinline__ F64Pending f64_pending(const F64Work &w, const F64PeerOut &po,
+                                                  unsigned long long code)
+{
+    F64Pending q;
+    q.m0 = q.n0 = 0;
+    q.width = kF64BN;
+    q.done = q.ops = 0;
+    if (code != 0) {
+        long long batch;
+        q.width = f64_unit(w, static_cast<long long>(code - 1), batch, q.m0, q.n0);
+        q.ops = (po.ndst - 1) * (kF64BM * q.width / 2 / 256);
+    }
+    return q;
+}
+
+__device__ __forceinline__ uint32_t sm_id()
+{
+    uint32_t id;
+    asm volatile("mov.u32 %0, %%smid;" : "=r"(id));
+    return id;
+}
+
+// WN = 4: full tiles (units [0, w.full)); WN = 2: half tiles (units
+// w.full + [0, 2 w.tail)), launched after the full tiles.
 template <int WN>
-__device__ __forceinline__ void f64_peer_unit(const SimtParams &p, const F64PeerOut &po,
-                                              double *sa_all, double *sb_all, int m0, int n0,
-                                              bool a_vec, bool b_vec, F64Pending &q)
+__global__ void __launch_bounds__(256, 1)
+    f64_dmma_handoff_kernel(const SimtParams p, int a_vec, int b_vec, const F64Work w,
+                            const F64PeerOut po)
 {
     using T = F64Tile<WN>;
+    // (no static shared memory: a static __shared__ word beside the dynamic
+    // ring measured 13-14 % slower; the first ring word carries the slot
+    // codes to the other threads instead, while the ring is idle)
+    extern __shared__ __align__(16) double f64_smem[];
+    unsigned long long *s_code = reinterpret_cast<unsigned long long *>(f64_smem);
+    double *sa_all = f64_smem, *sb_all = f64_smem + kF64Stages * kF64StageA;
+    const long long u = (WN == 4 ? 0 : w.full) + blockIdx.x;
+    long long batch;
+    int m0, n0;
+    f64_unit(w, u, batch, m0, n0);
+    const uint32_t sm = sm_id();
+    const bool slotted = sm < static_cast<uint32_t>(po.nslots);
+    // claim the tile the previous CTA on this SM left to be copied
+    if (threadIdx.x == 0) {
+        *s_code = slotted ? atomicExch(po.slots + sm, 0ull) : 0ull;
+        __threadfence();
+    }
+    __syncthreads();
+    F64Pending q = f64_pending(w, po, *s_code);
+    // (f64_tile_mainloop's first barrier orders these reads before the ring
+    // is filled)
     double acc[T::TI][T::TJ][4];
-    // a share of the previous unit's remote copies after each k-block,
-    // spread evenly over the k loop
+    // spread the q.ops copies evenly over the k blocks, Bresenham-style (a
+    // division per k-block cost the DMMA warps measurable issue time)
+    int credit = 0;
     f64_tile_mainloop<WN>(p, sa_all, sb_all, 0, 0, m0, n0, a_vec, b_vec, acc,
-                          [&](int kb, int k_blocks) {
-                              const int target = static_cast<int>(
-                                  (static_cast<long long>(kb + 1) * q.ops + k_blocks - 1) /
-                                  k_blocks);
-                              for (; q.done < target; q.done++)
-                                  f64_copy_piece(p, po, q, q.done);
+                          [&](int, int k_blocks) {
+                              if (q.ops == 0)
+                                  return;
+                              credit += q.ops;
+                              while (credit >= k_blocks && q.done < q.ops) {
+                                  credit -= k_blocks;
+                                  f64_copy_piece(p, po, q, q.done++);
+                              }
                           });
     for (; q.done < q.ops; q.done++)
         f64_copy_piece(p, po, q, q.done);
-    // this unit into the rank's own window
+    // this tile into the own window
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int g = lane >> 2, t = lane & 3;
     const int wm = (warp / WN) * T::kWarpM, wn = (warp % WN) * T::kWarpN;
@@ -542,108 +571,43 @@ __device__ __forceinline__ void f64_peer_unit(const SimtParams &p, const F64Peer
                                                  po.col_off + n) =
                         make_double2(acc[i][j][r], acc[i][j][r + 1]);
             }
-    __syncthreads();   // the unit is in the own window for every thread's copies
-    q.m0 = m0;
-    q.n0 = n0;
-    q.width = T::BN;
-    q.done = 0;
-    q.ops = (po.ndst - 1) * (kF64BM * T::BN / 2 / 256);
-}
-
-__global__ void __launch_bounds__(256, 1)
-    f64_dmma_peer_kernel(const SimtParams p, int a_vec, int b_vec, const F64PeerOut po,
-                         const F64Work w)
-{
-    extern __shared__ __align__(16) double f64_smem[];
-    double *sa_all = f64_smem;
-    double *sb_all = f64_smem + kF64Stages * kF64StageA;
-    F64Pending q;
-    q.m0 = q.n0 = 0;
-    q.width = kF64BN;
-    q.done = q.ops = 0;
-    const long long units = w.full + 2 * w.tail;
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int g = lane >> 2, t = lane & 3;
-    const int wm = (warp >> 2) * 64, wn = (warp & 3) * 32;
-    const int k_blocks = (p.K + kF64BK - 1) / kF64BK;
-    double *own = po.dst[po.rot];
-    // full tiles: the plain kernel's loop body (written out here rather than
-    // through f64_tile_mainloop, which measured a few % slower), with the
-    // previous unit's remote copies after each k-block
-    for (long long u = blockIdx.x; u < w.full; u += gridDim.x) {
-        int mb, nb;
-        f64_grouped_tile(u, w.m_blocks, w.n_blocks, mb, nb);
-        const int m0 = mb * kF64BM, n0 = nb * kF64BN;
-        double acc[4][4][4];
-#pragma unroll
-        for (int i = 0; i < 4; i++)
-#pragma unroll
-            for (int j = 0; j < 4; j++)
-#pragma unroll
-                for (int r = 0; r < 4; r++)
-                    acc[i][j][r] = 0.0;
-
-        __syncthreads();   // the previous tile's readers are done with the ring
-#pragma unroll
-        for (int s = 0; s < kF64Stages - 1; s++) {
-            if (s < k_blocks)
-                f64_load_stage<kF64BN>(p, sa_all + s * kF64StageA, sb_all + s * kF64StageB, 0, 0,
-                                       m0, n0, s * kF64BK, a_vec, b_vec);
-            cp_async_commit();
-        }
-        for (int kb = 0; kb < k_blocks; kb++) {
-            cp_async_wait<kF64Stages - 2>();
-            __syncthreads();
-            const int nxt = kb + kF64Stages - 1;
-            if (nxt < k_blocks)
-                f64_load_stage<kF64BN>(p, sa_all + (nxt % kF64Stages) * kF64StageA,
-                                       sb_all + (nxt % kF64Stages) * kF64StageB, 0, 0, m0, n0,
-                                       nxt * kF64BK, a_vec, b_vec);
-            cp_async_commit();
-            f64_mma_kblock<4, 4>(acc, sa_all + (kb % kF64Stages) * kF64StageA,
-                                 sb_all + (kb % kF64Stages) * kF64StageB, wm, wn, g, t);
-            const int target = static_cast<int>(
-                (static_cast<long long>(kb + 1) * q.ops + k_blocks - 1) / k_blocks);
-            for (; q.done < target; q.done++)
-                f64_copy_piece(p, po, q, q.done);
-        }
-        cp_async_wait<0>();
+    __syncthreads();   // every thread's part of the tile is written; the ring is idle
+    // hand the tile to the next CTA on this SM; copy it here when there is
+    // no slot, or copy what was left in the slot when two CTAs shared an SM
+    if (threadIdx.x == 0) {
+        __threadfence();
+        const unsigned long long mine = static_cast<unsigned long long>(u) + 1;
+        *s_code = slotted ? atomicExch(po.slots + sm, mine) : mine;
+        __threadfence();
+    }
+    __syncthreads();
+    const unsigned long long left = *s_code;
+    if (left != 0) {
+        q = f64_pending(w, po, left);
         for (; q.done < q.ops; q.done++)
             f64_copy_piece(p, po, q, q.done);
-#pragma unroll
-        for (int i = 0; i < 4; i++)
-#pragma unroll
-            for (int j = 0; j < 4; j++)
-#pragma unroll
-                for (int r = 0; r < 4; r += 2) {
-                    const int m = m0 + wm + i * 16 + g + (r >> 1) * 8;
-                    const int n = n0 + wn + j * 8 + t * 2;
-                    if (m < p.M && n < p.N)
-                        *reinterpret_cast<double2 *>(own + static_cast<long long>(m) * po.ldc +
-                                                     po.col_off + n) =
-                            make_double2(acc[i][j][r], acc[i][j][r + 1]);
-                }
-        __syncthreads();   // the tile is in the own window for every thread's copies
-        q.m0 = m0;
-        q.n0 = n0;
-        q.width = kF64BN;
-        q.done = 0;
-        q.ops = (po.ndst - 1) * (kF64BM * kF64BN / 2 / 256);
     }
-    // the last wave's tiles as halves, when the launch has them: the tiles
-    // from w.full on in the same grouped order
-    for (long long u = w.full + (blockIdx.x + gridDim.x - w.full % gridDim.x) % gridDim.x;
-         u < units; u += gridDim.x) {
-        int mb, nb;
-        f64_grouped_tile(w.full + (u - w.full) / 2, w.m_blocks, w.n_blocks, mb, nb);
-        const int m0 = mb * kF64BM;
-        const int n0 = nb * kF64BN + ((u - w.full) % 2 != 0 ? kF64BN / 2 : 0);
-        f64_peer_unit<2>(p, po, sa_all, sb_all, m0, n0, a_vec, b_vec, q);
-    }
-    for (; q.done < q.ops; q.done++)
-        f64_copy_piece(p, po, q, q.done);
     // make this thread's peer stores visible system-wide before the kernel
     // can be observed complete
+    __threadfence_system();
+}
+
+// Copies the tiles the last CTAs left in the slots (one CTA per slot) and
+// empties the slots for the next call.
+__global__ void __launch_bounds__(256)
+    f64_handoff_flush_kernel(const SimtParams p, const F64Work w, const F64PeerOut po)
+{
+    __shared__ unsigned long long s_code;
+    if (threadIdx.x == 0) {
+        s_code = atomicExch(po.slots + blockIdx.x, 0ull);
+        __threadfence();
+    }
+    __syncthreads();
+    if (s_code == 0)
+        return;
+    F64Pending q = f64_pending(w, po, s_code);
+    for (; q.done < q.ops; q.done++)
+        f64_copy_piece(p, po, q, q.done);
     __threadfence_system();
 }
 

@@ -547,8 +547,9 @@ enum KernelId : int {
     KID_F64_DMMA_HALF = KID_SKINNY_VEC + 12,   // float64 half tiles of a launch's last wave
     KID_F64_DMMA_PEER_STORE,                   // N-split block, epilogue stores to every window
     KID_F64_DMMA_PEER_HALF,                    // its half tiles
+    KID_F64_DMMA_HANDOFF_HALF,                 // half tiles of the hand-off kernel
 };
-static_assert(KID_F64_DMMA_PEER_HALF < 64, "kernel ids index a 64-bit attribute mask");
+static_assert(KID_F64_DMMA_HANDOFF_HALF < 64, "kernel ids index a 64-bit attribute mask");
 
 const char *kernel_name(int kid)
 {
@@ -1415,13 +1416,20 @@ cudaError_t ptg_launch_f64_peer(const double *a, size_t a_s0, size_t a_s1, const
             f64_dmma_half_kernel<true><<<static_cast<unsigned>(2 * w.tail), 256, kF64SmemBytes,
                                          stream>>>(s, a_vec ? 1 : 0, b_vec ? 1 : 0, w, po);
     } else {
-        // many ranks: persistent, the remote copies under the next tile's math
-        auto kernel = f64_dmma_peer_kernel;
-        if (!ensure_smem_attr(ds, KID_F64_DMMA_PEER, kernel, kF64PeerSmemBytes))
+        // the remote copies under later tiles' math: per-SM hand-off, then a
+        // flush of the tiles the last CTAs left behind
+        if (!po.slots || po.nslots < 1 ||
+            !ensure_smem_attr(ds, KID_F64_DMMA_PEER, f64_dmma_handoff_kernel<4>, kF64SmemBytes) ||
+            !ensure_smem_attr(ds, KID_F64_DMMA_HANDOFF_HALF, f64_dmma_handoff_kernel<2>,
+                              kF64SmemBytes))
             return cudaErrorInvalidConfiguration;
-        const long long grid = std::min<long long>(w.full + 2 * w.tail, ds->sms);
-        kernel<<<static_cast<unsigned>(grid), 256, kF64PeerSmemBytes, stream>>>(
-            s, a_vec ? 1 : 0, b_vec ? 1 : 0, po, w);
+        if (w.full > 0)
+            f64_dmma_handoff_kernel<4><<<static_cast<unsigned>(w.full), 256, kF64SmemBytes,
+                                         stream>>>(s, a_vec ? 1 : 0, b_vec ? 1 : 0, w, po);
+        if (w.tail > 0)
+            f64_dmma_handoff_kernel<2><<<static_cast<unsigned>(2 * w.tail), 256, kF64SmemBytes,
+                                         stream>>>(s, a_vec ? 1 : 0, b_vec ? 1 : 0, w, po);
+        f64_handoff_flush_kernel<<<static_cast<unsigned>(po.nslots), 256, 0, stream>>>(s, w, po);
     }
     const cudaError_t err = cudaGetLastError();
     if (err == cudaSuccess) {

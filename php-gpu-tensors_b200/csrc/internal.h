@@ -18,6 +18,8 @@ struct F64PeerOut {
     long long ldc;
     long long col_off;
     int exchange;         // GEMM_MGPU_EXCHANGE_*: store, overlap, or by rank count
+    unsigned long long *slots;   // overlap: per-SM hand-off slots (device memory, zeroed)
+    int nslots;
 };
 
 } // namespace ptg

@@ -323,7 +323,12 @@ struct gemm_mgpu_window {
     void *peer[8];
     int *sync;   // one int for the ordering all-reduces
     int exchange;  // GEMM_MGPU_EXCHANGE_*
+    unsigned long long *slots;   // the overlapped exchange's per-SM hand-off slots
 };
+
+namespace {
+constexpr int kHandoffSlots = 1024;   // more than any %smid of a B200
+}
 
 PT_API int gemm_mgpu_window_create(gemm_mgpu_comm *comm, size_t bytes, gemm_mgpu_window **win,
                                    void **local)
@@ -344,6 +349,8 @@ PT_API int gemm_mgpu_window_create(gemm_mgpu_comm *comm, size_t bytes, gemm_mgpu
     bool good = cudaMalloc(&w->local, bytes) == cudaSuccess &&
                 cudaMalloc(&w->sync, 16) == cudaSuccess &&
                 cudaMemset(w->sync, 0, 16) == cudaSuccess &&
+                cudaMalloc(&w->slots, kHandoffSlots * sizeof(unsigned long long)) == cudaSuccess &&
+                cudaMemset(w->slots, 0, kHandoffSlots * sizeof(unsigned long long)) == cudaSuccess &&
                 cudaIpcGetMemHandle(&mine, w->local) == cudaSuccess &&
                 cudaMalloc(&xdev, hb * G) == cudaSuccess &&
                 cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking) == cudaSuccess &&
@@ -372,6 +379,7 @@ PT_API int gemm_mgpu_window_create(gemm_mgpu_comm *comm, size_t bytes, gemm_mgpu
                 cudaIpcCloseMemHandle(w->peer[g]);
         if (w->local) cudaFree(w->local);
         if (w->sync) cudaFree(w->sync);
+        if (w->slots) cudaFree(w->slots);
         delete w;
         return 0;
     }
@@ -401,6 +409,7 @@ PT_API void gemm_mgpu_window_destroy(gemm_mgpu_window *win)
             cudaIpcCloseMemHandle(win->peer[g]);
     cudaFree(win->local);
     cudaFree(win->sync);
+    cudaFree(win->slots);
     delete win;
 }
 
@@ -438,6 +447,8 @@ PT_API int gemm_mgpu_nsplit_matmul_fused(gemm_mgpu_window *win, dtype_t dtype, c
     po.ndst = G;
     po.rot = comm->rank;
     po.exchange = win->exchange;
+    po.slots = win->slots;
+    po.nslots = kHandoffSlots;
     po.ldc = N;
     po.col_off = static_cast<long long>(comm->rank) * (N / G);
     const cudaError_t err = ptg_launch_f64_peer(
