@@ -339,8 +339,9 @@ int gemm_mgpu_nsplit_matmul_fused(gemm_mgpu_window *win, dtype_t dtype,
  *     than the copies on 1, 2 and 8 B200s);
  *   GEMM_MGPU_EXCHANGE_STORE: the tile's epilogue stores its rows into every
  *     window (one CTA per tile);
- *   GEMM_MGPU_EXCHANGE_OVERLAP: one persistent CTA per SM writes the tile to
- *     this rank's window and copies it to the peers during its next tile.
+ *   GEMM_MGPU_EXCHANGE_OVERLAP: the tile goes to this rank's window only;
+ *     the next tile computed on the same SM copies it to the peers during its
+ *     own math (a last short launch copies the final tiles).
  * Both give the same bits.  Returns 1, or 0 for an unknown mode or a null
  * window. */
 #define GEMM_MGPU_EXCHANGE_AUTO 0
