@@ -466,11 +466,19 @@ struct F64Pending {
     int done, ops;
 };
 
-// Issues copy number e of the pending tile: piece e / peers of it
-// (consecutive threads on consecutive 16-byte column pairs of a row) to
-// destination rank (rot + 1 + e % peers) % ndst.
-__device__ __forceinline__ void f64_copy_piece(const SimtParams &p, const F64PeerOut &po,
-                                               const F64Pending &q, int e)
+// Copy number e of a pending tile is piece e / peers of it (consecutive
+// threads on consecutive 16-byte column pairs of a row) for destination rank
+// (rot + 1 + e % peers) % ndst.  A piece read from the own window is stored
+// one copy later, so the load's latency overlaps DMMA work instead of
+// stalling a warp that feeds the tensor pipe.
+struct F64Staged {
+    double2 v;
+    double *dst;
+    bool valid;
+};
+
+__device__ __forceinline__ void f64_load_piece(const SimtParams &p, const F64PeerOut &po,
+                                               const F64Pending &q, int e, F64Staged &sp)
 {
     const int peers = po.ndst - 1;
     const int d = (po.rot + 1 + e % peers) % po.ndst;
@@ -478,10 +486,38 @@ __device__ __forceinline__ void f64_copy_piece(const SimtParams &p, const F64Pee
     const int idx = threadIdx.x + 256 * (e / peers);
     const int row = idx / pairs, pair = idx % pairs;
     const int m = q.m0 + row, n = q.n0 + 2 * pair;
-    if (m < p.M && n < p.N) {
+    sp.valid = m < p.M && n < p.N;
+    if (sp.valid) {
         const long long off = static_cast<long long>(m) * po.ldc + po.col_off + n;
-        const double2 v = __ldcg(reinterpret_cast<const double2 *>(po.dst[po.rot] + off));
-        *reinterpret_cast<double2 *>(po.dst[d] + off) = v;
+        sp.v = __ldcg(reinterpret_cast<const double2 *>(po.dst[po.rot] + off));
+        sp.dst = po.dst[d] + off;
+    }
+}
+
+__device__ __forceinline__ void f64_store_piece(F64Staged &sp)
+{
+    if (sp.valid)
+        *reinterpret_cast<double2 *>(sp.dst) = sp.v;
+    sp.valid = false;
+}
+
+// Issues copies [q.done, q.ops) four at a time: four loads, then four
+// stores, so a thread has several loads in flight.
+__device__ __forceinline__ void f64_copy_rest(const SimtParams &p, const F64PeerOut &po,
+                                              F64Pending &q)
+{
+    F64Staged sp[4];
+    while (q.done < q.ops) {
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            sp[i].valid = false;
+            if (q.done + i < q.ops)
+                f64_load_piece(p, po, q, q.done + i, sp[i]);
+        }
+#pragma unroll
+        for (int i = 0; i < 4; i++)
+            f64_store_piece(sp[i]);
+        q.done = min(q.done + 4, q.ops);
     }
 }
 
@@ -539,8 +575,11 @@ __global__ void __launch_bounds__(256, 1)
     // is filled)
     double acc[T::TI][T::TJ][4];
     // spread the q.ops copies evenly over the k blocks, Bresenham-style (a
-    // division per k-block cost the DMMA warps measurable issue time)
+    // division per k-block cost the DMMA warps measurable issue time); each
+    // piece is loaded at one copy and stored at the next
     int credit = 0;
+    F64Staged staged;
+    staged.valid = false;
     f64_tile_mainloop<WN>(p, sa_all, sb_all, 0, 0, m0, n0, a_vec, b_vec, acc,
                           [&](int, int k_blocks) {
                               if (q.ops == 0)
@@ -548,11 +587,12 @@ __global__ void __launch_bounds__(256, 1)
                               credit += q.ops;
                               while (credit >= k_blocks && q.done < q.ops) {
                                   credit -= k_blocks;
-                                  f64_copy_piece(p, po, q, q.done++);
+                                  f64_store_piece(staged);
+                                  f64_load_piece(p, po, q, q.done++, staged);
                               }
                           });
-    for (; q.done < q.ops; q.done++)
-        f64_copy_piece(p, po, q, q.done);
+    f64_store_piece(staged);
+    f64_copy_rest(p, po, q);
     // this tile into the own window
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int g = lane >> 2, t = lane & 3;
@@ -584,8 +624,7 @@ __global__ void __launch_bounds__(256, 1)
     const unsigned long long left = *s_code;
     if (left != 0) {
         q = f64_pending(w, po, left);
-        for (; q.done < q.ops; q.done++)
-            f64_copy_piece(p, po, q, q.done);
+        f64_copy_rest(p, po, q);
     }
     // make this thread's peer stores visible system-wide before the kernel
     // can be observed complete
@@ -606,8 +645,7 @@ __global__ void __launch_bounds__(256)
     if (s_code == 0)
         return;
     F64Pending q = f64_pending(w, po, s_code);
-    for (; q.done < q.ops; q.done++)
-        f64_copy_piece(p, po, q, q.done);
+    f64_copy_rest(p, po, q);
     __threadfence_system();
 }
 
