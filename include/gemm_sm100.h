@@ -240,7 +240,9 @@ void gemm_sm100_last_launch(int *grid, int *block, int *cluster);
  * kinds splitting K over clusters of 2 or 4 pairs when they have fewer tiles
  * than a quarter of the SMs (float64 and bf16/f16 x bf16/f16 -> float32 as 1),
  * 4 = few-column split-K CUDA-core kernel whenever N <= 32 and K >= 128
- * (otherwise as 0). */
+ * (otherwise as 0), 5 = 2-CTA kernel with 256 x 512 tiles for 16-bit
+ * products with a 16-bit result whenever the layout allows it (other
+ * products as 3). */
 int gemm_sm100_set_path(int path);
 
 /* Reads (and with clear != 0 resets) the device status word of `device`:

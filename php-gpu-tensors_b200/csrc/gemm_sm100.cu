@@ -20,6 +20,7 @@
 #include "gemm_skinny.cuh"
 #include "gemm_tc.cuh"
 #include "gemm_tc2.cuh"
+#include "gemm_tc2w.cuh"
 
 #include <cudaTypedefs.h>
 
@@ -63,6 +64,15 @@ constexpr double kPairTileCost = 1.79;
 // mixed kinds on the 2-CTA kernel: k-blocks (64 K each) per accumulator chunk,
 // 256 K as in the single-CTA mixed kernel
 constexpr int kMixPairChunkKB = 4;
+// Time of one 256 x 512 tile of the wide 16-bit pair kernel in 256 x 256
+// tiles of the plain one, and the shortest inner axis it is chosen for.
+// Measured on B200 (TFLOP/s, plain -> wide, both with the same wave
+// efficiency): bf16 [64,1024,1024]^2 1150 -> 1195, 8192^3 1447 -> 1609,
+// [512,2048,2048]^2 (power-capped) 1141-1177 -> 1199-1228; with half as many
+// waves' worth of padding lost the wide tile is slower (fp16 8192x4096x4096,
+// 3.5 waves of wide tiles against 6.9: 1367 -> 1277).
+constexpr double kWideTileCost = 1.9;
+constexpr int kWideMinK = 1024;
 constexpr double kTuneMinWork = 10000000.0; // matmul_kernels.cu:24 (MATMUL_LT_MIN_WORK)
 // Fused float64 N-split: up to this many ranks each tile's epilogue stores
 // it into every window; above it the persistent kernel copies a tile to the
@@ -548,8 +558,10 @@ enum KernelId : int {
     KID_F64_DMMA_PEER_STORE,                   // N-split block, epilogue stores to every window
     KID_F64_DMMA_PEER_HALF,                    // its half tiles
     KID_F64_DMMA_HANDOFF_HALF,                 // half tiles of the hand-off kernel
+    KID_BF16_WIDE,                             // bf16 on the 2-CTA 256 x 512 kernel
+    KID_F16_WIDE,                              // f16 on the 2-CTA 256 x 512 kernel
 };
-static_assert(KID_F64_DMMA_HANDOFF_HALF < 64, "kernel ids index a 64-bit attribute mask");
+static_assert(KID_F16_WIDE < 64, "kernel ids index a 64-bit attribute mask");
 
 const char *kernel_name(int kid)
 {
@@ -563,6 +575,8 @@ const char *kernel_name(int kid)
     case KID_F32X3_128: return "tc-3xtf32-128x128";
     case KID_BF16_PAIR: return "tc2-bf16-256x256";
     case KID_F16_PAIR: return "tc2-f16-256x256";
+    case KID_BF16_WIDE: return "tc2-bf16-256x512";
+    case KID_F16_WIDE: return "tc2-f16-256x512";
     case KID_F64_DMMA: return "dmma-f64-128x128";
     case KID_F32X3_PAIR: return "tc2-3xtf32-256x256";
     case KID_TF32_PAIR: return "tc2-tf32-256x256";
@@ -700,6 +714,29 @@ cudaError_t launch_tc2_kernel(DeviceState *ds, int kid, int slot, const CUtensor
                                                   mc, p, stream);
 }
 
+// The 256 x 512 kernel moves registers between its warpgroups
+// (setmaxnreg); an increase beyond the CTA's launch allocation would never
+// complete, so the compiled register count is checked before every launch.
+template <int IN, int OUT>
+cudaError_t launch_wide_kernel(DeviceState *ds, int kid, int slot, const CUtensorMap &ma,
+                               const CUtensorMap &mb, const CUtensorMap &mc, TcParams &p,
+                               cudaStream_t stream)
+{
+    using Cfg = Tc2wConfig<IN, OUT>;
+    auto kernel = tc2w_gemm_kernel<IN, OUT>;
+    static const int regs = [&] {
+        cudaFuncAttributes fa;
+        if (cudaFuncGetAttributes(&fa, kernel) != cudaSuccess) {
+            (void)cudaGetLastError();
+            return 0;
+        }
+        return fa.numRegs;
+    }();
+    if (regs * Cfg::kThreads < Cfg::kRegsTotal)
+        return cudaErrorInvalidConfiguration;
+    return launch_pair_kernel<Cfg>(ds, kid, slot, kernel, ma, mb, mc, p, stream);
+}
+
 const TunedPlan *find_plan(const Problem &P)
 {
     if (P.nbd != 0 || P.nfd != 0 || P.dt != DT_F32 || P.a_dt != DT_F32 || P.b_dt != DT_F32)
@@ -789,7 +826,7 @@ int try_tc(const Problem &P, DeviceState *ds, cudaStream_t stream, int *kid_out)
     // fewer bytes per FLOP (B200, tf32 4096x1024x1024 with 64 pair tiles:
     // 21.4 against 23.3 us); below it the 128 x 128 tiles fill more SMs.
     if ((!fp32 || !strict) && P.forced_bn == 0)
-        pair = t_path == 3 || (t_path != 1 && tiles_pair >= ds->sms / 4);
+        pair = t_path == 3 || t_path == 5 || (t_path != 1 && tiles_pair >= ds->sms / 4);
     if (wide_out || folded)
         bn = wide_out ? 128 : bn, pair = false;
     // Strict float32 and the mixed float32 x bf16 kinds: the 2-CTA split
@@ -816,7 +853,7 @@ int try_tc(const Problem &P, DeviceState *ds, cudaStream_t stream, int *kid_out)
                 }
             }
         }
-        if (t_path == 3) {
+        if (t_path == 3 || t_path == 5) {
             pair = true;
         } else if (t_path == 0) {
             const long long tiles1 = P.batches * m_blocks * ((P.N + 127) / 128);
@@ -836,6 +873,15 @@ int try_tc(const Problem &P, DeviceState *ds, cudaStream_t stream, int *kid_out)
     }
     if (pair)
         bn = 256;
+    // 16-bit products on the 256 x 512 pair tile: path 5, or automatically
+    // when its rounds of co-resident clusters, at kWideTileCost plain pair
+    // tiles each, take less time than the plain pair kernel's rounds
+    const long long tiles_wide = P.batches * ((P.M + 255) / 256) * ((P.N + 511) / 512);
+    const double rounds_pair = std::ceil(static_cast<double>(tiles_pair) / (ds->sms / 2));
+    const double rounds_wide = std::ceil(static_cast<double>(tiles_wide) / (ds->sms / 2));
+    const bool wide = pair && !fp32 && !wide_out && !folded && P.forced_bn == 0 &&
+                      (t_path == 5 || (t_path == 0 && P.K >= kWideMinK &&
+                                       rounds_wide * kWideTileCost < rounds_pair));
     if (wide_out)
         kid = mix_side == 0   ? (pair ? KID_MIX_A_PAIR : KID_MIX_A)
               : mix_side == 1 ? (pair ? KID_MIX_B_PAIR : KID_MIX_B)
@@ -844,9 +890,9 @@ int try_tc(const Problem &P, DeviceState *ds, cudaStream_t stream, int *kid_out)
         kid = strict ? (pair ? KID_F32X3_PAIR : KID_F32X3_128)
                      : (pair ? KID_TF32_PAIR : (bn == 256 ? KID_TF32_256 : KID_TF32_128));
     else if (P.dt == DT_BF16)
-        kid = pair ? KID_BF16_PAIR : (bn == 256 ? KID_BF16_256 : KID_BF16_128);
+        kid = wide ? KID_BF16_WIDE : pair ? KID_BF16_PAIR : (bn == 256 ? KID_BF16_256 : KID_BF16_128);
     else
-        kid = pair ? KID_F16_PAIR : (bn == 256 ? KID_F16_256 : KID_F16_128);
+        kid = wide ? KID_F16_WIDE : pair ? KID_F16_PAIR : (bn == 256 ? KID_F16_256 : KID_F16_128);
 
     const int bk = 128 / es;            // K elements per stage
     const int chunk = 128 / es;         // MN elements per 128-byte row
@@ -912,7 +958,7 @@ int try_tc(const Problem &P, DeviceState *ds, cudaStream_t stream, int *kid_out)
     p.N = P.N;
     p.K = P.K;
     p.m_blocks = static_cast<int>(pair ? (P.M + 255) / 256 : m_blocks);
-    p.n_blocks = (P.N + bn - 1) / bn;
+    p.n_blocks = (P.N + (wide ? 2 * bn : bn) - 1) / (wide ? 2 * bn : bn);
     p.k_per_fold = (P.K + bk - 1) / bk;
     if (static_cast<double>(p.k_per_fold) * P.folds > 2e9)
         return 0;
@@ -943,6 +989,12 @@ int try_tc(const Problem &P, DeviceState *ds, cudaStream_t stream, int *kid_out)
     case KID_BF16_PAIR: err = launch_tc2_kernel<IN_BF16, OUT_BF16>(ds, kid, 0, tma_a, tma_b, tma_c, p, stream); break;
     case KID_F16_PAIR: err = launch_tc2_kernel<IN_F16, OUT_F16>(ds, kid, 1, tma_a, tma_b, tma_c, p, stream); break;
     case KID_TF32_PAIR: err = launch_tc2_kernel<IN_TF32, OUT_F32>(ds, kid, 3, tma_a, tma_b, tma_c, p, stream); break;
+    case KID_BF16_WIDE:
+        err = launch_wide_kernel<IN_BF16, OUT_BF16>(ds, kid, 6, tma_a, tma_b, tma_c, p, stream);
+        break;
+    case KID_F16_WIDE:
+        err = launch_wide_kernel<IN_F16, OUT_F16>(ds, kid, 7, tma_a, tma_b, tma_c, p, stream);
+        break;
     case KID_F32X3_PAIR:
         err = launch_pair_kernel<Tc2x3Config<IN_F32X3, kPairChunkKB>>(
             ds, kid, 2, tc2x3_gemm_kernel<IN_F32X3, kPairChunkKB>, tma_a, tma_b, tma_c, p, stream);
@@ -1257,7 +1309,7 @@ int run(Problem &P, cudaStream_t stream)
     const double work =
         static_cast<double>(P.M) * P.N * P.K * static_cast<double>(P.batches) * P.folds;
     const bool want_tc = P.K > 0 && P.folds > 0 && t_path != 2 &&
-                         (t_path == 1 || t_path == 3 || work >= kTcMinWork);
+                         (t_path == 1 || t_path == 3 || t_path == 5 || work >= kTcMinWork);
     const bool wide_out = P.a_dt != P.dt || P.b_dt != P.dt;   // float32 result, 16-bit operand(s)
     const bool folded = P.nfd > 0 || P.folds != 1;             // summed batch axes
     const bool skinny_fit = !folded && P.N > 0 && P.N <= kSkinnyMaxN && P.M > 0 &&
@@ -1704,7 +1756,7 @@ PT_API void gemm_sm100_last_launch(int *grid, int *block, int *cluster)
 PT_API int gemm_sm100_set_path(int path)
 {
     const int prev = t_path;
-    if (path >= 0 && path <= 4)
+    if (path >= 0 && path <= 5)
         t_path = path;
     return prev;
 }

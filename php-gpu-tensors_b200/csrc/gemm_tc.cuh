@@ -205,6 +205,19 @@ __device__ __forceinline__ uint32_t pack2(float lo, float hi, int out)
     return *reinterpret_cast<uint32_t *>(&h);
 }
 
+// Inverse of pack2 (exact: every 16-bit value is a float).
+__device__ __forceinline__ void unpack2(uint32_t q, float &lo, float &hi, int out)
+{
+    if (out == OUT_F16) {
+        const __half2 h = *reinterpret_cast<const __half2 *>(&q);
+        lo = __low2float(h);
+        hi = __high2float(h);
+    } else {
+        lo = __uint_as_float(q << 16);
+        hi = __uint_as_float(q & 0xffff0000u);
+    }
+}
+
 // FP32 -> TF32 with round-to-nearest (ties away), low 13 bits cleared.
 __device__ __forceinline__ float round_tf32(float x)
 {

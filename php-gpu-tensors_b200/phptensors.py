@@ -490,9 +490,11 @@ def set_kernel_path(path):
     """0 automatic, 1 single-CTA tensor-core kernel whenever the layout allows,
     2 CUDA cores only, 3 2-CTA tensor-core kernel whenever allowed (16-bit,
     tf32, strict float32, float32 x bf16), 4 few-column split-K kernel
-    whenever N <= 32 and K >= 128."""
+    whenever N <= 32 and K >= 128, 5 the 2-CTA 256 x 512 kernel for 16-bit
+    products with a 16-bit result (other products as 3)."""
     return library().gemm_sm100_set_path(
-        {"auto": 0, "tensor-core": 1, "simt": 2, "tensor-core-pair": 3, "skinny": 4}[path])
+        {"auto": 0, "tensor-core": 1, "simt": 2, "tensor-core-pair": 3, "skinny": 4,
+         "tensor-core-wide": 5}[path])
 
 
 def last_launch():

@@ -89,7 +89,7 @@ def check_fp32(gpu, a, b, what, first=None, count=None):
 
 
 # ------------------------------------------------------------------ golden
-@pytest.mark.parametrize("path", ["auto", "tensor-core", "tensor-core-pair", "simt"])
+@pytest.mark.parametrize("path", ["auto", "tensor-core", "tensor-core-pair", "tensor-core-wide", "simt"])
 def test_golden_vectors(golden, path):
     P.set_kernel_path(path)
     for case in golden["cases"]:
@@ -190,7 +190,7 @@ SKINNY_CASES = [c for c in CASES if c[2][-1] <= 32 and c[2][-2] >= 128]
 
 
 @pytest.mark.parametrize("dtype", ["bfloat16", "float16", "float32"])
-@pytest.mark.parametrize("path", ["auto", "tensor-core", "tensor-core-pair", "skinny"])
+@pytest.mark.parametrize("path", ["auto", "tensor-core", "tensor-core-pair", "tensor-core-wide", "skinny"])
 @pytest.mark.parametrize("case", CASES, ids=[c[0] for c in CASES])
 def test_seeded_parity(case, path, dtype):
     name, ashape, bshape, at, bt, pad = case
@@ -202,8 +202,10 @@ def test_seeded_parity(case, path, dtype):
     b = padded(bv, bshape, pad, dtype, bt)
     c = to_device(a, dtype).matmul(to_device(b, dtype))
     what = (name, path, P.cuda_get_backend_info()["kernel"])
-    if path == "tensor-core-pair" and what[2].startswith("tc"):
+    if path in ("tensor-core-pair", "tensor-core-wide") and what[2].startswith("tc"):
         assert what[2].startswith("tc2-"), what
+    if path == "tensor-core-wide" and what[2].startswith("tc") and dtype != "float32":
+        assert what[2].endswith("256x512"), what
     if path == "skinny" and case in SKINNY_CASES:
         assert what[2].startswith("skinny-"), what
     if dtype == "float32":
@@ -554,7 +556,8 @@ def test_fused_epilogue_matches_unfused_plan(dtype, act, N):
     a = to_device(O.dense(O.to_storage(av, dtype), [M, K]), dtype)
     x = to_device(O.dense(O.to_storage(xv, dtype), [N, K]), dtype)
     bdev = to_device(O.dense(O.to_storage(bias, dtype), [N]), dtype)
-    for path in ("tensor-core", "tensor-core-pair", "simt") + (("skinny",) if N <= 32 else ()):
+    for path in ("tensor-core", "tensor-core-pair", "tensor-core-wide", "simt") + (
+            ("skinny",) if N <= 32 else ()):
         P.set_kernel_path(path)
         fused = a.matmul_epilogue(x.transpose(), bdev, act).to_torch().float()
         plain = a.matmul(x.transpose()).to_torch().float()
@@ -575,7 +578,8 @@ def test_config2_full_size_integer_exact():
     a = torch.randint(-3, 4, (64, 1024, 1024), generator=g).to(torch.bfloat16)
     b = torch.randint(-3, 4, (64, 1024, 1024), generator=g).to(torch.bfloat16)
     exact = torch.bmm(a.double().cuda(), b.double().cuda()).float().to(torch.bfloat16)
-    for path, prefix in (("auto", "tc"), ("tensor-core", "tc-bf16"), ("tensor-core-pair", "tc2-bf16")):
+    for path, prefix in (("auto", "tc"), ("tensor-core", "tc-bf16"), ("tensor-core-pair", "tc2-bf16"),
+                         ("tensor-core-wide", "tc2-bf16-256x512")):
         P.set_kernel_path(path)
         c = P.CudaArray.from_torch(a.cuda()).matmul(P.CudaArray.from_torch(b.cuda()))
         assert P.cuda_get_backend_info()["kernel"].startswith(prefix), path
@@ -600,10 +604,12 @@ def test_config2_random_sampled_rows():
             check_close(c[first:first + N], ref, "bfloat16", (batch, row))
 
 
-def test_config3_fp16_transposed_bias_tanh():
+@pytest.mark.parametrize("path", ["auto", "tensor-core-pair", "tensor-core-wide"])
+def test_config3_fp16_transposed_bias_tanh(path):
     """fp16 A[8192,4096] . X^T (X [4096,4096] row-major) + bias[4096], tanh:
     fused epilogue vs the unfused plan over the whole output, and the product
     vs the oracle on sampled rows."""
+    P.set_kernel_path(path)
     M, K, N = 8192, 4096, 4096
     av = O.seeded([M, K], 30, "uniform", -0.5, 0.5)
     xv = O.seeded([N, K], 31, "uniform", -0.5, 0.5)
@@ -613,8 +619,13 @@ def test_config3_fp16_transposed_bias_tanh():
     a, x = to_device(a_op, "float16"), to_device(x_op, "float16")
     bdev = to_device(O.dense(O.to_storage(bias, "float16"), [N]), "float16")
     fused = a.matmul_epilogue(x.transpose(), bdev, "tanh")
-    assert P.cuda_get_backend_info()["kernel"].startswith(("tc-f16", "tc2-f16"))
+    kernel = P.cuda_get_backend_info()["kernel"]
+    assert kernel.startswith(("tc-f16", "tc2-f16")), kernel
+    if path != "auto":
+        assert kernel == {"tensor-core-pair": "tc2-f16-256x256",
+                          "tensor-core-wide": "tc2-f16-256x512"}[path], kernel
     plain = a.matmul(x.transpose())
+    assert P.cuda_get_backend_info()["kernel"] == kernel
     unfused = torch.tanh(plain.to_torch().float() + bdev.to_torch().float()).half().float()
     assert torch.all((fused.to_torch().float() - unfused).abs() <= 2.0 ** -10)
     c = plain.to_numpy().reshape(-1)
@@ -1004,7 +1015,8 @@ def _random_case(rng):
 
 
 @pytest.mark.parametrize("dtype", ["bfloat16", "float16", "float32"])
-@pytest.mark.parametrize("path", ["auto", "tensor-core", "tensor-core-pair", "skinny"])
+@pytest.mark.parametrize("path", ["auto", "tensor-core", "tensor-core-pair", "tensor-core-wide",
+                                  "skinny"])
 def test_randomized_products(dtype, path):
     """40 seeded random products per dtype and kernel path against the oracle."""
     rng = np.random.default_rng(sum(map(ord, dtype + path)))
