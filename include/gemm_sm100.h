@@ -242,7 +242,9 @@ void gemm_sm100_last_launch(int *grid, int *block, int *cluster);
  * 4 = few-column split-K CUDA-core kernel whenever N <= 32 and K >= 128
  * (otherwise as 0), 5 = 2-CTA kernel with 256 x 512 tiles for 16-bit
  * products with a 16-bit result whenever the layout allows it (other
- * products as 3). */
+ * products as 3), 6 = the same kernel running every tile as two 256-column
+ * halves (the form its last round of clusters takes when the automatic
+ * choice splits it; for tests). */
 int gemm_sm100_set_path(int path);
 
 /* Reads (and with clear != 0 resets) the device status word of `device`:

@@ -650,6 +650,40 @@ cudaError_t launch_tc_kernel(DeviceState *ds, int kid, const CUtensorMap &ma,
     return err != cudaSuccess ? err : cudaGetLastError();
 }
 
+// Co-resident 2-CTA clusters of a pair kernel (the persistent, unsplit
+// launch's grid), queried once per device and kernel slot.
+template <typename Cfg, typename Kernel>
+int pair_cluster_count(DeviceState *ds, int slot, Kernel kernel, cudaStream_t stream)
+{
+    int clusters = 0;
+    {
+        std::lock_guard<std::mutex> lock(g_mutex);
+        clusters = ds->pair_clusters[slot];
+    }
+    if (clusters != 0)
+        return clusters;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cudaLaunchConfig_t cfg = {};
+    cfg.blockDim = dim3(Cfg::kThreads);
+    cfg.dynamicSmemBytes = Cfg::kSmemBytes;
+    cfg.stream = stream;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cfg.gridDim = dim3(static_cast<unsigned>(ds->sms & ~1));
+    // a failed query must not leave its error for a later launch check
+    if (cudaOccupancyMaxActiveClusters(&clusters, kernel, &cfg) != cudaSuccess || clusters < 1) {
+        (void)cudaGetLastError();
+        clusters = ds->sms / 2;
+    }
+    std::lock_guard<std::mutex> lock(g_mutex);
+    ds->pair_clusters[slot] = clusters;
+    return clusters;
+}
+
 // Cluster launch of the 2-CTA kernel: at most as many clusters as can be
 // co-resident (one CTA per SM), two CTAs each.
 template <typename Cfg, typename Kernel>
@@ -675,24 +709,7 @@ cudaError_t launch_pair_kernel(DeviceState *ds, int kid, int slot, Kernel kernel
     cfg.stream = stream;
     cfg.attrs = attr;
     cfg.numAttrs = 2;
-    int clusters = 0;
-    {
-        std::lock_guard<std::mutex> lock(g_mutex);
-        clusters = ds->pair_clusters[slot];
-    }
-    if (clusters == 0) {
-        // co-resident pairs (the persistent, unsplit launch's grid); a failed
-        // query must not leave its error for the launch check below
-        attr[0].val.clusterDim.x = 2;
-        cfg.gridDim = dim3(static_cast<unsigned>(ds->sms & ~1));
-        if (cudaOccupancyMaxActiveClusters(&clusters, kernel, &cfg) != cudaSuccess || clusters < 1) {
-            (void)cudaGetLastError();
-            clusters = ds->sms / 2;
-        }
-        attr[0].val.clusterDim.x = static_cast<unsigned>(2 * G);
-        std::lock_guard<std::mutex> lock(g_mutex);
-        ds->pair_clusters[slot] = clusters;
-    }
+    const int clusters = pair_cluster_count<Cfg>(ds, slot, kernel, stream);
     p.status = ds->status;
     const long long n = G > 1 ? p.tiles * G : std::min<long long>(p.tiles, clusters);
     cfg.gridDim = dim3(static_cast<unsigned>(2 * n));
@@ -734,6 +751,19 @@ cudaError_t launch_wide_kernel(DeviceState *ds, int kid, int slot, const CUtenso
     }();
     if (regs * Cfg::kThreads < Cfg::kRegsTotal)
         return cudaErrorInvalidConfiguration;
+    if (!ensure_smem_attr(ds, kid, kernel, Cfg::kSmemBytes))
+        return cudaErrorInvalidConfiguration;
+    // Work items: p.tiles holds the 256 x 512 tiles here.  wide_items < 0:
+    // whole tiles for every full round of co-resident clusters, the rest as
+    // 256-column halves (one more round of half-length items); 0: halves only.
+    const long long tiles = p.tiles;
+    if (p.wide_items < 0) {
+        const long long clusters = pair_cluster_count<Cfg>(ds, slot, kernel, stream);
+        p.wide_items = tiles / clusters * clusters;
+    } else if (p.wide_items > tiles) {
+        p.wide_items = tiles;
+    }
+    p.tiles = p.wide_items + 2 * (tiles - p.wide_items);
     return launch_pair_kernel<Cfg>(ds, kid, slot, kernel, ma, mb, mc, p, stream);
 }
 
@@ -826,7 +856,7 @@ int try_tc(const Problem &P, DeviceState *ds, cudaStream_t stream, int *kid_out)
     // fewer bytes per FLOP (B200, tf32 4096x1024x1024 with 64 pair tiles:
     // 21.4 against 23.3 us); below it the 128 x 128 tiles fill more SMs.
     if ((!fp32 || !strict) && P.forced_bn == 0)
-        pair = t_path == 3 || t_path == 5 || (t_path != 1 && tiles_pair >= ds->sms / 4);
+        pair = t_path == 3 || t_path >= 5 || (t_path != 1 && tiles_pair >= ds->sms / 4);
     if (wide_out || folded)
         bn = wide_out ? 128 : bn, pair = false;
     // Strict float32 and the mixed float32 x bf16 kinds: the 2-CTA split
@@ -853,7 +883,7 @@ int try_tc(const Problem &P, DeviceState *ds, cudaStream_t stream, int *kid_out)
                 }
             }
         }
-        if (t_path == 3 || t_path == 5) {
+        if (t_path == 3 || t_path >= 5) {
             pair = true;
         } else if (t_path == 0) {
             const long long tiles1 = P.batches * m_blocks * ((P.N + 127) / 128);
@@ -876,12 +906,21 @@ int try_tc(const Problem &P, DeviceState *ds, cudaStream_t stream, int *kid_out)
     // 16-bit products on the 256 x 512 pair tile: path 5, or automatically
     // when its rounds of co-resident clusters, at kWideTileCost plain pair
     // tiles each, take less time than the plain pair kernel's rounds
+    // (the whole tiles of every full round, the rest as 256-column halves,
+    // when that costs less than whole tiles throughout)
     const long long tiles_wide = P.batches * ((P.M + 255) / 256) * ((P.N + 511) / 512);
-    const double rounds_pair = std::ceil(static_cast<double>(tiles_pair) / (ds->sms / 2));
-    const double rounds_wide = std::ceil(static_cast<double>(tiles_wide) / (ds->sms / 2));
+    const long long clusters_est = ds->sms / 2;
+    const double rounds_pair = std::ceil(static_cast<double>(tiles_pair) / clusters_est);
+    const double cost_wide = std::ceil(static_cast<double>(tiles_wide) / clusters_est) * kWideTileCost;
+    const long long full_rounds = tiles_wide / clusters_est;
+    const double cost_mixed =
+        full_rounds * kWideTileCost +
+        std::ceil(2.0 * static_cast<double>(tiles_wide - full_rounds * clusters_est) / clusters_est);
     const bool wide = pair && !fp32 && !wide_out && !folded && P.forced_bn == 0 &&
-                      (t_path == 5 || (t_path == 0 && P.K >= kWideMinK &&
-                                       rounds_wide * kWideTileCost < rounds_pair));
+                      (t_path == 5 || t_path == 6 ||
+                       (t_path == 0 && P.K >= kWideMinK &&
+                        std::min(cost_wide, cost_mixed) < rounds_pair));
+    const long long wide_items = t_path == 6 ? 0 : (t_path == 0 && cost_mixed < cost_wide) ? -1 : tiles_wide;
     if (wide_out)
         kid = mix_side == 0   ? (pair ? KID_MIX_A_PAIR : KID_MIX_A)
               : mix_side == 1 ? (pair ? KID_MIX_B_PAIR : KID_MIX_B)
@@ -967,6 +1006,7 @@ int try_tc(const Problem &P, DeviceState *ds, cudaStream_t stream, int *kid_out)
     for (int d = 0; d < 3; d++)
         p.fshape[d] = tf.fshape[d];
     p.tiles = P.batches * p.m_blocks * p.n_blocks;
+    p.wide_items = wide ? wide_items : 0;
     p.nbd = tb.nbd;
     for (int d = 0; d < 3; d++)
         p.bshape[d] = tb.bshape[d];
@@ -1309,7 +1349,7 @@ int run(Problem &P, cudaStream_t stream)
     const double work =
         static_cast<double>(P.M) * P.N * P.K * static_cast<double>(P.batches) * P.folds;
     const bool want_tc = P.K > 0 && P.folds > 0 && t_path != 2 &&
-                         (t_path == 1 || t_path == 3 || t_path == 5 || work >= kTcMinWork);
+                         (t_path == 1 || t_path == 3 || t_path >= 5 || work >= kTcMinWork);
     const bool wide_out = P.a_dt != P.dt || P.b_dt != P.dt;   // float32 result, 16-bit operand(s)
     const bool folded = P.nfd > 0 || P.folds != 1;             // summed batch axes
     const bool skinny_fit = !folded && P.N > 0 && P.N <= kSkinnyMaxN && P.M > 0 &&
@@ -1756,7 +1796,7 @@ PT_API void gemm_sm100_last_launch(int *grid, int *block, int *cluster)
 PT_API int gemm_sm100_set_path(int path)
 {
     const int prev = t_path;
-    if (path >= 0 && path <= 5)
+    if (path >= 0 && path <= 6)
         t_path = path;
     return prev;
 }

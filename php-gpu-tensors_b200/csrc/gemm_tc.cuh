@@ -77,6 +77,10 @@ struct TcParams {
     int a_fslot[3];
     int b_fslot[3];
     int k_per_fold;
+    // 2-CTA 256 x 512 kernel: work items below wide_items are whole 256 x 512
+    // tiles; each later item is one 256-column half of tile wide_items +
+    // (item - wide_items) / 2 (tiles counts the items)
+    long long wide_items;
 };
 
 __device__ __forceinline__ float apply_activation(float v, int act)

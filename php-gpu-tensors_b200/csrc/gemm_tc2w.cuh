@@ -26,6 +26,13 @@
 // Ring: 4 stages of 48 KB per CTA (A 16 KB, B 2 x 16 KB), the same 192 KB in
 // flight as the 256 x 256 kernel's 6 stages of 32 KB.
 //
+// Work items (p.wide_items): the first wide_items items are whole 256 x 512
+// tiles; every later item is one 256-column half of a tile, run through
+// accumulator half 0 and B slot 0 only (half the loads, MMAs and stores).
+// The launcher makes the whole tiles fill every full round of co-resident
+// clusters and runs the remainder as halves, so a last round that would be
+// half empty takes half as long.
+//
 // Protocol (no TMA multicast anywhere), as in tc2_gemm_kernel:
 //   full[s]   lives in CTA 0; CTA 0 posts expect_tx for both CTAs' bytes and
 //             both CTAs' TMA loads complete on it.
@@ -86,6 +93,19 @@ struct Tc2wConfig {
     static_assert(IN_KIND == IN_F16 || IN_KIND == IN_BF16, "16-bit operands");
     static_assert(OUT == OUT_F16 || OUT == OUT_BF16, "16-bit output");
 };
+
+// Work item -> 256 x 512 tile index; hsel = -1 for the whole tile, else the
+// one 256-column half the item covers.
+__device__ __forceinline__ long long wide_item(const TcParams &p, long long i, int &hsel)
+{
+    if (i < p.wide_items) {
+        hsel = -1;
+        return i;
+    }
+    const long long j = i - p.wide_items;
+    hsel = static_cast<int>(j & 1);
+    return p.wide_items + (j >> 1);
+}
 
 template <int IN_KIND, int OUT>
 __global__ void __launch_bounds__(Tc2wConfig<IN_KIND, OUT>::kThreads, 1)
@@ -152,8 +172,11 @@ __global__ void __launch_bounds__(Tc2wConfig<IN_KIND, OUT>::kThreads, 1)
             uint32_t issued_mask = 0, parity_mask = 0;
             bool ok = true;
             for (long long t = cluster; ok && t < p.tiles; t += nclusters) {
-                const int nb = static_cast<int>(t % p.n_blocks);
-                const long long r = t / p.n_blocks;
+                int hsel;
+                const long long tile = wide_item(p, t, hsel);
+                const int nhalf = hsel < 0 ? 2 : 1;
+                const int nb = static_cast<int>(tile % p.n_blocks);
+                const long long r = tile / p.n_blocks;
                 const int mb = static_cast<int>(r % p.m_blocks);
                 const long long batch = r / p.m_blocks;
                 int c[3], ca[3], cb[3];
@@ -171,7 +194,8 @@ __global__ void __launch_bounds__(Tc2wConfig<IN_KIND, OUT>::kThreads, 1)
                     uint8_t *sa = smem + stage * Cfg::kStageBytes;
                     uint8_t *sb = sa + Cfg::kATile;
                     if (rank == 0)
-                        mbar_arrive_expect_tx(&full[stage], 2 * Cfg::kStageBytes);
+                        mbar_arrive_expect_tx(&full[stage],
+                                              2 * (Cfg::kATile + nhalf * Cfg::kBHalf));
                     const uint32_t full0 = map_to_cta(smem_addr(&full[stage]), 0);
                     const int k0 = kb * Cfg::BK;
                     if (!p.a_mn_major) {
@@ -184,8 +208,12 @@ __global__ void __launch_bounds__(Tc2wConfig<IN_KIND, OUT>::kThreads, 1)
                     }
 #pragma unroll
                     for (int h = 0; h < 2; h++) {
+                        if (h >= nhalf)
+                            break;
+                        // slot h holds the B columns of tile half h, or of
+                        // the item's one half
                         uint8_t *sbh = sb + h * Cfg::kBHalf;
-                        const int nh = n0 + h * Cfg::kHalfN;
+                        const int nh = n0 + (hsel < 0 ? h : hsel) * Cfg::kHalfN;
                         if (!p.b_mn_major) {
                             tma_load_5d_pair(sbh, &tma_b, full0, k0, nh, cb[0], cb[1], cb[2]);
                         } else {
@@ -225,6 +253,9 @@ __global__ void __launch_bounds__(Tc2wConfig<IN_KIND, OUT>::kThreads, 1)
             bool ok = true;
             const uint32_t smem_base = smem_addr(smem);
             for (long long t = cluster; ok && t < p.tiles; t += nclusters, iter++) {
+                int hsel;
+                (void)wide_item(p, t, hsel);
+                const int nhalf = hsel < 0 ? 2 : 1;
                 const uint32_t acc_phase = static_cast<uint32_t>(iter & 1);
                 if (!mbar_wait(&tempty[0], acc_phase ^ 1, abort)) {
                     record_failure(abort, p.status, DEV_TIMEOUT_MMA);
@@ -254,6 +285,8 @@ __global__ void __launch_bounds__(Tc2wConfig<IN_KIND, OUT>::kThreads, 1)
                             }
                             tc_fence_after();
                         }
+                        if (h >= nhalf)
+                            break;
 #pragma unroll
                         for (int k = 0; k < Cfg::kKSteps; k++) {
                             const uint32_t a_off = p.a_mn_major ? k * Cfg::kMmaK * 128 : k * 32;
@@ -307,14 +340,18 @@ __global__ void __launch_bounds__(Tc2wConfig<IN_KIND, OUT>::kThreads, 1)
                 break;
             }
             tc_fence_after();
-            const int nb = static_cast<int>(t % p.n_blocks);
-            const long long r = t / p.n_blocks;
+            int hsel;
+            const long long tile = wide_item(p, t, hsel);
+            const int nhalf = hsel < 0 ? 2 : 1;
+            const int nb = static_cast<int>(tile % p.n_blocks);
+            const long long r = tile / p.n_blocks;
             const int mb = static_cast<int>(r % p.m_blocks);
             const long long batch = r / p.m_blocks;
             int c[3];
             decode_batch(batch, p, c);
             const int row0 = mb * Cfg::BM + static_cast<int>(rank) * Cfg::kRowsCta + quad * 32;
-            const int n0 = nb * Cfg::BN + part * Cfg::kPartCols;
+            // first column of this warp's part of accumulator half 0
+            const int n0 = nb * Cfg::BN + (hsel < 0 ? 0 : hsel * Cfg::kHalfN) + part * Cfg::kPartCols;
             const uint32_t t_acc = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) +
                                    static_cast<uint32_t>(part * Cfg::kPartCols);
 
@@ -326,6 +363,7 @@ __global__ void __launch_bounds__(Tc2wConfig<IN_KIND, OUT>::kThreads, 1)
             constexpr int kLoads = Cfg::kPartCols / 16;
 #pragma unroll
             for (int h = 0; h < 2; h++) {
+              if (h < nhalf) {
                 const uint32_t t_half = t_acc + h * Cfg::kHalfN;
                 tmem_ld_32x32b_x16(t_half, buf0);
                 tmem_ld_wait_regs(buf0);
@@ -342,6 +380,7 @@ __global__ void __launch_bounds__(Tc2wConfig<IN_KIND, OUT>::kThreads, 1)
                     if (j + 1 < kLoads)
                         tmem_ld_wait_regs(nxt);
                 }
+              }
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0)
@@ -351,6 +390,8 @@ __global__ void __launch_bounds__(Tc2wConfig<IN_KIND, OUT>::kThreads, 1)
 #pragma unroll
             for (int ch = 0; ch < Cfg::kWarpCols / Cfg::kEpiCols; ch++) {
                 // chunks 0, 1: half 0; chunks 2, 3: half 1
+                if ((ch >> 1) >= nhalf)
+                    break;
                 const int col0 = n0 + (ch >> 1) * Cfg::kHalfN + (ch & 1) * Cfg::kEpiCols;
                 uint32_t *q32 = pk + ch * (Cfg::kEpiCols / 2);
                 if (fused) {

@@ -491,10 +491,11 @@ def set_kernel_path(path):
     2 CUDA cores only, 3 2-CTA tensor-core kernel whenever allowed (16-bit,
     tf32, strict float32, float32 x bf16), 4 few-column split-K kernel
     whenever N <= 32 and K >= 128, 5 the 2-CTA 256 x 512 kernel for 16-bit
-    products with a 16-bit result (other products as 3)."""
+    products with a 16-bit result (other products as 3), 6 the same kernel
+    running every tile as two 256-column halves."""
     return library().gemm_sm100_set_path(
         {"auto": 0, "tensor-core": 1, "simt": 2, "tensor-core-pair": 3, "skinny": 4,
-         "tensor-core-wide": 5}[path])
+         "tensor-core-wide": 5, "tensor-core-wide-halves": 6}[path])
 
 
 def last_launch():

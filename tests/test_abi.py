@@ -118,10 +118,10 @@ def test_path_selector():
     lib = P.library()
     prev = lib.gemm_sm100_set_path(2)
     assert lib.gemm_sm100_set_path(1) == 2
-    assert lib.gemm_sm100_set_path(5) == 1
-    assert lib.gemm_sm100_set_path(6) == 5       # invalid values leave it unchanged
-    assert lib.gemm_sm100_set_path(-1) == 5
-    assert lib.gemm_sm100_set_path(prev) == 5
+    assert lib.gemm_sm100_set_path(6) == 1
+    assert lib.gemm_sm100_set_path(7) == 6       # invalid values leave it unchanged
+    assert lib.gemm_sm100_set_path(-1) == 6
+    assert lib.gemm_sm100_set_path(prev) == 6
 
 
 def _pt(shape, dtype, strides=None):

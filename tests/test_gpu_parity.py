@@ -89,7 +89,8 @@ def check_fp32(gpu, a, b, what, first=None, count=None):
 
 
 # ------------------------------------------------------------------ golden
-@pytest.mark.parametrize("path", ["auto", "tensor-core", "tensor-core-pair", "tensor-core-wide", "simt"])
+@pytest.mark.parametrize("path", ["auto", "tensor-core", "tensor-core-pair", "tensor-core-wide",
+                                  "tensor-core-wide-halves", "simt"])
 def test_golden_vectors(golden, path):
     P.set_kernel_path(path)
     for case in golden["cases"]:
@@ -190,7 +191,8 @@ SKINNY_CASES = [c for c in CASES if c[2][-1] <= 32 and c[2][-2] >= 128]
 
 
 @pytest.mark.parametrize("dtype", ["bfloat16", "float16", "float32"])
-@pytest.mark.parametrize("path", ["auto", "tensor-core", "tensor-core-pair", "tensor-core-wide", "skinny"])
+@pytest.mark.parametrize("path", ["auto", "tensor-core", "tensor-core-pair", "tensor-core-wide",
+                                  "tensor-core-wide-halves", "skinny"])
 @pytest.mark.parametrize("case", CASES, ids=[c[0] for c in CASES])
 def test_seeded_parity(case, path, dtype):
     name, ashape, bshape, at, bt, pad = case
@@ -202,9 +204,9 @@ def test_seeded_parity(case, path, dtype):
     b = padded(bv, bshape, pad, dtype, bt)
     c = to_device(a, dtype).matmul(to_device(b, dtype))
     what = (name, path, P.cuda_get_backend_info()["kernel"])
-    if path in ("tensor-core-pair", "tensor-core-wide") and what[2].startswith("tc"):
+    if path.startswith(("tensor-core-pair", "tensor-core-wide")) and what[2].startswith("tc"):
         assert what[2].startswith("tc2-"), what
-    if path == "tensor-core-wide" and what[2].startswith("tc") and dtype != "float32":
+    if path.startswith("tensor-core-wide") and what[2].startswith("tc") and dtype != "float32":
         assert what[2].endswith("256x512"), what
     if path == "skinny" and case in SKINNY_CASES:
         assert what[2].startswith("skinny-"), what
@@ -556,7 +558,8 @@ def test_fused_epilogue_matches_unfused_plan(dtype, act, N):
     a = to_device(O.dense(O.to_storage(av, dtype), [M, K]), dtype)
     x = to_device(O.dense(O.to_storage(xv, dtype), [N, K]), dtype)
     bdev = to_device(O.dense(O.to_storage(bias, dtype), [N]), dtype)
-    for path in ("tensor-core", "tensor-core-pair", "tensor-core-wide", "simt") + (
+    for path in ("tensor-core", "tensor-core-pair", "tensor-core-wide", "tensor-core-wide-halves",
+                 "simt") + (
             ("skinny",) if N <= 32 else ()):
         P.set_kernel_path(path)
         fused = a.matmul_epilogue(x.transpose(), bdev, act).to_torch().float()
@@ -579,7 +582,8 @@ def test_config2_full_size_integer_exact():
     b = torch.randint(-3, 4, (64, 1024, 1024), generator=g).to(torch.bfloat16)
     exact = torch.bmm(a.double().cuda(), b.double().cuda()).float().to(torch.bfloat16)
     for path, prefix in (("auto", "tc"), ("tensor-core", "tc-bf16"), ("tensor-core-pair", "tc2-bf16"),
-                         ("tensor-core-wide", "tc2-bf16-256x512")):
+                         ("tensor-core-wide", "tc2-bf16-256x512"),
+                         ("tensor-core-wide-halves", "tc2-bf16-256x512")):
         P.set_kernel_path(path)
         c = P.CudaArray.from_torch(a.cuda()).matmul(P.CudaArray.from_torch(b.cuda()))
         assert P.cuda_get_backend_info()["kernel"].startswith(prefix), path
@@ -621,9 +625,11 @@ def test_config3_fp16_transposed_bias_tanh(path):
     fused = a.matmul_epilogue(x.transpose(), bdev, "tanh")
     kernel = P.cuda_get_backend_info()["kernel"]
     assert kernel.startswith(("tc-f16", "tc2-f16")), kernel
-    if path != "auto":
-        assert kernel == {"tensor-core-pair": "tc2-f16-256x256",
-                          "tensor-core-wide": "tc2-f16-256x512"}[path], kernel
+    # automatic choice: 256 x 4096 / 512 = 256 wide tiles are 3.5 rounds of
+    # the 74 co-resident clusters, so the wide kernel runs 3 rounds of whole
+    # tiles and the rest as 256-column halves
+    assert kernel == {"auto": "tc2-f16-256x512", "tensor-core-pair": "tc2-f16-256x256",
+                      "tensor-core-wide": "tc2-f16-256x512"}[path], kernel
     plain = a.matmul(x.transpose())
     assert P.cuda_get_backend_info()["kernel"] == kernel
     unfused = torch.tanh(plain.to_torch().float() + bdev.to_torch().float()).half().float()
@@ -1016,7 +1022,7 @@ def _random_case(rng):
 
 @pytest.mark.parametrize("dtype", ["bfloat16", "float16", "float32"])
 @pytest.mark.parametrize("path", ["auto", "tensor-core", "tensor-core-pair", "tensor-core-wide",
-                                  "skinny"])
+                                  "tensor-core-wide-halves", "skinny"])
 def test_randomized_products(dtype, path):
     """40 seeded random products per dtype and kernel path against the oracle."""
     rng = np.random.default_rng(sum(map(ord, dtype + path)))
