@@ -163,165 +163,167 @@ __global__ void __launch_bounds__(Tc2wConfig<IN_KIND, OUT>::kThreads, 1)
     grid_launch_dependents();
 
     if (warp < 4) {
-      warpgroup_reg_dealloc<Cfg::kRegsCtl>();
-      if (warp == 0) {
-        // ------------------------------------------------------------ producer (both CTAs)
-        if (lane == 0) {
-            int stage = 0;
-            uint32_t phase = 0;
-            uint32_t issued_mask = 0, parity_mask = 0;
-            bool ok = true;
-            for (long long t = cluster; ok && t < p.tiles; t += nclusters) {
-                int hsel;
-                const long long tile = wide_item(p, t, hsel);
-                const int nhalf = hsel < 0 ? 2 : 1;
-                const int nb = static_cast<int>(tile % p.n_blocks);
-                const long long r = tile / p.n_blocks;
-                const int mb = static_cast<int>(r % p.m_blocks);
-                const long long batch = r / p.m_blocks;
-                int c[3], ca[3], cb[3];
-                decode_batch(batch, p, c);
-                operand_coords(c, p.a_slot, p.nbd, ca);
-                operand_coords(c, p.b_slot, p.nbd, cb);
-                const int m0 = mb * Cfg::BM + static_cast<int>(rank) * Cfg::kRowsCta;
-                const int n0 = nb * Cfg::BN + static_cast<int>(rank) * Cfg::kColsCta;
-                for (int kb = 0; kb < p.k_blocks; kb++) {
-                    if (!mbar_wait(&empty[stage], phase ^ 1, abort)) {
-                        record_failure(abort, p.status, DEV_TIMEOUT_PRODUCER);
-                        ok = false;
-                        break;
-                    }
-                    uint8_t *sa = smem + stage * Cfg::kStageBytes;
-                    uint8_t *sb = sa + Cfg::kATile;
-                    if (rank == 0)
-                        mbar_arrive_expect_tx(&full[stage],
-                                              2 * (Cfg::kATile + nhalf * Cfg::kBHalf));
-                    const uint32_t full0 = map_to_cta(smem_addr(&full[stage]), 0);
-                    const int k0 = kb * Cfg::BK;
-                    if (!p.a_mn_major) {
-                        tma_load_5d_pair(sa, &tma_a, full0, k0, m0, ca[0], ca[1], ca[2]);
-                    } else {
-#pragma unroll
-                        for (int j = 0; j < Cfg::kRowsCta / Cfg::kChunk; j++)
-                            tma_load_5d_pair(sa + j * Cfg::kChunkBytes, &tma_a, full0,
-                                             m0 + j * Cfg::kChunk, k0, ca[0], ca[1], ca[2]);
-                    }
-#pragma unroll
-                    for (int h = 0; h < 2; h++) {
-                        if (h >= nhalf)
+        warpgroup_reg_dealloc<Cfg::kRegsCtl>();
+        if (warp == 0) {
+            // ------------------------------------------------------------ producer (both CTAs)
+            if (lane == 0) {
+                int stage = 0;
+                uint32_t phase = 0;
+                uint32_t issued_mask = 0, parity_mask = 0;
+                bool ok = true;
+                for (long long t = cluster; ok && t < p.tiles; t += nclusters) {
+                    int hsel;
+                    const long long tile = wide_item(p, t, hsel);
+                    const int nhalf = hsel < 0 ? 2 : 1;
+                    const int nb = static_cast<int>(tile % p.n_blocks);
+                    const long long r = tile / p.n_blocks;
+                    const int mb = static_cast<int>(r % p.m_blocks);
+                    const long long batch = r / p.m_blocks;
+                    int c[3], ca[3], cb[3];
+                    decode_batch(batch, p, c);
+                    operand_coords(c, p.a_slot, p.nbd, ca);
+                    operand_coords(c, p.b_slot, p.nbd, cb);
+                    const int m0 = mb * Cfg::BM + static_cast<int>(rank) * Cfg::kRowsCta;
+                    const int n0 = nb * Cfg::BN + static_cast<int>(rank) * Cfg::kColsCta;
+                    for (int kb = 0; kb < p.k_blocks; kb++) {
+                        if (!mbar_wait(&empty[stage], phase ^ 1, abort)) {
+                            record_failure(abort, p.status, DEV_TIMEOUT_PRODUCER);
+                            ok = false;
                             break;
-                        // slot h holds the B columns of tile half h, or of
-                        // the item's one half
-                        uint8_t *sbh = sb + h * Cfg::kBHalf;
-                        const int nh = n0 + (hsel < 0 ? h : hsel) * Cfg::kHalfN;
-                        if (!p.b_mn_major) {
-                            tma_load_5d_pair(sbh, &tma_b, full0, k0, nh, cb[0], cb[1], cb[2]);
+                        }
+                        uint8_t *sa = smem + stage * Cfg::kStageBytes;
+                        uint8_t *sb = sa + Cfg::kATile;
+                        if (rank == 0)
+                            mbar_arrive_expect_tx(&full[stage],
+                                                  2 * (Cfg::kATile + nhalf * Cfg::kBHalf));
+                        const uint32_t full0 = map_to_cta(smem_addr(&full[stage]), 0);
+                        const int k0 = kb * Cfg::BK;
+                        if (!p.a_mn_major) {
+                            tma_load_5d_pair(sa, &tma_a, full0, k0, m0, ca[0], ca[1], ca[2]);
                         } else {
 #pragma unroll
-                            for (int j = 0; j < Cfg::kColsCta / Cfg::kChunk; j++)
-                                tma_load_5d_pair(sbh + j * Cfg::kChunkBytes, &tma_b, full0,
-                                                 nh + j * Cfg::kChunk, k0, cb[0], cb[1], cb[2]);
+                            for (int j = 0; j < Cfg::kRowsCta / Cfg::kChunk; j++)
+                                tma_load_5d_pair(sa + j * Cfg::kChunkBytes, &tma_a, full0,
+                                                 m0 + j * Cfg::kChunk, k0, ca[0], ca[1], ca[2]);
+                        }
+#pragma unroll
+                        for (int h = 0; h < 2; h++) {
+                            if (h >= nhalf)
+                                break;
+                            // slot h holds the B columns of tile half h, or of
+                            // the item's one half
+                            uint8_t *sbh = sb + h * Cfg::kBHalf;
+                            const int nh = n0 + (hsel < 0 ? h : hsel) * Cfg::kHalfN;
+                            if (!p.b_mn_major) {
+                                tma_load_5d_pair(sbh, &tma_b, full0, k0, nh, cb[0], cb[1], cb[2]);
+                            } else {
+#pragma unroll
+                                for (int j = 0; j < Cfg::kColsCta / Cfg::kChunk; j++)
+                                    tma_load_5d_pair(sbh + j * Cfg::kChunkBytes, &tma_b, full0,
+                                                     nh + j * Cfg::kChunk, k0, cb[0], cb[1], cb[2]);
+                            }
+                        }
+                        issued_mask |= 1u << stage;
+                        parity_mask = (parity_mask & ~(1u << stage)) | (phase << stage);
+                        if (++stage == S) {
+                            stage = 0;
+                            phase ^= 1;
                         }
                     }
-                    issued_mask |= 1u << stage;
-                    parity_mask = (parity_mask & ~(1u << stage)) | (phase << stage);
-                    if (++stage == S) {
-                        stage = 0;
-                        phase ^= 1;
+                }
+                if (rank == 0) {
+                    // CTA 0's full barriers count both CTAs' bytes of every stage
+                    // it posted: let them land (bounded, ignores the abort flag)
+                    for (int s = 0; s < S; s++) {
+                        if (issued_mask & (1u << s)) {
+                            int no_abort = 0;
+                            mbar_wait(&full[s], (parity_mask >> s) & 1u, &no_abort);
+                        }
                     }
                 }
+                if (*abort)
+                    settle_after_abort();
             }
-            if (rank == 0) {
-                // CTA 0's full barriers count both CTAs' bytes of every stage
-                // it posted: let them land (bounded, ignores the abort flag)
-                for (int s = 0; s < S; s++) {
-                    if (issued_mask & (1u << s)) {
-                        int no_abort = 0;
-                        mbar_wait(&full[s], (parity_mask >> s) & 1u, &no_abort);
-                    }
-                }
-            }
-            if (*abort)
-                settle_after_abort();
-        }
-      } else if (warp == 1) {
-        // ------------------------------------------------------------ MMA issuer (CTA 0)
-        if (lane == 0 && rank == 0) {
-            int stage = 0;
-            uint32_t phase = 0;
-            long long iter = 0;
-            bool ok = true;
-            const uint32_t smem_base = smem_addr(smem);
-            for (long long t = cluster; ok && t < p.tiles; t += nclusters, iter++) {
-                int hsel;
-                (void)wide_item(p, t, hsel);
-                const int nhalf = hsel < 0 ? 2 : 1;
-                const uint32_t acc_phase = static_cast<uint32_t>(iter & 1);
-                if (!mbar_wait(&tempty[0], acc_phase ^ 1, abort)) {
-                    record_failure(abort, p.status, DEV_TIMEOUT_MMA);
-                    break;
-                }
-                tc_fence_after();
-                for (int kb = 0; kb < p.k_blocks; kb++) {
-                    if (!mbar_wait(&full[stage], phase, abort)) {
+        } else if (warp == 1) {
+            // ------------------------------------------------------------ MMA issuer (CTA 0)
+            if (lane == 0 && rank == 0) {
+                int stage = 0;
+                uint32_t phase = 0;
+                long long iter = 0;
+                bool ok = true;
+                const uint32_t smem_base = smem_addr(smem);
+                for (long long t = cluster; ok && t < p.tiles; t += nclusters, iter++) {
+                    int hsel;
+                    (void)wide_item(p, t, hsel);
+                    const int nhalf = hsel < 0 ? 2 : 1;
+                    const uint32_t acc_phase = static_cast<uint32_t>(iter & 1);
+                    if (!mbar_wait(&tempty[0], acc_phase ^ 1, abort)) {
                         record_failure(abort, p.status, DEV_TIMEOUT_MMA);
-                        ok = false;
                         break;
                     }
                     tc_fence_after();
-                    const uint32_t sa = smem_base + stage * Cfg::kStageBytes;
-                    const uint32_t sb = sa + Cfg::kATile;
-                    const uint32_t b_lbo = p.b_mn_major ? Cfg::kChunkBytes : 16;
-                    // accumulator half 0, then half 1 (on the tile's first
-                    // k-block, once the epilogue has read that half: its
-                    // drain overlaps half 0's MMAs)
-#pragma unroll
-                    for (int h = 0; h < 2; h++) {
-                        if (h == 1 && kb == 0) {
-                            if (!mbar_wait(&tempty[1], acc_phase ^ 1, abort)) {
-                                record_failure(abort, p.status, DEV_TIMEOUT_MMA);
-                                ok = false;
-                                break;
-                            }
-                            tc_fence_after();
-                        }
-                        if (h >= nhalf)
+                    for (int kb = 0; kb < p.k_blocks; kb++) {
+                        if (!mbar_wait(&full[stage], phase, abort)) {
+                            record_failure(abort, p.status, DEV_TIMEOUT_MMA);
+                            ok = false;
                             break;
+                        }
+                        tc_fence_after();
+                        const uint32_t sa = smem_base + stage * Cfg::kStageBytes;
+                        const uint32_t sb = sa + Cfg::kATile;
+                        const uint32_t b_lbo = p.b_mn_major ? Cfg::kChunkBytes : 16;
+                        // accumulator half 0, then half 1 (on the tile's first
+                        // k-block, once the epilogue has read that half: its
+                        // drain overlaps half 0's MMAs)
 #pragma unroll
-                        for (int k = 0; k < Cfg::kKSteps; k++) {
-                            const uint32_t a_off = p.a_mn_major ? k * Cfg::kMmaK * 128 : k * 32;
-                            const uint32_t b_off = p.b_mn_major ? k * Cfg::kMmaK * 128 : k * 32;
-                            // 16-bit operands: the MN-major SBO and layout equal
-                            // the K-major ones, only the LBO depends on the layout
-                            const uint64_t ad = smem_desc(
-                                sa + a_off, p.a_mn_major ? Cfg::kChunkBytes : 16, 1024, kLayoutSw128);
-                            const uint64_t bd =
-                                smem_desc(sb + h * Cfg::kBHalf + b_off, b_lbo, 1024, kLayoutSw128);
-                            umma_f16_pair(tmem_base + h * Cfg::kHalfN, ad, bd, p.idesc,
-                                          (kb | k) != 0);
+                        for (int h = 0; h < 2; h++) {
+                            if (h == 1 && kb == 0) {
+                                if (!mbar_wait(&tempty[1], acc_phase ^ 1, abort)) {
+                                    record_failure(abort, p.status, DEV_TIMEOUT_MMA);
+                                    ok = false;
+                                    break;
+                                }
+                                tc_fence_after();
+                            }
+                            if (h >= nhalf)
+                                break;
+#pragma unroll
+                            for (int k = 0; k < Cfg::kKSteps; k++) {
+                                const uint32_t a_off = p.a_mn_major ? k * Cfg::kMmaK * 128 : k * 32;
+                                const uint32_t b_off = p.b_mn_major ? k * Cfg::kMmaK * 128 : k * 32;
+                                // 16-bit operands: the MN-major SBO and layout equal
+                                // the K-major ones, only the LBO depends on the layout
+                                const uint64_t ad = smem_desc(
+                                    sa + a_off, p.a_mn_major ? Cfg::kChunkBytes : 16, 1024,
+                                    kLayoutSw128);
+                                const uint64_t bd =
+                                    smem_desc(sb + h * Cfg::kBHalf + b_off, b_lbo, 1024,
+                                              kLayoutSw128);
+                                umma_f16_pair(tmem_base + h * Cfg::kHalfN, ad, bd, p.idesc,
+                                              (kb | k) != 0);
+                            }
+                        }
+                        if (!ok)
+                            break;
+                        const uint32_t e0 = smem_addr(&empty[stage]);
+                        umma_commit_pair(e0);
+                        umma_commit_pair(map_to_cta(e0, 1));
+                        if (++stage == S) {
+                            stage = 0;
+                            phase ^= 1;
                         }
                     }
                     if (!ok)
                         break;
-                    const uint32_t e0 = smem_addr(&empty[stage]);
-                    umma_commit_pair(e0);
-                    umma_commit_pair(map_to_cta(e0, 1));
-                    if (++stage == S) {
-                        stage = 0;
-                        phase ^= 1;
-                    }
+                    const uint32_t f0 = smem_addr(tfull);
+                    umma_commit_pair(f0);
+                    umma_commit_pair(map_to_cta(f0, 1));
                 }
-                if (!ok)
-                    break;
-                const uint32_t f0 = smem_addr(tfull);
-                umma_commit_pair(f0);
-                umma_commit_pair(map_to_cta(f0, 1));
+                umma_commit_pair(smem_addr(drain));
+                int no_abort = 0;
+                mbar_wait(drain, 0, &no_abort);
             }
-            umma_commit_pair(smem_addr(drain));
-            int no_abort = 0;
-            mbar_wait(drain, 0, &no_abort);
         }
-      }
     } else {
         warpgroup_reg_alloc<Cfg::kRegsEpi>();
         // ------------------------------------------------------------ epilogue (both CTAs)
@@ -351,7 +353,8 @@ __global__ void __launch_bounds__(Tc2wConfig<IN_KIND, OUT>::kThreads, 1)
             decode_batch(batch, p, c);
             const int row0 = mb * Cfg::BM + static_cast<int>(rank) * Cfg::kRowsCta + quad * 32;
             // first column of this warp's part of accumulator half 0
-            const int n0 = nb * Cfg::BN + (hsel < 0 ? 0 : hsel * Cfg::kHalfN) + part * Cfg::kPartCols;
+            const int n0 =
+                nb * Cfg::BN + (hsel < 0 ? 0 : hsel * Cfg::kHalfN) + part * Cfg::kPartCols;
             const uint32_t t_acc = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) +
                                    static_cast<uint32_t>(part * Cfg::kPartCols);
 
@@ -363,24 +366,25 @@ __global__ void __launch_bounds__(Tc2wConfig<IN_KIND, OUT>::kThreads, 1)
             constexpr int kLoads = Cfg::kPartCols / 16;
 #pragma unroll
             for (int h = 0; h < 2; h++) {
-              if (h < nhalf) {
-                const uint32_t t_half = t_acc + h * Cfg::kHalfN;
-                tmem_ld_32x32b_x16(t_half, buf0);
-                tmem_ld_wait_regs(buf0);
+                if (h < nhalf) {
+                    const uint32_t t_half = t_acc + h * Cfg::kHalfN;
+                    tmem_ld_32x32b_x16(t_half, buf0);
+                    tmem_ld_wait_regs(buf0);
 #pragma unroll
-                for (int j = 0; j < kLoads; j++) {
-                    uint32_t(&cur)[16] = (j & 1) ? buf1 : buf0;
-                    uint32_t(&nxt)[16] = (j & 1) ? buf0 : buf1;
-                    if (j + 1 < kLoads)
-                        tmem_ld_32x32b_x16(t_half + (j + 1) * 16, nxt);
+                    for (int j = 0; j < kLoads; j++) {
+                        uint32_t(&cur)[16] = (j & 1) ? buf1 : buf0;
+                        uint32_t(&nxt)[16] = (j & 1) ? buf0 : buf1;
+                        if (j + 1 < kLoads)
+                            tmem_ld_32x32b_x16(t_half + (j + 1) * 16, nxt);
 #pragma unroll
-                    for (int i = 0; i < 8; i++)
-                        pk[(h * kLoads + j) * 8 + i] = pack2(__uint_as_float(cur[2 * i]),
-                                                             __uint_as_float(cur[2 * i + 1]), OUT);
-                    if (j + 1 < kLoads)
-                        tmem_ld_wait_regs(nxt);
+                        for (int i = 0; i < 8; i++)
+                            pk[(h * kLoads + j) * 8 + i] =
+                                pack2(__uint_as_float(cur[2 * i]), __uint_as_float(cur[2 * i + 1]),
+                                      OUT);
+                        if (j + 1 < kLoads)
+                            tmem_ld_wait_regs(nxt);
+                    }
                 }
-              }
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0)
