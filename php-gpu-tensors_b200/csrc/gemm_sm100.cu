@@ -21,6 +21,7 @@
 #include "gemm_tc.cuh"
 #include "gemm_tc2.cuh"
 #include "gemm_tc2w.cuh"
+#include "gemm_tc2t.cuh"
 
 #include <cudaTypedefs.h>
 
@@ -61,6 +62,12 @@ constexpr int kPairChunkKB = PTG_PAIR_CHUNK_KB;
 // choice matches the faster kernel on every measured shape (8192^3 pair,
 // 4096^3 single-CTA, the config-4 layer products pair, their dW single-CTA).
 constexpr double kPairTileCost = 1.79;
+// The same for the 2-CTA strict float32 kernel with A in tensor memory
+// (K-major A; B200: 4096 x 1024 x 1024 152 against 145 TFLOP/s for the
+// shared-memory pair kernel, 4096^3 164-173 against 154-160): 1.79 scaled by
+// those ratios.  With it 4096^3 (4 rounds of 74 pair tiles against 7 waves of
+// 148 single-CTA tiles, 148-161 TFLOP/s) moves to the pair kernel.
+constexpr double kPairTmemTileCost = 1.70;
 // mixed kinds on the 2-CTA kernel: k-blocks (64 K each) per accumulator chunk,
 // 256 K as in the single-CTA mixed kernel
 constexpr int kMixPairChunkKB = 4;
@@ -130,7 +137,7 @@ struct DeviceState {
     int cc_major, cc_minor;
     int *status;                   // this device's copy of g_device_status
     unsigned long long attr_mask;  // kernels whose shared-memory limit has been raised
-    int pair_clusters[8];          // co-resident 2-CTA clusters per pair kernel (0 = unknown)
+    int pair_clusters[12];          // co-resident 2-CTA clusters per pair kernel (0 = unknown)
 };
 std::mutex g_mutex;
 DeviceState g_devices[kMaxDevices];
@@ -560,8 +567,9 @@ enum KernelId : int {
     KID_F64_DMMA_HANDOFF_HALF,                 // half tiles of the hand-off kernel
     KID_BF16_WIDE,                             // bf16 on the 2-CTA 256 x 512 kernel
     KID_F16_WIDE,                              // f16 on the 2-CTA 256 x 512 kernel
+    KID_F32X3_TPAIR,                           // strict float32, 2-CTA, A split into TMEM
 };
-static_assert(KID_F16_WIDE < 64, "kernel ids index a 64-bit attribute mask");
+static_assert(KID_F32X3_TPAIR < 64, "kernel ids index a 64-bit attribute mask");
 
 const char *kernel_name(int kid)
 {
@@ -579,6 +587,7 @@ const char *kernel_name(int kid)
     case KID_F16_WIDE: return "tc2-f16-256x512";
     case KID_F64_DMMA: return "dmma-f64-128x128";
     case KID_F32X3_PAIR: return "tc2-3xtf32-256x256";
+    case KID_F32X3_TPAIR: return "tc2-3xtf32-tmem-256x256";
     case KID_TF32_PAIR: return "tc2-tf32-256x256";
     case KID_MIX_A_PAIR: return "tc2-f32xbf16-bf16x3-256x256";
     case KID_MIX_B_PAIR: return "tc2-bf16xf32-bf16x3-256x256";
@@ -731,16 +740,13 @@ cudaError_t launch_tc2_kernel(DeviceState *ds, int kid, int slot, const CUtensor
                                                   mc, p, stream);
 }
 
-// The 256 x 512 kernel moves registers between its warpgroups
-// (setmaxnreg); an increase beyond the CTA's launch allocation would never
-// complete, so the compiled register count is checked before every launch.
-template <int IN, int OUT>
-cudaError_t launch_wide_kernel(DeviceState *ds, int kid, int slot, const CUtensorMap &ma,
-                               const CUtensorMap &mb, const CUtensorMap &mc, TcParams &p,
-                               cudaStream_t stream)
+// Kernels that move registers between their warpgroups (setmaxnreg): an
+// increase beyond the CTA's launch allocation (threads x registers per
+// thread as compiled) would never complete, so the compiled register count
+// is checked before every launch (read once per kernel).
+template <typename Cfg, typename Kernel>
+bool regs_cover_realloc(Kernel kernel)
 {
-    using Cfg = Tc2wConfig<IN, OUT>;
-    auto kernel = tc2w_gemm_kernel<IN, OUT>;
     static const int regs = [&] {
         cudaFuncAttributes fa;
         if (cudaFuncGetAttributes(&fa, kernel) != cudaSuccess) {
@@ -749,7 +755,18 @@ cudaError_t launch_wide_kernel(DeviceState *ds, int kid, int slot, const CUtenso
         }
         return fa.numRegs;
     }();
-    if (regs * Cfg::kThreads < Cfg::kRegsTotal)
+    return regs * Cfg::kThreads >= Cfg::kRegsTotal;
+}
+
+// The 256 x 512 kernel: register check, then its work items.
+template <int IN, int OUT>
+cudaError_t launch_wide_kernel(DeviceState *ds, int kid, int slot, const CUtensorMap &ma,
+                               const CUtensorMap &mb, const CUtensorMap &mc, TcParams &p,
+                               cudaStream_t stream)
+{
+    using Cfg = Tc2wConfig<IN, OUT>;
+    auto kernel = tc2w_gemm_kernel<IN, OUT>;
+    if (!regs_cover_realloc<Cfg>(kernel))
         return cudaErrorInvalidConfiguration;
     if (!ensure_smem_attr(ds, kid, kernel, Cfg::kSmemBytes))
         return cudaErrorInvalidConfiguration;
@@ -896,8 +913,8 @@ int try_tc(const Problem &P, DeviceState *ds, cudaStream_t stream, int *kid_out)
                     }
                 }
             }
-            const double t2 =
-                std::ceil(static_cast<double>(tiles_pair) / (ds->sms / 2)) * kPairTileCost;
+            const double t2 = std::ceil(static_cast<double>(tiles_pair) / (ds->sms / 2)) *
+                              (strict && !a_mn && !folded ? kPairTmemTileCost : kPairTileCost);
             pair = pair_g == 1 && t2 < t1;
         }
     }
@@ -926,7 +943,10 @@ int try_tc(const Problem &P, DeviceState *ds, cudaStream_t stream, int *kid_out)
               : mix_side == 1 ? (pair ? KID_MIX_B_PAIR : KID_MIX_B)
                               : (op_dt == DT_BF16 ? KID_BF16_F32 : KID_F16_F32);
     else if (fp32)
-        kid = strict ? (pair ? KID_F32X3_PAIR : KID_F32X3_128)
+        // the pair kernel with A in tensor memory takes K-major A without
+        // split-K or summed batch axes
+        kid = strict ? (pair ? (!a_mn && pair_g == 1 && !folded ? KID_F32X3_TPAIR : KID_F32X3_PAIR)
+                             : KID_F32X3_128)
                      : (pair ? KID_TF32_PAIR : (bn == 256 ? KID_TF32_256 : KID_TF32_128));
     else if (P.dt == DT_BF16)
         kid = wide ? KID_BF16_WIDE : pair ? KID_BF16_PAIR : (bn == 256 ? KID_BF16_256 : KID_BF16_128);
@@ -1034,6 +1054,12 @@ int try_tc(const Problem &P, DeviceState *ds, cudaStream_t stream, int *kid_out)
         break;
     case KID_F16_WIDE:
         err = launch_wide_kernel<IN_F16, OUT_F16>(ds, kid, 7, tma_a, tma_b, tma_c, p, stream);
+        break;
+    case KID_F32X3_TPAIR:
+        err = regs_cover_realloc<Tc2tConfig>(tc2t_gemm_kernel)
+                  ? launch_pair_kernel<Tc2tConfig>(ds, kid, 8, tc2t_gemm_kernel, tma_a, tma_b,
+                                                   tma_c, p, stream)
+                  : cudaErrorInvalidConfiguration;
         break;
     case KID_F32X3_PAIR:
         err = launch_pair_kernel<Tc2x3Config<IN_F32X3, kPairChunkKB>>(

@@ -414,9 +414,12 @@ def test_pair_3xtf32(case):
     b = padded(O.seeded(bshape, seed + 1, "normal"), bshape, 0, "float32", bt)
     ad, bd = to_device(a, "float32"), to_device(b, "float32")
     c = ad.matmul(bd)
-    assert P.cuda_get_backend_info()["kernel"] == "tc2-3xtf32-256x256", name
     # few tiles split K over clusters of 2 or 4 pairs, 64 tiles and more do not
-    assert P.last_launch()[2] in (2, 4, 8)
+    cluster = P.last_launch()[2]
+    assert cluster in (2, 4, 8)
+    # K-major A without split-K: A's hi and lo in tensor memory
+    expect = "tc2-3xtf32-tmem-256x256" if not at and cluster == 2 else "tc2-3xtf32-256x256"
+    assert P.cuda_get_backend_info()["kernel"] == expect, name
     first = c.to_numpy()
     check_fp32(first, a, b, name)
     for _ in range(2):
@@ -573,6 +576,38 @@ def test_fused_epilogue_matches_unfused_plan(dtype, act, N):
 
 
 # ------------------------------------------------------------------ configs
+@pytest.mark.parametrize("shape", [(640, 520, 300), (3, 1024, 1024, 1000), (2048, 2048, 4096)],
+                         ids=["ragged", "batched", "long_k"])
+def test_strict_pair_tmem_a_matches_smem_a(shape):
+    """Strict float32 on the 2-CTA kernels: with K-major A the split puts A's
+    hi and lo in tensor memory (tc2-3xtf32-tmem), with an M-major A view it
+    stays in shared memory (tc2-3xtf32); both issue the same MMAs and add the
+    K chunks in the same order, so the products are bit-identical, and within
+    the float32 bound of the oracle.  (The shapes have enough tiles, or too
+    short a K, for the forced pair path not to split K, which only the
+    shared-memory kernel does.)"""
+    *batch, M, N, K = shape
+    P.set_kernel_path("tensor-core-pair")
+    av = O.seeded(list(batch) + [M, K], 51, "normal")
+    bv = O.seeded(list(batch) + [K, N], 52, "normal")
+    a_k = padded(av, list(batch) + [M, K], 0, "float32")
+    # the same matrix stored M-contiguous: storage [.., K, M] holds A^T
+    av_t = np.swapaxes(np.asarray(av).reshape(list(batch) + [M, K]), -1, -2).reshape(-1)
+    a_m = padded(av_t, list(batch) + [M, K], 0, "float32", transpose=True)
+    b = padded(bv, list(batch) + [K, N], 0, "float32")
+    bd = to_device(b, "float32")
+    c_k = to_device(a_k, "float32").matmul(bd)
+    k_kernel = P.cuda_get_backend_info()["kernel"]
+    c_m = to_device(a_m, "float32").matmul(bd)
+    m_kernel = P.cuda_get_backend_info()["kernel"]
+    assert k_kernel == "tc2-3xtf32-tmem-256x256", k_kernel
+    assert m_kernel == "tc2-3xtf32-256x256", m_kernel
+    assert np.array_equal(c_k.to_numpy().view(np.uint32), c_m.to_numpy().view(np.uint32))
+    if len(batch) == 0 and K <= 1024:
+        check_fp32(c_k.to_numpy(), a_k, b, ("tmem-a", shape))
+    assert P.device_status() == 0
+
+
 def test_config2_full_size_integer_exact():
     """bf16 [64,1024,1024] x [64,1024,1024]: with small-integer inputs every
     partial sum is exact in float32, so the product must be bit-identical to
