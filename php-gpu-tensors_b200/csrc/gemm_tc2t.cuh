@@ -55,7 +55,10 @@ struct Tc2tConfig {
     static constexpr int kATile = kRowsCta * BK * 4;    // 16 KB
     static constexpr int kBTile = kColsCta * BK * 4;    // 16 KB
     static constexpr int kLoadBytes = kATile + kBTile;
-    static constexpr int kStages = 4;                   // raw A + B tiles
+#ifndef PTG_TC2T_STAGES
+#define PTG_TC2T_STAGES 4
+#endif
+    static constexpr int kStages = PTG_TC2T_STAGES;     // raw A + B tiles
 #ifndef PTG_TC2T_LO_STAGES
 #define PTG_TC2T_LO_STAGES 3
 #endif
