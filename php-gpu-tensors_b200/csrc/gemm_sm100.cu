@@ -137,7 +137,7 @@ struct DeviceState {
     int cc_major, cc_minor;
     int *status;                   // this device's copy of g_device_status
     unsigned long long attr_mask;  // kernels whose shared-memory limit has been raised
-    int pair_clusters[12];          // co-resident 2-CTA clusters per pair kernel (0 = unknown)
+    int pair_clusters[12];         // co-resident 2-CTA clusters per pair kernel (0 = unknown)
 };
 std::mutex g_mutex;
 DeviceState g_devices[kMaxDevices];
@@ -928,16 +928,19 @@ int try_tc(const Problem &P, DeviceState *ds, cudaStream_t stream, int *kid_out)
     const long long tiles_wide = P.batches * ((P.M + 255) / 256) * ((P.N + 511) / 512);
     const long long clusters_est = ds->sms / 2;
     const double rounds_pair = std::ceil(static_cast<double>(tiles_pair) / clusters_est);
-    const double cost_wide = std::ceil(static_cast<double>(tiles_wide) / clusters_est) * kWideTileCost;
+    const double cost_wide =
+        std::ceil(static_cast<double>(tiles_wide) / clusters_est) * kWideTileCost;
     const long long full_rounds = tiles_wide / clusters_est;
     const double cost_mixed =
         full_rounds * kWideTileCost +
-        std::ceil(2.0 * static_cast<double>(tiles_wide - full_rounds * clusters_est) / clusters_est);
+        std::ceil(2.0 * static_cast<double>(tiles_wide - full_rounds * clusters_est) /
+                  clusters_est);
     const bool wide = pair && !fp32 && !wide_out && !folded && P.forced_bn == 0 &&
                       (t_path == 5 || t_path == 6 ||
                        (t_path == 0 && P.K >= kWideMinK &&
                         std::min(cost_wide, cost_mixed) < rounds_pair));
-    const long long wide_items = t_path == 6 ? 0 : (t_path == 0 && cost_mixed < cost_wide) ? -1 : tiles_wide;
+    const long long wide_items =
+        t_path == 6 ? 0 : (t_path == 0 && cost_mixed < cost_wide) ? -1 : tiles_wide;
     if (wide_out)
         kid = mix_side == 0   ? (pair ? KID_MIX_A_PAIR : KID_MIX_A)
               : mix_side == 1 ? (pair ? KID_MIX_B_PAIR : KID_MIX_B)
@@ -949,9 +952,13 @@ int try_tc(const Problem &P, DeviceState *ds, cudaStream_t stream, int *kid_out)
                              : KID_F32X3_128)
                      : (pair ? KID_TF32_PAIR : (bn == 256 ? KID_TF32_256 : KID_TF32_128));
     else if (P.dt == DT_BF16)
-        kid = wide ? KID_BF16_WIDE : pair ? KID_BF16_PAIR : (bn == 256 ? KID_BF16_256 : KID_BF16_128);
+        kid = wide   ? KID_BF16_WIDE
+              : pair ? KID_BF16_PAIR
+                     : (bn == 256 ? KID_BF16_256 : KID_BF16_128);
     else
-        kid = wide ? KID_F16_WIDE : pair ? KID_F16_PAIR : (bn == 256 ? KID_F16_256 : KID_F16_128);
+        kid = wide   ? KID_F16_WIDE
+              : pair ? KID_F16_PAIR
+                     : (bn == 256 ? KID_F16_256 : KID_F16_128);
 
     const int bk = 128 / es;            // K elements per stage
     const int chunk = 128 / es;         // MN elements per 128-byte row

@@ -252,8 +252,8 @@ __global__ void __launch_bounds__(Tc2tConfig::kThreads, 1)
                         tc_fence_after();
                         const uint32_t sb = smem_base + stage * Cfg::kLoadBytes + Cfg::kATile;
                         const uint32_t lb = smem_base + Cfg::kLoOffset + slot * Cfg::kBTile;
-                        const uint32_t a_hi =
-                            tmem_base + static_cast<uint32_t>(Cfg::kASlot0 + slot * Cfg::kASlotCols);
+                        const uint32_t a_hi = tmem_base + static_cast<uint32_t>(
+                                                              Cfg::kASlot0 + slot * Cfg::kASlotCols);
                         const uint32_t a_lo = a_hi + Cfg::BK;
 #pragma unroll
                         for (int k = 0; k < Cfg::kKSteps; k++) {
@@ -316,13 +316,15 @@ __global__ void __launch_bounds__(Tc2tConfig::kThreads, 1)
                         const float4 x = raw[bt + j * kThr];
                         l[j] = make_float4(tf32_lo(x.x), tf32_lo(x.y), tf32_lo(x.z), tf32_lo(x.w));
                     }
-                    if (!__all_sync(0xffffffffu, mbar_wait(&lo_free[slot], lo_phase ^ 1, abort))) {
+                    if (!__all_sync(0xffffffffu,
+                                    mbar_wait(&lo_free[slot], lo_phase ^ 1, abort))) {
                         if (lane == 0)
                             record_failure(abort, p.status, DEV_TIMEOUT_SPLIT);
                         ok = false;
                         break;
                     }
-                    float4 *lo = reinterpret_cast<float4 *>(smem + Cfg::kLoOffset + slot * Cfg::kBTile);
+                    float4 *lo =
+                        reinterpret_cast<float4 *>(smem + Cfg::kLoOffset + slot * Cfg::kBTile);
 #pragma unroll
                     for (int j = 0; j < kPer; j++)
                         lo[bt + j * kThr] = l[j];
@@ -383,7 +385,8 @@ __global__ void __launch_bounds__(Tc2tConfig::kThreads, 1)
                         }
                     };
                     split_half(0);
-                    if (!__all_sync(0xffffffffu, mbar_wait(&lo_free[slot], lo_phase ^ 1, abort))) {
+                    if (!__all_sync(0xffffffffu,
+                                    mbar_wait(&lo_free[slot], lo_phase ^ 1, abort))) {
                         if (lane == 0)
                             record_failure(abort, p.status, DEV_TIMEOUT_SPLIT);
                         ok = false;
