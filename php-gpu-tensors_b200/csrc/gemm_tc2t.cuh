@@ -252,8 +252,8 @@ __global__ void __launch_bounds__(Tc2tConfig::kThreads, 1)
                         tc_fence_after();
                         const uint32_t sb = smem_base + stage * Cfg::kLoadBytes + Cfg::kATile;
                         const uint32_t lb = smem_base + Cfg::kLoOffset + slot * Cfg::kBTile;
-                        const uint32_t a_hi = tmem_base + static_cast<uint32_t>(
-                                                              Cfg::kASlot0 + slot * Cfg::kASlotCols);
+                        const int a_col = Cfg::kASlot0 + slot * Cfg::kASlotCols;
+                        const uint32_t a_hi = tmem_base + static_cast<uint32_t>(a_col);
                         const uint32_t a_lo = a_hi + Cfg::BK;
 #pragma unroll
                         for (int k = 0; k < Cfg::kKSteps; k++) {
