@@ -935,10 +935,18 @@ int try_tc(const Problem &P, DeviceState *ds, cudaStream_t stream, int *kid_out)
         full_rounds * kWideTileCost +
         std::ceil(2.0 * static_cast<double>(tiles_wide - full_rounds * clusters_est) /
                   clusters_est);
+    // (the kernels that move registers between warpgroups are taken only
+    // when their compiled register count covers the move; otherwise the
+    // earlier kernel of the same kind runs)
     const bool wide = pair && !fp32 && !wide_out && !folded && P.forced_bn == 0 &&
                       (t_path == 5 || t_path == 6 ||
                        (t_path == 0 && P.K >= kWideMinK &&
-                        std::min(cost_wide, cost_mixed) < rounds_pair));
+                        std::min(cost_wide, cost_mixed) < rounds_pair)) &&
+                      (P.dt == DT_BF16
+                           ? regs_cover_realloc<Tc2wConfig<IN_BF16, OUT_BF16>>(
+                                 tc2w_gemm_kernel<IN_BF16, OUT_BF16>)
+                           : regs_cover_realloc<Tc2wConfig<IN_F16, OUT_F16>>(
+                                 tc2w_gemm_kernel<IN_F16, OUT_F16>));
     const long long wide_items =
         t_path == 6 ? 0 : (t_path == 0 && cost_mixed < cost_wide) ? -1 : tiles_wide;
     if (wide_out)
@@ -948,7 +956,10 @@ int try_tc(const Problem &P, DeviceState *ds, cudaStream_t stream, int *kid_out)
     else if (fp32)
         // the pair kernel with A in tensor memory takes K-major A without
         // split-K or summed batch axes
-        kid = strict ? (pair ? (!a_mn && pair_g == 1 && !folded ? KID_F32X3_TPAIR : KID_F32X3_PAIR)
+        kid = strict ? (pair ? (!a_mn && pair_g == 1 && !folded &&
+                                        regs_cover_realloc<Tc2tConfig>(tc2t_gemm_kernel)
+                                    ? KID_F32X3_TPAIR
+                                    : KID_F32X3_PAIR)
                              : KID_F32X3_128)
                      : (pair ? KID_TF32_PAIR : (bn == 256 ? KID_TF32_256 : KID_TF32_128));
     else if (P.dt == DT_BF16)
