@@ -17,7 +17,21 @@ def test_kernel_divisor_by_pass_count():
     assert bench.kernel_divisor("tc-tf32-128x256") == 2.0
     assert bench.kernel_divisor("tc2-f32xbf16-bf16x3-256x256") == 3.0
     assert bench.kernel_divisor("tc2-bf16-256x256") == 1.0
+    assert bench.kernel_divisor("tc2-3xtf32-tmem-256x256") == 6.0
+    assert bench.kernel_divisor("tc2-bf16-256x512") == 1.0
+    assert bench.kernel_divisor("tc2-f16-256x512") == 1.0
     assert bench.kernel_divisor("skinny-f32") is None
+
+
+def test_traffic_entries_for_the_bench_kernels():
+    """Every kernel the default bench runs on its workloads has a committed
+    DRAM traffic figure (the roofline's traffic field)."""
+    for workload, kernel in (("config5a", "tc2-bf16-256x512"), ("config2", "tc2-bf16-256x512"),
+                             ("config3", "tc2-f16-256x512"),
+                             ("config4", "tc2-3xtf32-tmem-256x256"),
+                             ("config5b", "dmma-f64-128x128")):
+        t = bench.traffic_for(workload, kernel)
+        assert isinstance(t, int) and t > 0, (workload, kernel)
     assert bench.kernel_divisor("simt-f32") is None
 
 
