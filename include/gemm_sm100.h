@@ -223,7 +223,8 @@ int cuda_matmul_epilogue_nd_launcher(
     const void *bias, int activation, cudaStream_t stream);
 
 /* Name of the kernel the last successful launch on this thread used, e.g.
- * "tc2-bf16-256x256", "tc2-3xtf32-256x256", "tc-3xtf32-128x128",
+ * "tc2-bf16-256x512", "tc2-bf16-256x256", "tc2-3xtf32-tmem-256x256",
+ * "tc2-3xtf32-256x256", "tc-3xtf32-128x128",
  * "skinny-f32", "simt-f32"; "none" before any. */
 const char *gemm_sm100_last_kernel(void);
 
