@@ -118,7 +118,17 @@ typedef struct {
 void cuda_blas_shutdown(void);
 
 /* matmul_kernels.h:32.  Returns 1 and sets the thread's float32 mode, or 0
- * for an unknown mode. */
+ * for an unknown mode.
+ * Non-finite inputs in the strict mode: the tensor-core kernels form float32
+ * products from split operands (hi*hi + hi*lo + lo*hi; for float32 x
+ * bfloat16 gradients three bf16 parts of the float32 operand), so an infinite
+ * element meets the zero low part of the other operand's element in a cross
+ * term (inf * 0 = NaN): a dot product that involves an infinite input can
+ * come out NaN where the IEEE float32 loop of HostArray::matmul gives +-Inf.
+ * Finite inputs and NaN inputs behave as in that loop (within its error
+ * bound; NaN propagates).  gemm_sm100_set_path(2) runs the CUDA-core kernel,
+ * whose fma chains equal the loop bit for bit, for callers that need IEEE
+ * infinities. */
 int cuda_blas_set_precision(int precision);
 
 /* matmul_kernels.h:33.  "fp32-strict" or "tf32". */
